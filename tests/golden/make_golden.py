@@ -1,0 +1,214 @@
+"""Generate the golden fixtures by running the REFERENCE engine's own fp32 code on seeded inputs.
+
+Run in a container where the reference checkout is readable (default path from $Q3_REFERENCE, else /root/reference):
+    python tests/golden/make_golden.py
+It imports engine.talker / engine.arrivals / engine.code_predictor from the reference (read-only; flash-attn and triton
+only need to import) and calls:
+  * Talker._attn_ref            (engine/talker.py:82-88)      paged decode on page-gathered caches  -> decode_c1.npz
+  * FastAdmit._attn_ref         (engine/arrivals.py:125-131)  prefix / causal prefill              -> prefill.npz
+  * CodePredictor._post         (engine/code_predictor.py:44-50) with identity o-proj and a zero MLP, so it returns
+                                 the attention expression of code_predictor.py:46-47 exactly     -> cp_attn.npz
+  * Talker._frame               (engine/talker.py:107-112) + CodePredictor.run, fp32, greedy (top_k=1), on random-init
+                                 weights and a synthetic K/V history                              -> frame_*.npz
+Inputs are regenerated from seeds by q3attn.synth / q3attn.weights (torch CPU generators); each fixture stores a
+checksum of its inputs so a generator mismatch is detected before outputs are compared. The GPU box never runs this.
+"""
+import hashlib
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(REPO, "qwen3-tts-engine_b200"))
+from q3attn import synth, weights  # noqa: E402
+
+REF = os.environ.get("Q3_REFERENCE", "/root/reference")
+
+
+def digest(*ts) -> str:
+    h = hashlib.sha256()
+    for t in ts:
+        h.update(t.detach().contiguous().float().numpy().tobytes())
+    return h.hexdigest()[:32]
+
+
+def ref_modules():
+    sys.path.insert(0, REF)
+    from engine import talker, arrivals, code_predictor   # noqa: F401
+    return talker, arrivals, code_predictor
+
+
+# --------------------------------------------------------------------------- decode (C1)
+def c1_inputs(seed=1):
+    lay = synth.c1_layout(seed)
+    d = synth.decode_case(seed, lay, scale=1.0, dtype=torch.float32)
+    return lay, d
+
+
+def gen_decode(talker):
+    out = {}
+    for seed in (1, 11, 12):
+        lay, d = c1_inputs(seed)
+        B, page = lay.B, lay.page
+        # the reference reads a contiguous per-seat slice: lay each seat's gathered tokens out back to back
+        rowsK, rowsV, slot, base = [], [], [], 0
+        for b in range(B):
+            n = int(lay.ctx[b])
+            pg = lay.block_table[b, : (n + page - 1) // page].long()
+            rowsK.append(d["k_pool"][pg].reshape(-1, 8, 128)[:n])
+            rowsV.append(d["v_pool"][pg].reshape(-1, 8, 128)[:n])
+            slot.append(base + n - 1)
+            base += n
+        ns = types.SimpleNamespace(kc=[torch.cat(rowsK)], vc=[torch.cat(rowsV)], nkv=8, hd=128, nh=16, scale=128 ** -0.5)
+        o = talker.Talker._attn_ref(ns, d["q"], 0, torch.tensor(slot), lay.ctx)
+        out[f"s{seed}_out"] = o.numpy()
+        out[f"s{seed}_ctx"] = lay.ctx.numpy()
+        out[f"s{seed}_bt"] = lay.block_table.numpy()
+        out[f"s{seed}_digest"] = np.array(digest(d["q"], d["k_pool"], d["v_pool"]))
+    np.savez_compressed(os.path.join(HERE, "decode_c1.npz"), **out)
+
+
+# --------------------------------------------------------------------------- prefill
+PREFILL_CASES = {          # name: (seed, S, R, k)
+    "arrivals": (21, 2, 42, 35),     # FastAdmit shape: R new positions over k cached prefix positions
+    "causal": (22, 1, 77, 0),        # eager prompt prefill (no prefix)
+    "ragged": (23, 3, 17, 5),
+}
+
+
+def prefill_inputs(seed, S, R, k):
+    g = synth.cpu_gen(seed)
+    q = synth.randn((S, R, 16, 128), g, 0.5)
+    K = synth.randn((S, k + R, 8, 128), g, 0.5)
+    V = synth.randn((S, k + R, 8, 128), g, 0.5)
+    return q, K, V
+
+
+def gen_prefill(arrivals):
+    out = {}
+    for name, (seed, S, R, k) in PREFILL_CASES.items():
+        q, K, V = prefill_inputs(seed, S, R, k)
+        ns = types.SimpleNamespace(T=types.SimpleNamespace(nkv=8, nh=16, hd=128, scale=128 ** -0.5))
+        o = arrivals.FastAdmit._attn_ref(ns, q, K, V)
+        out[f"{name}_out"] = o.numpy()
+        out[f"{name}_digest"] = np.array(digest(q, K, V))
+    np.savez_compressed(os.path.join(HERE, "prefill.npz"), **out)
+
+
+# --------------------------------------------------------------------------- code predictor attention
+def gen_cp(code_predictor):
+    out = {}
+    B = 8
+    for p in range(16):
+        d = synth.cp_case(40 + p, B, dtype=torch.float32)
+        cp = object.__new__(code_predictor.CodePredictor)
+        cp.nh, cp.nkv, cp.hd, cp.scale, cp.ffn = 16, 8, 128, 128 ** -0.5, 8
+        mask = torch.full((16, 16), float("-inf")).triu(1)
+        x = torch.zeros(B, 2048)
+        o = code_predictor.CodePredictor._post(cp, x, d["q"], d["K"], d["V"], mask[p], torch.eye(2048), torch.ones(2048),
+                                               torch.zeros(16, 2048), torch.zeros(2048, 8))
+        out[f"p{p}_out"] = o.numpy()
+        out[f"p{p}_digest"] = np.array(digest(d["q"], d["K"], d["V"]))
+    np.savez_compressed(os.path.join(HERE, "cp_attn.npz"), **out)
+
+
+# --------------------------------------------------------------------------- full frame (e2e)
+FRAME_CASES = {
+    # name: (size, talker layers (None = all), n_seats, live seats, bucket, seat_len, ctx range, frames, seed)
+    "frame06": ("0.6B", None, 40, 29, 32, 512, (100, 400), 2, 7),
+    "frame17": ("1.7B", 2, 12, 5, 8, 512, (50, 300), 2, 8),
+}
+
+
+def frame_state(size, n_layers, n_seats, n_live, seat_len, ctx_rng, seed):
+    """Seeded synthetic engine state: bf16-rounded weights, K/V history per seat (N(0,1)*0.5), pending inputs,
+    trailing text, generation counters. Returns plain fp32 tensors in the reference's identity layout."""
+    W = weights.cast(weights.cast(weights.random_weights(seed, size, max_pos=seat_len + 64, n_layers=n_layers),
+                                  torch.bfloat16), torch.float32)
+    g = synth.cpu_gen(seed + 500)
+    S1 = n_seats + 1
+    nl = len(W.layers)
+    live = torch.randperm(n_seats, generator=g)[:n_live]
+    ctx = torch.zeros(S1, dtype=torch.int64)
+    ctx[live] = torch.randint(ctx_rng[0], ctx_rng[1] + 1, (n_live,), generator=g)
+    kv = synth.randn((2, nl, S1, seat_len, 8, 128), g, 0.5, torch.bfloat16).float()
+    pos_idx = torch.arange(seat_len)[None, :]
+    kv = kv * (pos_idx < ctx[:, None]).float()[None, None, :, :, None, None]      # positions >= ctx start empty
+    x_in = synth.randn((S1, W.H), g, 0.1, torch.bfloat16).float()
+    max_text = 16
+    trail = synth.randn((S1, max_text + 1, W.H), g, 0.02, torch.bfloat16).float()
+    trail_len = torch.randint(0, max_text + 1, (S1,), generator=g)
+    ngen = torch.randint(0, 6, (S1,), generator=g)
+    return W, dict(live=live, ctx=ctx, kv=kv, x_in=x_in, trail=trail, trail_len=trail_len, ngen=ngen, max_text=max_text)
+
+
+def ref_talker(talker_mod, code_predictor_mod, W, n_seats, seat_len, bucket, st):
+    """A reference Talker built without CUDA (object.__new__ + the attributes of engine/talker.py:24-54), fp32, top_k=1."""
+    T = object.__new__(talker_mod.Talker)
+    T.W = W
+    T.d, T.dt = torch.device("cpu"), torch.float32
+    T.n_seats, T.seat_len, T.page, T.P = n_seats, seat_len, 256, seat_len // 256
+    T.H, T.nh, T.nkv, T.hd, T.ffn = W.H, W.heads, W.kv_heads, W.head_dim, W.ffn
+    T.scale = float(T.hd) ** -0.5
+    T.temperature, T.top_k, T.rep, T.min_new = 0.9, 1, 1.05, 2
+    S1 = n_seats + 1
+    T.kc = [st["kv"][0, l].reshape(S1 * T.P, 256, 8, 128).clone() for l in range(len(W.layers))]
+    T.vc = [st["kv"][1, l].reshape(S1 * T.P, 256, 8, 128).clone() for l in range(len(W.layers))]
+    T.pos = st["ctx"].clone()
+    T.x_in = st["x_in"].clone()
+    T.seen = torch.zeros(S1, W.vocab, dtype=torch.bool)
+    T.ngen = st["ngen"].clone()
+    T.max_text = st["max_text"]
+    T.trail = st["trail"].clone()
+    T.trail_len = st["trail_len"].clone()
+    T.seat_pages = (torch.arange(S1, dtype=torch.int32)[:, None] * T.P + torch.arange(T.P, dtype=torch.int32)[None, :]).contiguous()
+    sup = torch.zeros(W.vocab)
+    sup[W.vocab - 1024:] = float("-inf")
+    sup[W.eos] = 0.0
+    T.suppress = sup
+    T.eos_col = torch.zeros(W.vocab, dtype=torch.bool)
+    T.eos_col[W.eos] = True
+    T.one = torch.ones(1, dtype=torch.int64)
+    T.gen = torch.Generator().manual_seed(0)
+    T.buckets = [bucket]
+    T.max_bs = bucket
+    T.s_seat = torch.full((bucket,), n_seats, dtype=torch.int64)
+    T.o_codes = torch.zeros(bucket, 16, dtype=torch.int64)
+    T.cp = code_predictor_mod.CodePredictor(W, bucket, compile_mode="off", temperature=0.9, top_k=1)
+    T.decode = T._decode
+    return T
+
+
+def gen_frames(talker, code_predictor):
+    for name, (size, nl, n_seats, n_live, bucket, seat_len, rng, frames, seed) in FRAME_CASES.items():
+        W, st = frame_state(size, nl, n_seats, n_live, seat_len, rng, seed)
+        T = ref_talker(talker, code_predictor, W, n_seats, seat_len, bucket, st)
+        live = st["live"]
+        T.s_seat[:n_live] = live
+        codes, hx = [], []
+        with torch.inference_mode():
+            for f in range(frames):
+                T.pos[n_seats] = 0
+                T._frame(bucket)
+                codes.append(T.o_codes[:n_live].clone())
+        # the rows the first frame appended (placement pin): K of layer 0 at each live seat's first new position
+        slot0 = live * seat_len + st["ctx"][live]
+        krow0 = T.kc[0].view(-1, 8, 128)[slot0]
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), codes=torch.stack(codes).numpy(), live=live.numpy(),
+                            x_in=T.x_in[live].numpy(), pos=T.pos.numpy(), ngen=T.ngen.numpy(), krow0=krow0.numpy(),
+                            digest=np.array(digest(st["kv"][:, :, :, :8], st["x_in"], W.layers[0].qkv, W.cp_head[3])))
+        print(f"[golden] {name}: codes {tuple(torch.stack(codes).shape)}", flush=True)
+
+
+if __name__ == "__main__":
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    talker, arrivals, code_predictor = ref_modules()
+    gen_decode(talker)
+    gen_prefill(arrivals)
+    gen_cp(code_predictor)
+    gen_frames(talker, code_predictor)
+    print("[golden] done", flush=True)
