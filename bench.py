@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""Decode-attention throughput of the talker's paged KV cache on 1..8 B200s.
+
+One step = one 28-layer talker decode step of the attention hot path for 576 seats per GPU: per layer, the fused
+K/V page append + paged decode attention (GQA 16/8, d128, bf16), contexts U[200,1200], 16-token pages in a shuffled
+pool sized for 576 x 1216 tokens (engine/talker.py:72-77 with BASELINE's layout). 28 distinct per-layer pools (80 GB)
+exceed the 126 MB L2, so no flush is needed between steps. The step is captured in a CUDA graph and replayed.
+
+  value  seat-steps/s over all GPUs = seats_per_gpu * N / (max over ranks of device time per step), inputs resident
+  e2e    the same metric through the public API with host buffers: every step copies its q/k/v (all layers) from
+         pinned host memory and reads every layer's attention output back, double-buffered on copy streams
+  roofline  algorithmic HBM bytes per launch (one layer) / average launch time, against MEASURED_PEAKS.json hbm_gbs
+  cpu_baseline  the reference's CPU attention path (oracle restatement of Talker._attn_ref with the page gather and the
+         append, fp32, all host threads) on a bounded sample of seats, rank 0 at N=1
+
+--impl reference times that CPU path alone (rank 0; other ranks exit) on the same metric and config.
+Multi-GPU: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N (seats shard with no collective; the
+process group is used only for the start barrier and the max over ranks of the timing).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "qwen3-tts-engine_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "decode-attn seat-steps/s @576 seats; achieved HBM GB/s (% peak) at 1/2/4/8 GPU"
+UNIT = "seat-steps/s"
+SCALE = 128 ** -0.5
+PAGE, CTX_LO, CTX_HI, TOKENS_PER_SEAT = 16, 200, 1200, 1216
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--seats", type=int, default=576)
+    p.add_argument("--layers", type=int, default=28)
+    p.add_argument("--seed", type=int, default=2)
+    p.add_argument("--variant", type=int, default=0, help="decode kernel variant (q3_set_decode_variant)")
+    p.add_argument("--num-splits", type=int, default=0)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--cpu-seats", type=int, default=48)
+    return p.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def hbm_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(path))["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def layout_for_rank(seed, rank, seats):
+    """Rank r's seats: ctx U[200,1200] and a shuffled local page table (rank 0 == the config-2 layout)."""
+    from q3attn import synth
+    return synth.paged_layout(seed + 7919 * rank, B=seats, ctx_lo=CTX_LO, ctx_hi=CTX_HI, page=PAGE,
+                              pages_per_seat=TOKENS_PER_SEAT // PAGE)
+
+
+# ----------------------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, device_index):
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            ident = str(device_index)
+        self.cmd = ["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = []
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                rows.append(dict(sm=float(f[0]), smax=float(f[1]), power=float(f[2]), hw=f[4], hwt=f[5], swt=f[6], pcap=f[7]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        load = [r for r in rows if r["power"] > 250.0] or rows
+        reasons = set()
+        for r in load:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
+                              ("pcap", "sw_power_cap")):
+                if r[key].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows), "samples_under_load": len(load),
+                "power_w_max": max(r["power"] for r in rows)}
+
+
+# ----------------------------------------------------------------------------------------------------- CPU path
+def cpu_sample(lay, seed, n_seats):
+    """K/V of a sample of seats of the workload (one layer), fp32 on the host, plus the sampled seats' q/k/v."""
+    from q3attn import synth
+    pick = torch.linspace(0, lay.B - 1, n_seats).long()
+    pps = lay.block_table.shape[1]
+    g = synth.cpu_gen(seed + 31)
+    kp = synth.randn((n_seats * pps, PAGE, 8, 128), g, 0.5)
+    vp = synth.randn((n_seats * pps, PAGE, 8, 128), g, 0.5)
+    bt = torch.randperm(n_seats * pps, generator=g).view(n_seats, pps).to(torch.int32)
+    q = synth.randn((n_seats, 16, 128), g, 0.5)
+    kn = synth.randn((n_seats, 8, 128), g, 0.5)
+    vn = synth.randn((n_seats, 8, 128), g, 0.5)
+    return dict(ctx=lay.ctx[pick].clone(), bt=bt, kp=kp, vp=vp, q=q, kn=kn, vn=vn, n=n_seats)
+
+
+def cpu_layer(s):
+    """One layer of the reference CPU path for the sampled seats: append (talker.py:72-73) + Talker._attn_ref
+    (talker.py:82-88) over page-gathered K/V, fp32."""
+    from oracle import attention as OA
+    return OA.decode_step(s["q"], s["kn"], s["vn"], s["kp"], s["vp"], s["ctx"], s["bt"], SCALE)
+
+
+def cpu_rate(s, layers, seconds):
+    cpu_layer(s)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        cpu_layer(s)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return s["n"] * n / el / layers, n, el
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------------------------------------------- reference arm
+def run_reference(a):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    torch.set_num_threads(host_cores())
+    lay = layout_for_rank(a.seed, 0, a.seats)
+    s = cpu_sample(lay, a.seed, a.cpu_seats)
+    for _ in range(max(a.warmup, 1)):
+        cpu_layer(s)
+    times = []
+    for _ in range(a.steps):
+        t0 = time.perf_counter()
+        cpu_layer(s)
+        times.append(time.perf_counter() - t0)
+    per_layer = sum(times) / len(times)
+    value = s["n"] / per_layer / a.layers
+    sample = (f"each step: 1 of {a.layers} layers for {s['n']} of {a.seats} seats (append + page gather + "
+              f"Talker._attn_ref restated, fp32 torch CPU); seat-steps/s = seats / layer time / {a.layers}")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": per_layer * a.layers * 1e3 * a.seats / s["n"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE config 2 shapes)",
+            "config": config_dict(a, world),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(a, world):
+    return {"workload": "C2: 0.6B talker decode-attention step (28 layers x fused K/V append + paged decode), "
+                        f"{a.seats} seats/GPU, ctx U[{CTX_LO},{CTX_HI}], page {PAGE}, shuffled page table",
+            "seats_per_gpu": a.seats, "layers": a.layers, "page_size": PAGE, "heads": "16q/8kv", "head_dim": 128,
+            "parallelism": f"seat-sharded x{world} (no collective)", "l2": "inputs larger than L2 (28 per-layer pools)",
+            "decode_variant": a.variant}
+
+
+# ----------------------------------------------------------------------------------------------------- our arm
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+    import q3attn
+    from q3attn import synth
+
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+        pg = dist
+    q3attn.set_decode_variant(a.variant)
+
+    L, B = a.layers, a.seats
+    lay = layout_for_rank(a.seed, rank, B)
+    seq = lay.ctx.to(dev)
+    bt = lay.block_table.to(dev)
+    gen = torch.Generator(device=dev).manual_seed(a.seed * 1000 + rank)
+    shp = (lay.num_pages, PAGE, 8, 128)
+    kp = [torch.randn(shp, generator=gen, device=dev, dtype=torch.bfloat16).mul_(0.5) for _ in range(L)]
+    vp = [torch.randn(shp, generator=gen, device=dev, dtype=torch.bfloat16).mul_(0.5) for _ in range(L)]
+
+    def inputs():
+        return (torch.randn((L, B, 16, 128), generator=gen, device=dev, dtype=torch.bfloat16).mul_(0.5),
+                torch.randn((L, B, 8, 128), generator=gen, device=dev, dtype=torch.bfloat16).mul_(0.5),
+                torch.randn((L, B, 8, 128), generator=gen, device=dev, dtype=torch.bfloat16).mul_(0.5))
+
+    def step(qkv):
+        q, k, v = qkv
+        return [q3attn.paged_decode_append(q[l], k[l], v[l], kp[l], vp[l], seq, bt, SCALE, a.num_splits) for l in range(L)]
+
+    sets = [inputs(), inputs()] if not a.no_e2e else [inputs()]
+    cap = torch.cuda.Stream(device=dev)
+    graphs, outs = [], []
+    with torch.cuda.stream(cap):
+        for s in sets:
+            step(s)
+        torch.cuda.synchronize()
+        for s in sets:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                o = step(s)
+            graphs.append(g)
+            outs.append(o)
+    torch.cuda.synchronize()
+    if q3attn._lib.read_status():
+        raise RuntimeError("device status raised during warm-up")
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if pg is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------- device-resident timing
+    for _ in range(a.warmup):
+        graphs[0].replay()
+    clocks = ClockSampler(local)
+    barrier()
+    clocks.start()
+    barrier()
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(a.steps):
+        graphs[0].replay()
+    e1.record(st)
+    e1.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms_total = max_over_ranks(e0.elapsed_time(e1))
+    ms_step = ms_total / a.steps
+    value = B * world / (ms_step / 1e3)
+    if q3attn._lib.read_status():
+        raise RuntimeError("device status raised during the timed region")
+
+    # ---------------- roofline of the decode kernel (one launch == one layer)
+    bytes_launch = synth.decode_bytes(lay.ctx + 1, append=True)
+    launch_s = ms_step / 1e3 / L
+    achieved = bytes_launch / launch_s / 1e9
+    peak, peak_kind = hbm_peak()
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "decode_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            t = json.load(open(tpath))
+            traffic = t.get("dram_bytes_per_launch_scaled_to_bench") or t.get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": traffic, "peak_source": peak_kind, "bytes_per_launch": bytes_launch, "launch_us": launch_s * 1e6,
+            "kernel": "q3::paged_decode_kernel (fused append)"}
+
+    # ---------------- end to end through the public API with host buffers
+    e2e = None
+    if not a.no_e2e:
+        hq = [sets[0][i].cpu().pin_memory() for i in range(3)]
+        hout = torch.empty((L, B, 16, 128), dtype=torch.bfloat16).pin_memory()
+        h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        ev_in = [torch.cuda.Event(), torch.cuda.Event()]
+        ev_done = [torch.cuda.Event(), torch.cuda.Event()]
+        ev_out = [torch.cuda.Event(), torch.cuda.Event()]
+
+        def h2d(j):
+            with torch.cuda.stream(h2d_s):
+                for i in range(3):
+                    sets[j][i].copy_(hq[i], non_blocking=True)
+                ev_in[j].record(h2d_s)
+
+        def run_e2e(n):
+            h2d_s.wait_stream(st)                 # nothing of an earlier run may still read the input sets
+            d2h_s.wait_stream(st)
+            for j in range(2):
+                ev_done[j].record(st)
+                ev_out[j].record(st)
+            h2d(0)
+            for i in range(n):
+                j = i % 2
+                st.wait_event(ev_in[j])
+                st.wait_event(ev_out[j])          # D2H of the step that last used this output set has finished
+                graphs[j].replay()
+                ev_done[j].record(st)
+                if i + 1 < n:
+                    h2d_s.wait_event(ev_done[1 - j])   # the previous step that read set 1-j has finished
+                    h2d(1 - j)
+                with torch.cuda.stream(d2h_s):
+                    d2h_s.wait_event(ev_done[j])
+                    for l in range(L):
+                        hout[l].copy_(outs[j][l], non_blocking=True)
+                    ev_out[j].record(d2h_s)
+            st.wait_stream(d2h_s)
+            st.wait_stream(h2d_s)
+
+        run_e2e(max(a.warmup, 2))
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(st)
+        run_e2e(a.steps)
+        f1.record(st)
+        f1.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1)) / a.steps
+        elem = 2
+        e2e = {"value": B * world / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": int(sum(t.numel() for t in hq) * elem),
+               "d2h_bytes_per_step": int(hout.numel() * elem),
+               "how": "pinned host q/k/v of all layers copied in and every layer's output copied out each step, "
+                      "double-buffered on two copy streams around the captured step"}
+        # the copied-back outputs must equal the device-resident ones
+        torch.cuda.synchronize()
+        if not torch.equal(hout.view(torch.int16), torch.stack(outs[(a.steps - 1) % 2]).cpu().view(torch.int16)):
+            raise RuntimeError("e2e outputs differ from the device outputs")
+
+    # ---------------- CPU baseline (rank 0, N = 1)
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        torch.set_num_threads(host_cores())
+        s = cpu_sample(lay, a.seed, a.cpu_seats)
+        rate, n, el = cpu_rate(s, L, a.cpu_seconds)
+        cpu = {"value": rate, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{n} layer passes over {s['n']} of {B} seats in {el:.1f} s (append + page gather + "
+                         f"Talker._attn_ref restated, fp32 torch CPU), scaled by 1/{L} layers"}
+
+    for g in graphs:
+        del g
+    graphs.clear()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+                "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded, BASELINE config 2 shapes; K/V N(0,1)*0.5)",
+                "config": config_dict(a, world), "gpu_launches": a.steps * L, "roofline": roof,
+                "e2e": e2e, "cpu_baseline": cpu, "clocks": clk,
+                "hbm_gbs_per_gpu": achieved, "hbm_frac_of_peak": achieved / peak}
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

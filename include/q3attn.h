@@ -1,0 +1,114 @@
+/* q3attn — B200 (sm_100a) attention hot path of a Qwen3-TTS streaming engine, as a C ABI.
+ *
+ * Every entry point takes raw device pointers, element strides and sizes, launches on the given CUDA stream
+ * (a cudaStream_t passed as void*, NULL = the legacy default stream) and returns Q3_OK or an error code. Nothing here
+ * allocates, synchronises or reads device memory on the host, so every call can be recorded inside a CUDA graph
+ * (make the first call of each entry point on a device outside capture: it sets kernel attributes).
+ *
+ * Tensor conventions (the engine's model family: 16 query heads, 8 KV heads, head_dim 128, bf16 storage):
+ *   q rows          [B, 16, 128]        innermost 128 contiguous, heads contiguous; batch stride given
+ *   K/V page pool   [num_pages, page_size, 8, 128] fully contiguous (one token row = 2048 bytes)
+ *   block table     int32 [B, stride]   physical page of each seat's j-th page
+ *   code-predictor  K/V [B, 8, S, 128]  (S >= n_live) with explicit batch/head/slot strides
+ * Only num_heads=16, num_kv_heads=8, head_dim=128 are compiled; other shapes return Q3_ERR_UNSUPPORTED.
+ *
+ * Each function names the reference interface (saicherry93479/Qwen3-TTS-Engine, path:line) it replaces.
+ */
+#ifndef Q3ATTN_H_
+#define Q3ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q3_OK 0
+#define Q3_ERR_INVALID 1      /* null pointer, negative size, inconsistent strides */
+#define Q3_ERR_UNSUPPORTED 2  /* head counts / head_dim / slot count outside the compiled family */
+#define Q3_ERR_ALIGNMENT 3    /* a pointer or stride breaks the 16-byte (pools, rows) or 8-byte (q/out) rule */
+#define Q3_ERR_WORKSPACE 4    /* workspace missing or smaller than q3_paged_decode_workspace_bytes() */
+#define Q3_ERR_CUDA 5         /* a CUDA runtime call failed; see q3_last_cuda_error() */
+
+/* Status bits a kernel may set on the device (read with q3_read_status). */
+#define Q3_STATUS_WAIT_TIMEOUT 1u  /* a pipeline wait gave up (kernel returned early; outputs invalid) */
+#define Q3_STATUS_BAD_PAGE 2u      /* a block-table entry or slot outside the pool (access skipped / clamped) */
+#define Q3_STATUS_BAD_LENGTH 4u    /* a sequence length beyond the seat's block-table capacity (clamped) */
+
+int q3_version(void);
+const char* q3_error_string(int code);
+/* Text of the last CUDA error seen by this thread's q3 calls ("" if none). */
+const char* q3_last_cuda_error(void);
+/* Streaming multiprocessors of the current device (148 on B200). */
+int q3_device_sm_count(void);
+/* Read (and optionally clear) the device status word of the current device. Synchronous; not for the hot loop. */
+int q3_read_status(uint32_t* status_out, int clear);
+
+/* ---------------------------------------------------------------- paged decode attention
+ * Replaces flash_attn_with_kvcache(q, k_cache, v_cache, k=, v=, cache_seqlens=, block_table=, softmax_scale=,
+ * causal=True) as called at engine/talker.py:77, and, when k_new/v_new are given, the index_copy_ append before it
+ * (engine/talker.py:72-73) fused into the same launch.
+ *   k_new == NULL: seat b attends over cache_seqlens[b] tokens.
+ *   k_new != NULL: the new K/V row of seat b is written at position cache_seqlens[b] and seat b attends over
+ *                  cache_seqlens[b] + 1 tokens (flash-attn's k/v-append semantics).
+ * A seat with nothing to attend gets a zero output. num_splits = CTAs sharing the work (0 = SMs x resident CTAs).
+ * The workspace (q3_paged_decode_workspace_bytes) must be zero-filled once before its first use; every launch leaves
+ * it ready for the next. Calls that share one workspace must not overlap on the GPU. */
+size_t q3_paged_decode_workspace_bytes(int32_t batch, int32_t num_splits);
+int q3_paged_decode(const void* q, int64_t q_batch_stride,
+                    const void* k_new, const void* v_new, int64_t kv_new_batch_stride,
+                    void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,
+                    const int32_t* cache_seqlens,
+                    const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
+                    int32_t batch, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                    float softmax_scale,
+                    void* out, int64_t out_batch_stride,
+                    void* workspace, size_t workspace_bytes, int32_t num_splits,
+                    void* stream);
+/* Kernel variant used by q3_paged_decode: 0 = 16-token chunks x 3 stages (1 CTA/SM, default),
+ * 1 = 8-token chunks x 3 stages (2 CTAs/SM), 2 = 16-token chunks x 2 stages. Returns the previous value. */
+int q3_set_decode_variant(int variant);
+
+/* ---------------------------------------------------------------- K/V append into pages
+ * Replaces kc[l].view(-1, nkv, hd).index_copy_(0, slot, k) (and the same for V): engine/talker.py:72-73 and 161-162,
+ * engine/arrivals.py:144-145. Row i of k/v (n_rows rows of num_kv_heads*head_dim bf16, row stride row_stride
+ * elements) is written to pool row slots[i] (flat row index in [0, pool_rows)). Placement is bit-exact. */
+int q3_kv_append_slots(const void* k, const void* v, int64_t row_stride,
+                       void* k_pool, void* v_pool, int64_t pool_rows,
+                       int32_t num_kv_heads, int32_t head_dim,
+                       const int64_t* slots, int32_t n_rows, void* stream);
+/* Same, addressed by (seat, position) through the block table: row i goes to token positions[i] of seat
+ * seat_of_row[i] (seat_of_row == NULL: seat i), i.e. pool row block_table[seat, pos / page_size] * page_size +
+ * pos % page_size. */
+int q3_kv_append_paged(const void* k, const void* v, int64_t row_stride,
+                       void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,
+                       int32_t num_kv_heads, int32_t head_dim,
+                       const int32_t* positions, const int32_t* seat_of_row,
+                       const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
+                       int32_t n_rows, void* stream);
+
+/* ---------------------------------------------------------------- code-predictor attention
+ * Replaces cp_attn(q, K, V, n_live, scale) (engine/cp_attn.py:33-39), i.e. the attention expression of
+ * CodePredictor._post (engine/code_predictor.py:46-47): q [B,16,128] over slots 0..n_live-1 of K/V [B,8,S,128];
+ * fp32 scores and softmax, probabilities rounded to bf16, fp32 P.V, bf16 out [B, 2048]. 1 <= n_live <= min(S,16). */
+int q3_cp_attn(const void* q, int64_t q_batch_stride,
+               const void* K, const void* V,
+               int64_t k_batch_stride, int64_t k_head_stride, int64_t k_slot_stride,
+               int64_t v_batch_stride, int64_t v_head_stride, int64_t v_slot_stride,
+               int32_t batch, int32_t n_slots, int32_t n_live, float softmax_scale,
+               void* out, int64_t out_batch_stride, void* stream);
+/* One fused code-predictor step: writes k_new/v_new [B,8,128] into slot `slot` of K/V (engine/code_predictor.py:58,
+ * K.index_copy_(2, [p], k)) and attends over slots 0..slot (n_live = slot + 1), one launch per (step, layer). */
+int q3_cp_step(const void* q, int64_t q_batch_stride,
+               const void* k_new, const void* v_new, int64_t kv_new_batch_stride,
+               void* K, void* V,
+               int64_t k_batch_stride, int64_t k_head_stride, int64_t k_slot_stride,
+               int64_t v_batch_stride, int64_t v_head_stride, int64_t v_slot_stride,
+               int32_t batch, int32_t n_slots, int32_t slot, float softmax_scale,
+               void* out, int64_t out_batch_stride, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q3ATTN_H_ */

@@ -1,0 +1,296 @@
+// C ABI of q3attn (declared in include/q3attn.h): argument checks on the host, then one kernel launch per call.
+#include <cstdio>
+#include <cstring>
+
+#include "q3_common.cuh"
+#include "q3_kernels.h"
+#include "q3attn.h"
+
+namespace {
+
+__device__ uint32_t g_status_word;   // OR of q3::kStatus* bits raised by any kernel of this library on this device
+
+constexpr int kMaxDevices = 64;
+thread_local char t_last_cuda_error[256] = "";
+int g_decode_variant = 0;
+int g_sm_count[kMaxDevices] = {0};
+uint32_t* g_status_ptr[kMaxDevices] = {nullptr};
+
+int record(cudaError_t e) {
+  if (e == cudaSuccess) return Q3_OK;
+  snprintf(t_last_cuda_error, sizeof(t_last_cuda_error), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+  return Q3_ERR_CUDA;
+}
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return record(e);
+  if (*dev < 0 || *dev >= kMaxDevices) return Q3_ERR_UNSUPPORTED;
+  return Q3_OK;
+}
+
+int sm_count(int dev) {
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+// Device address of the status word of `dev` (cudaGetSymbolAddress with `dev` current).
+int status_ptr(int dev, uint32_t** out) {
+  if (g_status_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_status_word);
+    if (e != cudaSuccess) return record(e);
+    g_status_ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  *out = g_status_ptr[dev];
+  return Q3_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_family(int32_t nh, int32_t nkv, int32_t hd) {
+  return (nh == q3::kQHeads && nkv == q3::kKvHeads && hd == q3::kHeadDim) ? Q3_OK : Q3_ERR_UNSUPPORTED;
+}
+
+long long decode_grid(int dev, int32_t batch, int32_t num_splits, int32_t max_pages, int32_t page_size) {
+  const int rows = q3::decode_rows_per_chunk(g_decode_variant);
+  long long G = num_splits > 0 ? num_splits : static_cast<long long>(sm_count(dev)) * q3::decode_ctas_per_sm(g_decode_variant);
+  const long long max_chunks = static_cast<long long>(batch) * ((static_cast<long long>(max_pages) * page_size + rows - 1) / rows);
+  if (max_pages > 0 && page_size > 0 && G > max_chunks) G = max_chunks;
+  return G < 1 ? 1 : G;
+}
+
+struct WsLayout {
+  size_t counters, ml, o, total;
+};
+
+WsLayout ws_layout(int32_t batch, long long G) {
+  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  WsLayout w;
+  const size_t slots = static_cast<size_t>(G) + static_cast<size_t>(batch);
+  w.counters = 0;
+  w.ml = up(static_cast<size_t>(batch) * q3::kKvHeads * sizeof(uint32_t));
+  w.o = w.ml + up(slots * q3::kKvHeads * q3::kGroup * 2 * sizeof(float));
+  w.total = w.o + up(slots * q3::kKvHeads * q3::kGroup * q3::kHeadDim * sizeof(float));
+  return w;
+}
+
+}  // namespace
+
+extern "C" {
+
+int q3_version(void) { return 100; }
+
+const char* q3_error_string(int code) {
+  switch (code) {
+    case Q3_OK: return "ok";
+    case Q3_ERR_INVALID: return "invalid argument";
+    case Q3_ERR_UNSUPPORTED: return "unsupported shape (compiled for 16 q heads, 8 kv heads, head_dim 128)";
+    case Q3_ERR_ALIGNMENT: return "misaligned pointer or stride";
+    case Q3_ERR_WORKSPACE: return "workspace missing or too small";
+    case Q3_ERR_CUDA: return "CUDA runtime error";
+    default: return "unknown error";
+  }
+}
+
+const char* q3_last_cuda_error(void) { return t_last_cuda_error; }
+
+int q3_device_sm_count(void) {
+  int dev = 0;
+  if (current_device(&dev) != Q3_OK) return 0;
+  return sm_count(dev);
+}
+
+int q3_read_status(uint32_t* status_out, int clear) {
+  int dev = 0, rc = current_device(&dev);
+  if (rc != Q3_OK) return rc;
+  uint32_t* p = nullptr;
+  if ((rc = status_ptr(dev, &p)) != Q3_OK) return rc;
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpy(&v, p, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return record(e);
+  if (status_out) *status_out = v;
+  if (clear) {
+    e = cudaMemset(p, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) return record(e);
+  }
+  return Q3_OK;
+}
+
+int q3_set_decode_variant(int variant) {
+  const int prev = g_decode_variant;
+  if (variant >= 0 && variant <= 2) g_decode_variant = variant;
+  return prev;
+}
+
+size_t q3_paged_decode_workspace_bytes(int32_t batch, int32_t num_splits) {
+  int dev = 0;
+  if (batch < 0 || current_device(&dev) != Q3_OK) return 0;
+  // Upper bound over all block-table shapes: the grid is at most SMs x CTAs/SM (or num_splits).
+  const long long G = decode_grid(dev, batch, num_splits, 0, 0);
+  return ws_layout(batch, G).total;
+}
+
+int q3_paged_decode(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
+                    int64_t kv_new_batch_stride, void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,
+                    const int32_t* cache_seqlens, const int32_t* block_table, int64_t block_table_stride,
+                    int32_t max_pages_per_seat, int32_t batch, int32_t num_heads, int32_t num_kv_heads,
+                    int32_t head_dim, float softmax_scale, void* out, int64_t out_batch_stride, void* workspace,
+                    size_t workspace_bytes, int32_t num_splits, void* stream) {
+  int rc = check_family(num_heads, num_kv_heads, head_dim);
+  if (rc != Q3_OK) return rc;
+  if (batch < 0 || num_pages <= 0 || page_size <= 0 || max_pages_per_seat <= 0 || num_splits < 0) return Q3_ERR_INVALID;
+  if (batch == 0) return Q3_OK;
+  if (!q || !k_pool || !v_pool || !cache_seqlens || !block_table || !out) return Q3_ERR_INVALID;
+  if ((k_new == nullptr) != (v_new == nullptr)) return Q3_ERR_INVALID;
+  if (block_table_stride < max_pages_per_seat || q_batch_stride < q3::kQHeads * q3::kHeadDim ||
+      out_batch_stride < q3::kQHeads * q3::kHeadDim)
+    return Q3_ERR_INVALID;
+  if (static_cast<long long>(max_pages_per_seat) * page_size > (1ll << 30)) return Q3_ERR_INVALID;
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 8) || !aligned(out, 8) || (q_batch_stride % 4) ||
+      (out_batch_stride % 4))
+    return Q3_ERR_ALIGNMENT;
+  if (k_new && (!aligned(k_new, 16) || !aligned(v_new, 16) || (kv_new_batch_stride % 8) ||
+                kv_new_batch_stride < q3::kKvHeads * q3::kHeadDim))
+    return Q3_ERR_ALIGNMENT;
+  int dev = 0;
+  if ((rc = current_device(&dev)) != Q3_OK) return rc;
+  const long long G = decode_grid(dev, batch, num_splits, max_pages_per_seat, page_size);
+  if (G > (1ll << 30)) return Q3_ERR_INVALID;
+  const WsLayout w = ws_layout(batch, G);
+  if (!workspace || workspace_bytes < w.total || !aligned(workspace, 256)) return Q3_ERR_WORKSPACE;
+  uint32_t* st = nullptr;
+  if ((rc = status_ptr(dev, &st)) != Q3_OK) return rc;
+
+  q3::DecodeArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_stride = q_batch_stride;
+  a.k_new = static_cast<const __nv_bfloat16*>(k_new);
+  a.v_new = static_cast<const __nv_bfloat16*>(v_new);
+  a.kv_new_stride = kv_new_batch_stride;
+  a.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+  a.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+  a.seqlens = cache_seqlens;
+  a.block_table = block_table;
+  a.bt_stride = block_table_stride;
+  a.max_pages = max_pages_per_seat;
+  a.num_pages = num_pages;
+  a.page_size = page_size;
+  a.B = batch;
+  a.scale_log2 = softmax_scale * q3::kLog2e;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_stride = out_batch_stride;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  a.counters = reinterpret_cast<uint32_t*>(ws + w.counters);
+  a.ws_ml = reinterpret_cast<float*>(ws + w.ml);
+  a.ws_o = reinterpret_cast<float*>(ws + w.o);
+  a.status = st;
+  return record(q3::launch_paged_decode(a, static_cast<int>(G), g_decode_variant, static_cast<cudaStream_t>(stream)));
+}
+
+static int append_common(q3::AppendArgs& a, const void* k, const void* v, int64_t row_stride, void* k_pool,
+                         void* v_pool, int32_t nkv, int32_t hd, int32_t n_rows, void* stream) {
+  if (n_rows < 0 || nkv <= 0 || hd <= 0) return Q3_ERR_INVALID;
+  if (n_rows == 0) return Q3_OK;
+  if (!k || !v || !k_pool || !v_pool) return Q3_ERR_INVALID;
+  const int row_elems = nkv * hd;
+  if (row_elems % 8 || row_stride < row_elems) return Q3_ERR_INVALID;
+  if (!aligned(k, 16) || !aligned(v, 16) || !aligned(k_pool, 16) || !aligned(v_pool, 16) || (row_stride % 8))
+    return Q3_ERR_ALIGNMENT;
+  int dev = 0, rc = current_device(&dev);
+  if (rc != Q3_OK) return rc;
+  uint32_t* st = nullptr;
+  if ((rc = status_ptr(dev, &st)) != Q3_OK) return rc;
+  a.k_rows = static_cast<const __nv_bfloat16*>(k);
+  a.v_rows = static_cast<const __nv_bfloat16*>(v);
+  a.rows_stride = row_stride;
+  a.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+  a.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+  a.row_elems = row_elems;
+  a.n_rows = n_rows;
+  a.status = st;
+  return record(q3::launch_kv_append(a, sm_count(dev), static_cast<cudaStream_t>(stream)));
+}
+
+int q3_kv_append_slots(const void* k, const void* v, int64_t row_stride, void* k_pool, void* v_pool, int64_t pool_rows,
+                       int32_t num_kv_heads, int32_t head_dim, const int64_t* slots, int32_t n_rows, void* stream) {
+  if (n_rows > 0 && (!slots || pool_rows <= 0)) return Q3_ERR_INVALID;
+  q3::AppendArgs a{};
+  a.slots = slots;
+  a.pool_rows = pool_rows;
+  a.page_size = 1;
+  return append_common(a, k, v, row_stride, k_pool, v_pool, num_kv_heads, head_dim, n_rows, stream);
+}
+
+int q3_kv_append_paged(const void* k, const void* v, int64_t row_stride, void* k_pool, void* v_pool, int32_t num_pages,
+                       int32_t page_size, int32_t num_kv_heads, int32_t head_dim, const int32_t* positions,
+                       const int32_t* seat_of_row, const int32_t* block_table, int64_t block_table_stride,
+                       int32_t max_pages_per_seat, int32_t n_rows, void* stream) {
+  if (n_rows > 0 && (!positions || !block_table || num_pages <= 0 || page_size <= 0 || max_pages_per_seat <= 0 ||
+                     block_table_stride < max_pages_per_seat))
+    return Q3_ERR_INVALID;
+  q3::AppendArgs a{};
+  a.positions = positions;
+  a.seat_of_row = seat_of_row;
+  a.block_table = block_table;
+  a.bt_stride = block_table_stride;
+  a.max_pages = max_pages_per_seat;
+  a.page_size = page_size;
+  a.pool_rows = static_cast<long long>(num_pages) * page_size;
+  return append_common(a, k, v, row_stride, k_pool, v_pool, num_kv_heads, head_dim, n_rows, stream);
+}
+
+static int cp_common(q3::CpArgs& a, const void* q, int64_t q_batch_stride, void* K, void* V, int64_t kb, int64_t kh,
+                     int64_t ks, int64_t vb, int64_t vh, int64_t vs, int32_t batch, int32_t n_slots, int32_t n_live,
+                     float scale, void* out, int64_t out_stride, void* stream) {
+  if (batch < 0 || n_slots <= 0 || n_live < 1 || n_live > n_slots) return Q3_ERR_INVALID;
+  if (n_live > 16) return Q3_ERR_UNSUPPORTED;
+  if (batch == 0) return Q3_OK;
+  if (!q || !K || !V || !out) return Q3_ERR_INVALID;
+  if (q_batch_stride < q3::kQHeads * q3::kHeadDim || out_stride < q3::kQHeads * q3::kHeadDim) return Q3_ERR_INVALID;
+  if (!aligned(q, 8) || !aligned(K, 8) || !aligned(V, 8) || !aligned(out, 8) || (q_batch_stride % 4) || (out_stride % 4) ||
+      (kb % 4) || (kh % 4) || (ks % 4) || (vb % 4) || (vh % 4) || (vs % 4))
+    return Q3_ERR_ALIGNMENT;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_stride = q_batch_stride;
+  a.K = static_cast<__nv_bfloat16*>(K);
+  a.V = static_cast<__nv_bfloat16*>(V);
+  a.sk_b = kb; a.sk_h = kh; a.sk_s = ks;
+  a.sv_b = vb; a.sv_h = vh; a.sv_s = vs;
+  a.B = batch;
+  a.n_live = n_live;
+  a.scale_log2 = scale * q3::kLog2e;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_stride = out_stride;
+  return record(q3::launch_cp_attn(a, static_cast<cudaStream_t>(stream)));
+}
+
+int q3_cp_attn(const void* q, int64_t q_batch_stride, const void* K, const void* V, int64_t k_batch_stride,
+               int64_t k_head_stride, int64_t k_slot_stride, int64_t v_batch_stride, int64_t v_head_stride,
+               int64_t v_slot_stride, int32_t batch, int32_t n_slots, int32_t n_live, float softmax_scale, void* out,
+               int64_t out_batch_stride, void* stream) {
+  q3::CpArgs a{};
+  return cp_common(a, q, q_batch_stride, const_cast<void*>(K), const_cast<void*>(V), k_batch_stride, k_head_stride,
+                   k_slot_stride, v_batch_stride, v_head_stride, v_slot_stride, batch, n_slots, n_live, softmax_scale,
+                   out, out_batch_stride, stream);
+}
+
+int q3_cp_step(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new, int64_t kv_new_batch_stride,
+               void* K, void* V, int64_t k_batch_stride, int64_t k_head_stride, int64_t k_slot_stride,
+               int64_t v_batch_stride, int64_t v_head_stride, int64_t v_slot_stride, int32_t batch, int32_t n_slots,
+               int32_t slot, float softmax_scale, void* out, int64_t out_batch_stride, void* stream) {
+  if (batch > 0 && (!k_new || !v_new || kv_new_batch_stride < q3::kKvHeads * q3::kHeadDim)) return Q3_ERR_INVALID;
+  if (batch > 0 && (!aligned(k_new, 8) || !aligned(v_new, 8) || (kv_new_batch_stride % 4))) return Q3_ERR_ALIGNMENT;
+  q3::CpArgs a{};
+  a.k_new = static_cast<const __nv_bfloat16*>(k_new);
+  a.v_new = static_cast<const __nv_bfloat16*>(v_new);
+  a.kv_new_stride = kv_new_batch_stride;
+  return cp_common(a, q, q_batch_stride, K, V, k_batch_stride, k_head_stride, k_slot_stride, v_batch_stride,
+                   v_head_stride, v_slot_stride, batch, n_slots, slot + 1, softmax_scale, out, out_batch_stride, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,103 @@
+// Code-predictor attention step, sm_100a: one query token over a per-seat 16-slot K/V cache, GQA 16/8, head_dim 128.
+//
+// Replaces, per (step, layer) of CodePredictor._s (engine/code_predictor.py:52-60):
+//   K.index_copy_(2, [p], k); V.index_copy_(2, [p], v)                  engine/code_predictor.py:58
+//   att = q.view(B,8,2,128) @ K^T * scale + mask[p]; softmax; @ V       engine/code_predictor.py:46-47
+// with the arithmetic of the reference's intended kernel cp_attn (engine/cp_attn.py:14-30): fp32 scores and softmax,
+// probabilities rounded to bf16 before P.V, fp32 accumulation, bf16 output. Slots >= n_live are not read.
+//
+// One CTA per seat, one warp per KV head; lane l owns dims 4l..4l+3 of both q heads of the group. All K and V rows are
+// loaded up front (at most 16 x 8 bytes each per lane) so the whole step costs one round of memory latency. With k_new
+// given, the new row is stored to slot n_live-1 and used from registers.
+#include "q3_common.cuh"
+#include "q3_kernels.h"
+
+namespace q3 {
+
+__global__ void __launch_bounds__(256) cp_attn_kernel(const CpArgs a) {
+  __shared__ float pbuf[kKvHeads][32];
+  const int b = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = a.n_live, pnew = n - 1;
+  const bool append = a.k_new != nullptr;
+
+  const __nv_bfloat16* qp = a.q + static_cast<long long>(b) * a.q_stride + (2 * h) * kHeadDim + 4 * lane;
+  float4 q0 = bf16x4_to_float4(*reinterpret_cast<const uint2*>(qp));
+  float4 q1 = bf16x4_to_float4(*reinterpret_cast<const uint2*>(qp + kHeadDim));
+
+  const __nv_bfloat16* kb = a.K + static_cast<long long>(b) * a.sk_b + h * a.sk_h + 4 * lane;
+  const __nv_bfloat16* vb = a.V + static_cast<long long>(b) * a.sv_b + h * a.sv_h + 4 * lane;
+  uint2 kw[16], vw[16];
+  uint2 kn = make_uint2(0, 0), vn = make_uint2(0, 0);
+  if (append) {
+    const long long off = static_cast<long long>(b) * a.kv_new_stride + h * kHeadDim + 4 * lane;
+    kn = *reinterpret_cast<const uint2*>(a.k_new + off);
+    vn = *reinterpret_cast<const uint2*>(a.v_new + off);
+  }
+#pragma unroll
+  for (int s = 0; s < 16; ++s) {
+    if (s < n) {
+      if (append && s == pnew) {
+        kw[s] = kn;
+        vw[s] = vn;
+      } else {
+        kw[s] = *reinterpret_cast<const uint2*>(kb + s * a.sk_s);
+        vw[s] = *reinterpret_cast<const uint2*>(vb + s * a.sv_s);
+      }
+    }
+  }
+  if (append) {
+    *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(kb) + pnew * a.sk_s) = kn;
+    *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(vb) + pnew * a.sv_s) = vn;
+  }
+
+  const float sl = a.scale_log2;
+  q0.x *= sl; q0.y *= sl; q0.z *= sl; q0.w *= sl;
+  q1.x *= sl; q1.y *= sl; q1.z *= sl; q1.w *= sl;
+  float sc[32];
+#pragma unroll
+  for (int s = 0; s < 16; ++s) {
+    if (s < n) {
+      const float4 k = bf16x4_to_float4(kw[s]);
+      sc[s] = q0.x * k.x + q0.y * k.y + q0.z * k.z + q0.w * k.w;
+      sc[16 + s] = q1.x * k.x + q1.y * k.y + q1.z * k.z + q1.w * k.w;
+    } else {
+      sc[s] = 0.f;
+      sc[16 + s] = 0.f;
+    }
+  }
+  const float x0 = transpose_reduce<32>(sc, lane);   // lane l: q head (l >> 4) of the group, slot (l & 15)
+  const bool valid = (lane & 15) < n;
+  const float x = valid ? x0 : -INFINITY;
+  float m = x;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float p = valid ? exp2f(x - m) : 0.f;
+  float sum = p;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  p = round_bf16(p / sum);                            // engine/cp_attn.py:26-27: P rounded to the model dtype
+  pbuf[h][lane] = p;
+  __syncwarp();
+
+  float4 o0 = make_float4(0, 0, 0, 0), o1 = o0;
+#pragma unroll
+  for (int s = 0; s < 16; ++s) {
+    if (s < n) {
+      const float p0 = pbuf[h][s], p1 = pbuf[h][16 + s];
+      const float4 v = bf16x4_to_float4(vw[s]);
+      o0.x += p0 * v.x; o0.y += p0 * v.y; o0.z += p0 * v.z; o0.w += p0 * v.w;
+      o1.x += p1 * v.x; o1.y += p1 * v.y; o1.z += p1 * v.z; o1.w += p1 * v.w;
+    }
+  }
+  __nv_bfloat16* op = a.out + static_cast<long long>(b) * a.out_stride + (2 * h) * kHeadDim + 4 * lane;
+  *reinterpret_cast<uint2*>(op) = float4_to_bf16x4(o0);
+  *reinterpret_cast<uint2*>(op + kHeadDim) = float4_to_bf16x4(o1);
+}
+
+cudaError_t launch_cp_attn(const CpArgs& a, cudaStream_t stream) {
+  if (a.B == 0) return cudaSuccess;
+  cp_attn_kernel<<<a.B, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace q3

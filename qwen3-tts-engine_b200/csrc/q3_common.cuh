@@ -1,0 +1,155 @@
+// Shared device helpers for the q3attn kernels (sm_100a only).
+//
+// Layout facts used everywhere (the engine's model family, engine/talker.py:26-31):
+//   16 query heads, 8 KV heads (GQA group 2: q head h reads KV head h/2), head_dim 128, bf16 storage.
+//   A KV pool is [num_pages, page_size, 8, 128] bf16: one token row holds all 8 KV heads = 2048 contiguous bytes, and
+//   one KV head of a row is 256 contiguous bytes.
+#pragma once
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "q3attn kernels are written for sm_100a (B200) only"
+#endif
+
+namespace q3 {
+
+constexpr int kHeadDim = 128;
+constexpr int kKvHeads = 8;
+constexpr int kGroup = 2;                       // q heads per KV head
+constexpr int kQHeads = kKvHeads * kGroup;      // 16
+constexpr int kRowBytes = kKvHeads * kHeadDim * 2;   // 2048: one token row, all KV heads
+constexpr int kHeadBytes = kHeadDim * 2;             // 256: one KV head of one token row
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Error bits a kernel may OR into its status word (read back by q3_read_status()).
+enum : uint32_t {
+  kStatusWaitTimeout = 1u << 0,   // an mbarrier wait gave up after its time limit
+  kStatusBadPage = 1u << 1,       // a block-table entry outside [0, num_pages)
+  kStatusBadLength = 1u << 2,     // a sequence length beyond the block table's capacity
+};
+
+// ---------------------------------------------------------------- bf16 <-> fp32
+// Four bf16 packed in a uint2 -> four floats (a bf16 is the top half of an fp32).
+__device__ __forceinline__ float4 bf16x4_to_float4(uint2 w) {
+  float4 f;
+  f.x = __uint_as_float(w.x << 16);
+  f.y = __uint_as_float(w.x & 0xffff0000u);
+  f.z = __uint_as_float(w.y << 16);
+  f.w = __uint_as_float(w.y & 0xffff0000u);
+  return f;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint2 float4_to_bf16x4(float4 f) {
+  return make_uint2(pack_bf16x2(f.x, f.y), pack_bf16x2(f.z, f.w));
+}
+
+__device__ __forceinline__ float round_bf16(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// ---------------------------------------------------------------- shared-memory barriers and bulk copies
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for phase `parity` of `bar` to complete, giving up after ~`limit_ns` (default 2 s). Returns false on timeout.
+// No wait in these kernels is expected to take more than microseconds; the limit only turns a broken pipeline into an
+// error status instead of a hung GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {
+#pragma unroll 1
+  for (int i = 0; i < 4096; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+#pragma unroll 1
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// One-dimensional bulk copy global -> this CTA's shared memory, completion signalled on `bar` as transaction bytes.
+// dst/src 16-byte aligned, bytes a multiple of 16 (the callers copy whole 2048-byte token rows).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------- global loads
+__device__ __forceinline__ uint2 ld_nc_u2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Reduce NV per-lane partial sums across the warp so that each lane ends with ONE complete sum.
+// After the call v[0] of lane l holds the full sum of value index (l >> (5 - log2 NV)); e.g. NV = 32 -> index l,
+// NV = 16 -> index l/2 (lane pairs hold the same total). Each halving step trades half the values with the partner lane.
+template <int NV>
+__device__ __forceinline__ float transpose_reduce(float (&v)[NV], int lane) {
+  static_assert(NV >= 1 && NV <= 32 && (NV & (NV - 1)) == 0, "NV must be a power of two <= 32");
+  int off = 16;
+#pragma unroll
+  for (int n = NV; n > 1; n >>= 1, off >>= 1) {
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = up ? v[i] : v[i + n / 2];
+      const float keep = up ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+#pragma unroll
+  for (; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+  return v[0];
+}
+
+}  // namespace q3

@@ -1,0 +1,78 @@
+// Internal launch interface between the C-ABI layer (capi.cu) and the kernels. Not installed; include/q3attn.h is the
+// public boundary.
+#pragma once
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace q3 {
+
+struct DecodeArgs {
+  const __nv_bfloat16* q;          // [B, 16, 128] rows, batch stride q_stride (elements)
+  long long q_stride;
+  const __nv_bfloat16* k_new;      // [B, 8, 128] or nullptr (no append)
+  const __nv_bfloat16* v_new;
+  long long kv_new_stride;
+  __nv_bfloat16* k_pool;           // [num_pages, page_size, 8, 128] contiguous
+  __nv_bfloat16* v_pool;
+  const int32_t* seqlens;          // [B] tokens in the cache before the append (== tokens attended without append)
+  const int32_t* block_table;      // [B, bt_stride] (first max_pages entries of a row are usable)
+  long long bt_stride;
+  int max_pages;
+  int num_pages;
+  int page_size;
+  int B;
+  float scale_log2;                // softmax_scale * log2(e)
+  __nv_bfloat16* out;              // [B, 16, 128] rows, batch stride out_stride
+  long long out_stride;
+  float* ws_o;                     // [(G + B), 8, 2, 128] fp32 partial outputs
+  float* ws_ml;                    // [(G + B), 8, 2, 2] fp32 (running max, running sum)
+  uint32_t* counters;              // [B, 8] zero between launches
+  uint32_t* status;
+};
+
+int decode_rows_per_chunk(int variant);
+int decode_ctas_per_sm(int variant);
+cudaError_t launch_paged_decode(const DecodeArgs& a, int grid, int variant, cudaStream_t stream);
+
+struct AppendArgs {
+  const __nv_bfloat16* k_rows;     // [n_rows, row_elems] with row stride rows_stride (elements)
+  const __nv_bfloat16* v_rows;
+  long long rows_stride;
+  __nv_bfloat16* k_pool;           // [num_pages * page_size, row_elems]
+  __nv_bfloat16* v_pool;
+  long long pool_rows;             // num_pages * page_size
+  int page_size;
+  int row_elems;                   // nkv * head_dim
+  int n_rows;
+  const int64_t* slots;            // flat destination row per input row, or nullptr
+  const int32_t* positions;        // token position per input row (paged mode)
+  const int32_t* seat_of_row;      // seat per input row (paged mode; nullptr = row i belongs to seat i)
+  const int32_t* block_table;
+  long long bt_stride;
+  int max_pages;
+  uint32_t* status;
+};
+
+cudaError_t launch_kv_append(const AppendArgs& a, int num_sms, cudaStream_t stream);
+
+struct CpArgs {
+  const __nv_bfloat16* q;          // [B, 16, 128] rows, batch stride q_stride
+  long long q_stride;
+  const __nv_bfloat16* k_new;      // [B, 8, 128] or nullptr (attention only)
+  const __nv_bfloat16* v_new;
+  long long kv_new_stride;
+  __nv_bfloat16* K;                // [B, 8, S, 128] with strides (elements) sk_b, sk_h, sk_s; innermost contiguous
+  __nv_bfloat16* V;
+  long long sk_b, sk_h, sk_s;
+  long long sv_b, sv_h, sv_s;
+  int B;
+  int n_live;                      // slots attended: 1..16; with k_new the new row lands in slot n_live - 1
+  float scale_log2;
+  __nv_bfloat16* out;              // [B, 16*128] rows, batch stride out_stride
+  long long out_stride;
+};
+
+cudaError_t launch_cp_attn(const CpArgs& a, cudaStream_t stream);
+
+}  // namespace q3

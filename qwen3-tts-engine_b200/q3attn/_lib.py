@@ -1,0 +1,73 @@
+"""ctypes binding of libq3attn.so (the C ABI declared in include/q3attn.h).
+
+The library is loaded from this package directory. There is no fallback: if it is missing or fails to load, importing
+the ops raises, so a caller can never silently run something other than the CUDA kernels.
+"""
+import ctypes
+import os
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libq3attn.so")
+
+Q3_OK, Q3_ERR_INVALID, Q3_ERR_UNSUPPORTED, Q3_ERR_ALIGNMENT, Q3_ERR_WORKSPACE, Q3_ERR_CUDA = range(6)
+STATUS_WAIT_TIMEOUT, STATUS_BAD_PAGE, STATUS_BAD_LENGTH = 1, 2, 4
+
+_P, _I32, _I64, _F32, _SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+
+# name -> (restype, argtypes); every symbol include/q3attn.h declares
+SIGNATURES = {
+    "q3_version": (ctypes.c_int, []),
+    "q3_error_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "q3_last_cuda_error": (ctypes.c_char_p, []),
+    "q3_device_sm_count": (ctypes.c_int, []),
+    "q3_read_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
+    "q3_paged_decode_workspace_bytes": (_SZ, [_I32, _I32]),
+    "q3_paged_decode": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P, _I32, _I32, _P, _P, _I64, _I32,
+                                       _I32, _I32, _I32, _I32, _F32, _P, _I64, _P, _SZ, _I32, _P]),
+    "q3_set_decode_variant": (ctypes.c_int, [ctypes.c_int]),
+    "q3_kv_append_slots": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _I32, _I32, _P, _I32, _P]),
+    "q3_kv_append_paged": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _I64, _I32,
+                                          _I32, _P]),
+    "q3_cp_attn": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _F32,
+                                  _P, _I64, _P]),
+    "q3_cp_step": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
+                                  _I32, _F32, _P, _I64, _P]),
+}
+
+_lib = None
+
+
+class Q3Error(RuntimeError):
+    pass
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the library; raises Q3Error if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise Q3Error(f"q3attn CUDA library not built ({LIB_PATH} missing): run `python -m q3attn.build` "
+                      "from qwen3-tts-engine_b200/ or __graft_entry__.build()")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != Q3_OK:
+        lib = load()
+        msg = lib.q3_error_string(rc).decode()
+        if rc == Q3_ERR_CUDA:
+            msg += f" ({lib.q3_last_cuda_error().decode()})"
+        raise Q3Error(f"{what}: {msg}")
+
+
+def read_status(clear: bool = True) -> int:
+    """Device status bits (STATUS_*) raised by kernels since the last clear, for the current device."""
+    v = ctypes.c_uint32(0)
+    check(load().q3_read_status(ctypes.byref(v), int(clear)), "q3_read_status")
+    return int(v.value)

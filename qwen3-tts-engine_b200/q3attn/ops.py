@@ -1,0 +1,231 @@
+"""PyTorch custom ops over the q3attn C ABI (torch.library.custom_op, opaque to torch.compile, graph-capturable).
+
+Ops (namespace ``q3attn``):
+  paged_decode(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, num_splits) -> out
+  paged_decode_append(q, k, v, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, num_splits) -> out
+      (mutates k_cache/v_cache: the new rows land at position cache_seqlens[b])
+  kv_append_slots(k, v, k_cache, v_cache, slots)                      (mutates k_cache/v_cache)
+  kv_append_paged(k, v, k_cache, v_cache, positions, block_table, seat_of_row)   (mutates k_cache/v_cache)
+  cp_attn(q, K, V, n_live, softmax_scale) -> out [B, 2048]
+  cp_step(q, k, v, K, V, slot, softmax_scale) -> out [B, 2048]         (mutates K/V)
+
+Every op launches on torch.cuda.current_stream() of its tensors' device, so it is recorded by CUDA-graph capture.
+The decode workspace is a per-(device, stream) buffer allocated outside capture: run each batch shape once before
+capturing (the engine's warm-up passes do, engine/talker.py:120). Its observable content is unchanged by a call (the
+ticket counters return to zero), so it is not declared as a mutated argument.
+"""
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+NH, NKV, HD = 16, 8, 128
+
+_ws = {}                     # (device index, stream handle) -> uint8 workspace tensor
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(f"q3attn: {msg}")
+
+
+def _check_cuda_bf16(name: str, t: torch.Tensor) -> None:
+    _need(t.is_cuda, f"{name} must be a CUDA tensor (there is no CPU path)")
+    _need(t.dtype == torch.bfloat16, f"{name} must be bfloat16, got {t.dtype}")
+
+
+def workspace(batch: int, num_splits: int, device: torch.device) -> torch.Tensor:
+    """The zero-initialised decode workspace for (device, current stream), grown outside capture only."""
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        need = int(lib.q3_paged_decode_workspace_bytes(int(batch), int(num_splits)))
+        key = (device.index, _stream(device))
+        ws = _ws.get(key)
+        if ws is None or ws.numel() < need:
+            _need(not torch.cuda.is_current_stream_capturing(),
+                  "decode workspace must grow during CUDA-graph capture: run this batch size once before capturing")
+            ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
+            _ws[key] = ws
+        return ws
+
+
+def _decode_impl(q, k_new, v_new, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, num_splits):
+    lib = _lib.load()
+    B = q.shape[0]
+    _check_cuda_bf16("q", q)
+    _check_cuda_bf16("k_cache", k_cache)
+    _check_cuda_bf16("v_cache", v_cache)
+    _need(q.dim() == 3 and q.shape[1] == NH and q.shape[2] == HD, f"q must be [B, 16, 128], got {tuple(q.shape)}")
+    _need(q.stride(2) == 1 and q.stride(1) == HD, "q rows must be contiguous [16, 128]")
+    _need(k_cache.dim() == 4 and k_cache.shape[2] == NKV and k_cache.shape[3] == HD and k_cache.is_contiguous()
+          and v_cache.shape == k_cache.shape and v_cache.is_contiguous(),
+          "k_cache/v_cache must be contiguous [num_pages, page_size, 8, 128]")
+    _need(cache_seqlens.dtype == torch.int32 and cache_seqlens.is_cuda and cache_seqlens.numel() == B
+          and cache_seqlens.is_contiguous(), "cache_seqlens must be a contiguous int32 CUDA tensor [B]")
+    _need(block_table.dtype == torch.int32 and block_table.dim() == 2 and block_table.shape[0] == B
+          and block_table.stride(1) == 1, "block_table must be int32 [B, max_pages] with unit inner stride")
+    kvs = 0
+    if k_new is not None:
+        _check_cuda_bf16("k", k_new)
+        _check_cuda_bf16("v", v_new)
+        _need(k_new.shape == (B, NKV, HD) and v_new.shape == k_new.shape and k_new.stride(2) == 1
+              and k_new.stride(1) == HD and v_new.stride() == k_new.stride(), "k/v must be [B, 8, 128] rows")
+        kvs = k_new.stride(0)
+    out = torch.empty(B, NH, HD, dtype=torch.bfloat16, device=q.device)
+    if B == 0:
+        return out
+    ws = workspace(B, num_splits, q.device)
+    with torch.cuda.device(q.device):
+        rc = lib.q3_paged_decode(
+            q.data_ptr(), q.stride(0), _ptr(k_new), _ptr(v_new), kvs,
+            k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0], k_cache.shape[1],
+            cache_seqlens.data_ptr(), block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+            B, NH, NKV, HD, float(softmax_scale), out.data_ptr(), out.stride(0),
+            ws.data_ptr(), ws.numel(), int(num_splits), _stream(q.device))
+    _lib.check(rc, "q3_paged_decode")
+    return out
+
+
+@torch.library.custom_op("q3attn::paged_decode", mutates_args=())
+def paged_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, cache_seqlens: torch.Tensor,
+                 block_table: torch.Tensor, softmax_scale: float, num_splits: int = 0) -> torch.Tensor:
+    """Decode attention of q [B,16,128] over cache_seqlens[b] tokens of seat b's pages -> [B,16,128] bf16."""
+    return _decode_impl(q, None, None, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, num_splits)
+
+
+@paged_decode.register_fake
+def _(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, num_splits=0):
+    return q.new_empty(q.shape[0], NH, HD)
+
+
+@torch.library.custom_op("q3attn::paged_decode_append", mutates_args=("k_cache", "v_cache"))
+def paged_decode_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor,
+                        v_cache: torch.Tensor, cache_seqlens: torch.Tensor, block_table: torch.Tensor,
+                        softmax_scale: float, num_splits: int = 0) -> torch.Tensor:
+    """Append k/v [B,8,128] at position cache_seqlens[b], then attend over cache_seqlens[b] + 1 tokens (one launch)."""
+    return _decode_impl(q, k, v, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, num_splits)
+
+
+@paged_decode_append.register_fake
+def _(q, k, v, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, num_splits=0):
+    return q.new_empty(q.shape[0], NH, HD)
+
+
+def _rows(name, t, n_rows_dims=1):
+    _check_cuda_bf16(name, t)
+    _need(t.dim() >= 2 and t.shape[-1] == HD and t.shape[-2] == NKV and t.stride(-1) == 1 and t.stride(-2) == HD,
+          f"{name} must be rows of [8, 128] contiguous elements")
+    return t.reshape(-1, NKV, HD) if t.dim() != 3 else t
+
+
+@torch.library.custom_op("q3attn::kv_append_slots", mutates_args=("k_cache", "v_cache"))
+def kv_append_slots(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    slots: torch.Tensor) -> None:
+    """k_cache.view(-1,8,128).index_copy_(0, slots, k) and the same for v (engine/talker.py:72-73)."""
+    lib = _lib.load()
+    k, v = _rows("k", k), _rows("v", v)
+    _check_cuda_bf16("k_cache", k_cache)
+    _check_cuda_bf16("v_cache", v_cache)
+    _need(k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.shape == v_cache.shape
+          and k_cache.shape[-1] == HD and k_cache.shape[-2] == NKV, "caches must be contiguous [..., 8, 128]")
+    _need(v.shape == k.shape and v.stride(0) == k.stride(0), "k and v must have the same shape and row stride")
+    s = slots.to(device=k.device, dtype=torch.int64).contiguous()
+    _need(s.numel() == k.shape[0], "one slot per row")
+    with torch.cuda.device(k.device):
+        rc = lib.q3_kv_append_slots(k.data_ptr(), v.data_ptr(), k.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                    k_cache.numel() // (NKV * HD), NKV, HD, s.data_ptr(), k.shape[0], _stream(k.device))
+    _lib.check(rc, "q3_kv_append_slots")
+
+
+@torch.library.custom_op("q3attn::kv_append_paged", mutates_args=("k_cache", "v_cache"))
+def kv_append_paged(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    positions: torch.Tensor, block_table: torch.Tensor,
+                    seat_of_row: Optional[torch.Tensor] = None) -> None:
+    """Row i -> token positions[i] of seat seat_of_row[i] (default: seat i) through the block table."""
+    lib = _lib.load()
+    k, v = _rows("k", k), _rows("v", v)
+    _check_cuda_bf16("k_cache", k_cache)
+    _check_cuda_bf16("v_cache", v_cache)
+    _need(k_cache.dim() == 4 and k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.shape == v_cache.shape,
+          "caches must be contiguous [num_pages, page_size, 8, 128]")
+    _need(v.shape == k.shape and v.stride(0) == k.stride(0), "k and v must have the same shape and row stride")
+    pos = positions.to(device=k.device, dtype=torch.int32).contiguous()
+    _need(block_table.dtype == torch.int32 and block_table.dim() == 2 and block_table.stride(1) == 1,
+          "block_table must be int32 [seats, max_pages]")
+    sor = None if seat_of_row is None else seat_of_row.to(device=k.device, dtype=torch.int32).contiguous()
+    with torch.cuda.device(k.device):
+        rc = lib.q3_kv_append_paged(k.data_ptr(), v.data_ptr(), k.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                    k_cache.shape[0], k_cache.shape[1], NKV, HD, pos.data_ptr(), _ptr(sor),
+                                    block_table.data_ptr(), block_table.stride(0), block_table.shape[1], k.shape[0],
+                                    _stream(k.device))
+    _lib.check(rc, "q3_kv_append_paged")
+
+
+def _cp_check(q, K, V):
+    _check_cuda_bf16("q", q)
+    _check_cuda_bf16("K", K)
+    _check_cuda_bf16("V", V)
+    B = q.shape[0]
+    q2 = q.reshape(B, NH * HD)
+    _need(q2.stride(1) == 1, "q rows must be contiguous")
+    _need(K.dim() == 4 and K.shape[0] >= B and K.shape[1] == NKV and K.shape[3] == HD and K.stride(3) == 1
+          and V.shape == K.shape and V.stride(3) == 1, "K/V must be [B, 8, S, 128] with contiguous 128")
+    return q2
+
+
+@torch.library.custom_op("q3attn::cp_attn", mutates_args=())
+def cp_attn_op(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, n_live: int, softmax_scale: float) -> torch.Tensor:
+    lib = _lib.load()
+    q2 = _cp_check(q, K, V)
+    B = q2.shape[0]
+    out = torch.empty(B, NH * HD, dtype=torch.bfloat16, device=q.device)
+    with torch.cuda.device(q.device):
+        rc = lib.q3_cp_attn(q2.data_ptr(), q2.stride(0), K.data_ptr(), V.data_ptr(), K.stride(0), K.stride(1),
+                            K.stride(2), V.stride(0), V.stride(1), V.stride(2), B, K.shape[2], int(n_live),
+                            float(softmax_scale), out.data_ptr(), out.stride(0), _stream(q.device))
+    _lib.check(rc, "q3_cp_attn")
+    return out
+
+
+@cp_attn_op.register_fake
+def _(q, K, V, n_live, softmax_scale):
+    return q.new_empty(q.shape[0], NH * HD)
+
+
+@torch.library.custom_op("q3attn::cp_step", mutates_args=("K", "V"))
+def cp_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, K: torch.Tensor, V: torch.Tensor, slot: int,
+            softmax_scale: float) -> torch.Tensor:
+    """K[:, :, slot] = k; V[:, :, slot] = v; attention over slots 0..slot -> [B, 2048] (one launch)."""
+    lib = _lib.load()
+    q2 = _cp_check(q, K, V)
+    B = q2.shape[0]
+    k3, v3 = _rows("k", k), _rows("v", v)
+    _need(k3.shape[0] == B and v3.shape == k3.shape and v3.stride(0) == k3.stride(0), "k/v must be [B, 8, 128]")
+    out = torch.empty(B, NH * HD, dtype=torch.bfloat16, device=q.device)
+    with torch.cuda.device(q.device):
+        rc = lib.q3_cp_step(q2.data_ptr(), q2.stride(0), k3.data_ptr(), v3.data_ptr(), k3.stride(0), K.data_ptr(),
+                            V.data_ptr(), K.stride(0), K.stride(1), K.stride(2), V.stride(0), V.stride(1), V.stride(2),
+                            B, K.shape[2], int(slot), float(softmax_scale), out.data_ptr(), out.stride(0),
+                            _stream(q.device))
+    _lib.check(rc, "q3_cp_step")
+    return out
+
+
+@cp_step.register_fake
+def _(q, k, v, K, V, slot, softmax_scale):
+    return q.new_empty(q.shape[0], NH * HD)
+
+
+def set_decode_variant(variant: int) -> int:
+    """Select the decode kernel variant (0: 16-token chunks x 3 stages; 1: 8-token x 3, two CTAs/SM; 2: 16 x 2)."""
+    _ws.clear()
+    return int(_lib.load().q3_set_decode_variant(int(variant)))

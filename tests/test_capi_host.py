@@ -1,0 +1,106 @@
+"""CPU: the C-ABI library loads, exports every symbol include/q3attn.h declares, and rejects bad arguments on the host
+(no kernel is launched: every case below fails its argument check before any CUDA call)."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from q3attn import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    src = open(os.path.join(REPO, "include", "q3attn.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(q3_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = header_functions()
+    assert len(names) >= 11
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/q3attn.h but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature in q3attn._lib"
+
+
+def test_version_and_error_strings():
+    lib = _lib.load()
+    assert lib.q3_version() >= 100
+    for code in range(6):
+        assert lib.q3_error_string(code)
+    assert b"unsupported" in lib.q3_error_string(_lib.Q3_ERR_UNSUPPORTED)
+
+
+def test_decode_rejects_unsupported_family_before_cuda():
+    lib = _lib.load()
+    rc = lib.q3_paged_decode(1, 4096, None, None, 0, 1, 1, 10, 16, 1, 1, 4, 4, 4, 32, 8, 128, 0.1, 1, 4096, 1, 1 << 20,
+                             0, None)
+    assert rc == _lib.Q3_ERR_UNSUPPORTED
+    rc = lib.q3_paged_decode(1, 4096, None, None, 0, 1, 1, 10, 16, 1, 1, 4, 4, 4, 16, 8, 64, 0.1, 1, 4096, 1, 1 << 20,
+                             0, None)
+    assert rc == _lib.Q3_ERR_UNSUPPORTED
+
+
+def test_decode_rejects_invalid_sizes_before_cuda():
+    lib = _lib.load()
+    # negative batch, zero pages, zero page size, k without v
+    assert lib.q3_paged_decode(1, 2048, None, None, 0, 1, 1, 10, 16, 1, 1, 4, 4, -1, 16, 8, 128, 0.1, 1, 2048, 1, 1,
+                               0, None) == _lib.Q3_ERR_INVALID
+    assert lib.q3_paged_decode(1, 2048, None, None, 0, 1, 1, 0, 16, 1, 1, 4, 4, 2, 16, 8, 128, 0.1, 1, 2048, 1, 1, 0,
+                               None) == _lib.Q3_ERR_INVALID
+    assert lib.q3_paged_decode(1, 2048, 16, None, 1024, 1, 1, 10, 16, 1, 1, 4, 4, 2, 16, 8, 128, 0.1, 1, 2048, 1, 1,
+                               0, None) == _lib.Q3_ERR_INVALID
+    # block-table stride shorter than the pages it claims
+    assert lib.q3_paged_decode(1, 2048, None, None, 0, 1, 1, 10, 16, 1, 1, 2, 4, 2, 16, 8, 128, 0.1, 1, 2048, 1, 1,
+                               0, None) == _lib.Q3_ERR_INVALID
+    # batch 0 is a no-op
+    assert lib.q3_paged_decode(None, 2048, None, None, 0, None, None, 10, 16, None, None, 4, 4, 0, 16, 8, 128, 0.1,
+                               None, 2048, None, 0, 0, None) == _lib.Q3_OK
+
+
+def test_decode_rejects_misaligned_pools_before_cuda():
+    lib = _lib.load()
+    assert lib.q3_paged_decode(16, 2048, None, None, 0, 24, 32, 10, 16, 64, 64, 4, 4, 2, 16, 8, 128, 0.1, 16, 2048, 256,
+                               1 << 20, 0, None) == _lib.Q3_ERR_ALIGNMENT
+
+
+def test_cp_rejects_bad_slot_counts_before_cuda():
+    lib = _lib.load()
+    args = (16, 2048, 16, 16, 16384, 2048, 128, 16384, 2048, 128)
+    assert lib.q3_cp_attn(*args, 4, 16, 0, 0.1, 16, 2048, None) == _lib.Q3_ERR_INVALID      # n_live 0
+    assert lib.q3_cp_attn(*args, 4, 16, 17, 0.1, 16, 2048, None) == _lib.Q3_ERR_INVALID     # n_live > slots
+    assert lib.q3_cp_attn(*args, 4, 32, 17, 0.1, 16, 2048, None) == _lib.Q3_ERR_UNSUPPORTED  # > 16 slots attended
+    assert lib.q3_cp_attn(*args, 0, 16, 3, 0.1, 16, 2048, None) == _lib.Q3_OK               # empty batch
+
+
+def test_append_rejects_bad_arguments_before_cuda():
+    lib = _lib.load()
+    assert lib.q3_kv_append_slots(16, 16, 1024, 16, 16, 0, 8, 128, 16, 4, None) == _lib.Q3_ERR_INVALID   # no pool
+    assert lib.q3_kv_append_slots(16, 16, 1000, 16, 16, 64, 8, 128, 16, 4, None) == _lib.Q3_ERR_INVALID  # stride < row
+    assert lib.q3_kv_append_slots(24, 16, 1024, 16, 16, 64, 8, 128, 16, 4, None) == _lib.Q3_ERR_ALIGNMENT
+    assert lib.q3_kv_append_paged(16, 16, 1024, 16, 16, 4, 16, 8, 128, 16, None, 16, 2, 4, 3, None) == \
+        _lib.Q3_ERR_INVALID                                                                             # bt stride < pages
+
+
+def test_ops_refuse_cpu_tensors():
+    import q3attn
+    q = torch.zeros(2, 16, 128, dtype=torch.bfloat16)
+    kc = torch.zeros(4, 16, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        q3attn.paged_decode(q, kc, kc, torch.ones(2, dtype=torch.int32), torch.zeros(2, 2, dtype=torch.int32), 0.1, 0)
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        q3attn.cp_attn(q, torch.zeros(2, 8, 16, 128, dtype=torch.bfloat16), torch.zeros(2, 8, 16, 128,
+                                                                                          dtype=torch.bfloat16), 3, 0.1)
+
+
+def test_flash_api_refuses_unimplemented_options():
+    import q3attn
+    q = torch.zeros(2, 1, 16, 128, dtype=torch.bfloat16)
+    with pytest.raises(NotImplementedError):
+        q3attn.flash_attn_with_kvcache(q, q, q, cache_seqlens=1, window_size=(4, 0))
+    with pytest.raises(NotImplementedError):
+        q3attn.flash_attn_with_kvcache(q, q, q, cache_seqlens=1, return_softmax_lse=True)
