@@ -64,19 +64,36 @@ long long decode_grid(int dev, int32_t batch, int32_t num_splits, int32_t max_pa
   return G < 1 ? 1 : G;
 }
 
+// Decode workspace layout. The ticket counters (8 per seat) live in a front region whose size depends only on the
+// workspace's byte count, never on the batch or the grid of a call, so partials written by one launch can never land
+// where a later launch (any batch, any split count) keeps its counters. The counters are zero between launches.
+constexpr size_t kSeatTicketBytes = q3::kKvHeads * sizeof(uint32_t);                                // 32
+constexpr size_t kSlotMlBytes = q3::kKvHeads * q3::kGroup * 2 * sizeof(float);                      // 128
+constexpr size_t kSlotOBytes = q3::kKvHeads * q3::kGroup * q3::kHeadDim * sizeof(float);            // 8192
+
+size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
 struct WsLayout {
-  size_t counters, ml, o, total;
+  size_t counters, ml, o, end;
+  bool fits;
 };
 
-WsLayout ws_layout(int32_t batch, long long G) {
-  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+WsLayout ws_layout(size_t bytes, int32_t batch, long long G) {
   WsLayout w;
   const size_t slots = static_cast<size_t>(G) + static_cast<size_t>(batch);
   w.counters = 0;
-  w.ml = up(static_cast<size_t>(batch) * q3::kKvHeads * sizeof(uint32_t));
-  w.o = w.ml + up(slots * q3::kKvHeads * q3::kGroup * 2 * sizeof(float));
-  w.total = w.o + up(slots * q3::kKvHeads * q3::kGroup * q3::kHeadDim * sizeof(float));
+  w.ml = up256(kSeatTicketBytes * (bytes / (kSlotMlBytes + kSlotOBytes + kSeatTicketBytes)));
+  w.o = w.ml + up256(slots * kSlotMlBytes);
+  w.end = w.o + slots * kSlotOBytes;
+  w.fits = kSeatTicketBytes * static_cast<size_t>(batch) <= w.ml && w.end <= bytes;
   return w;
+}
+
+size_t ws_bytes_needed(int32_t batch, long long G) {
+  const size_t slots = static_cast<size_t>(G) + static_cast<size_t>(batch);
+  size_t bytes = up256(slots * kSlotMlBytes) + slots * kSlotOBytes + kSeatTicketBytes * slots + 1024;
+  while (!ws_layout(bytes, batch, G).fits) bytes += 4096;
+  return bytes;
 }
 
 }  // namespace
@@ -132,7 +149,7 @@ size_t q3_paged_decode_workspace_bytes(int32_t batch, int32_t num_splits) {
   if (batch < 0 || current_device(&dev) != Q3_OK) return 0;
   // Upper bound over all block-table shapes: the grid is at most SMs x CTAs/SM (or num_splits).
   const long long G = decode_grid(dev, batch, num_splits, 0, 0);
-  return ws_layout(batch, G).total;
+  return ws_bytes_needed(batch, G);
 }
 
 int q3_paged_decode(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
@@ -161,8 +178,8 @@ int q3_paged_decode(const void* q, int64_t q_batch_stride, const void* k_new, co
   if ((rc = current_device(&dev)) != Q3_OK) return rc;
   const long long G = decode_grid(dev, batch, num_splits, max_pages_per_seat, page_size);
   if (G > (1ll << 30)) return Q3_ERR_INVALID;
-  const WsLayout w = ws_layout(batch, G);
-  if (!workspace || workspace_bytes < w.total || !aligned(workspace, 256)) return Q3_ERR_WORKSPACE;
+  const WsLayout w = ws_layout(workspace_bytes, batch, G);
+  if (!workspace || !w.fits || !aligned(workspace, 256)) return Q3_ERR_WORKSPACE;
   uint32_t* st = nullptr;
   if ((rc = status_ptr(dev, &st)) != Q3_OK) return rc;
 

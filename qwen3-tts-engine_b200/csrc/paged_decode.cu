@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(kDecodeThreads, MIN_CTAS) paged_decode_kernel(
   volatile int* abort_flag = reinterpret_cast<int*>(smem + SL::kMiscOff);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int G = gridDim.x, c = blockIdx.x;
+  const int G = gridDim.x, c = blockIdx.x;   // G: launched CTAs (the split is re-derived below from N)
   const bool append = a.k_new != nullptr;
 
   if (tid == 0) {
@@ -126,8 +126,11 @@ __global__ void __launch_bounds__(kDecodeThreads, MIN_CTAS) paged_decode_kernel(
   long long N = 0;
 #pragma unroll
   for (int w = 0; w <= kConsumerWarps; ++w) N += warp_sums[w];
-  const long long c0 = (N * c) / G, c1 = (N * (c + 1)) / G;
-  if (c0 >= c1) return;   // no work (uniform across the CTA; no barrier has been armed)
+  // Effective CTA count: never more CTAs than chunks, so every CTA in [0, Ge) owns at least one chunk and the
+  // CTAs between a seat's first and last owner all contribute a partial (the merge counts them).
+  const int Ge = static_cast<int>(N < G ? N : G);
+  if (c >= Ge) return;    // uniform across the CTA; no barrier has been armed
+  const long long c0 = (N * c) / Ge, c1 = (N * (c + 1)) / Ge;
 
   __shared__ long long plan_first;
   __shared__ int plan_seat;
@@ -316,8 +319,8 @@ __global__ void __launch_bounds__(kDecodeThreads, MIN_CTAS) paged_decode_kernel(
       for (int o = 8; o > 0; o >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, o);
       const float l0 = __shfl_sync(0xffffffffu, lg, 0);
       const float l1 = __shfl_sync(0xffffffffu, lg, 16);
-      const int c_first = cta_of_chunk(cur.first, N, G);
-      const int c_last = cta_of_chunk(cur.first + cur.nch - 1, N, G);
+      const int c_first = cta_of_chunk(cur.first, N, Ge);
+      const int c_last = cta_of_chunk(cur.first + cur.nch - 1, N, Ge);
       __nv_bfloat16* op = a.out + static_cast<long long>(cur.seat) * a.out_stride + (2 * h) * kHeadDim + 4 * lane;
       if (c_first == c_last) {
         const float r0 = 1.f / l0, r1 = 1.f / l1;

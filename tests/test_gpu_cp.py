@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import assert_close_attn, bits_equal
+from helpers import assert_close_attn, bits_equal, poison_allocator
 from oracle import attention as OA
 from q3attn import synth
 
@@ -25,6 +25,7 @@ def q3():
 def test_cp_attn_matches_oracle(q3, n_live):
     d = synth.cp_case(n_live, 64)
     dd = {k: v.to(DEV) for k, v in d.items()}
+    poison_allocator((64, 2048))
     out = q3.cp_attn(dd["q"], dd["K"], dd["V"], n_live, SCALE)
     torch.cuda.synchronize()
     ref = OA.cp_attention(d["q"], d["K"], d["V"], n_live, SCALE)
@@ -47,6 +48,7 @@ def test_cp_step_fused_append(q3, p):
     rK, rV = Kall[l, :B].clone(), Vall[l, :B].clone()
     ref = OA.cp_step(q, k, v, rK, rV, p, SCALE)
     gK, gV = Kall.to(DEV), Vall.to(DEV)
+    poison_allocator((B, 2048))
     out = q3.cp_step(q.to(DEV), k.to(DEV), v.to(DEV), gK[l, :B], gV[l, :B], p, SCALE)
     torch.cuda.synchronize()
     assert_close_attn(out, ref, what=f"cp_step p {p}")

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import assert_close_attn, bits_equal
+from helpers import assert_close_attn, bits_equal, poison_allocator
 from oracle import attention as OA
 from q3attn import synth
 
@@ -37,6 +37,7 @@ def _run_decode(q3, lay, d, append, num_splits=0):
     dd = _to(d)
     seq = lay.ctx.to(DEV)
     bt = lay.block_table.to(DEV)
+    poison_allocator((lay.B, 16, 128))
     if append:
         out = q3.paged_decode_append(dd["q"], dd["k_new"], dd["v_new"], dd["k_pool"], dd["v_pool"], seq, bt, SCALE, num_splits)
     else:
@@ -131,9 +132,11 @@ def test_decode_c2_full_size_subset(q3):
     kn = synth.randn((B, 8, 128), g, 0.5, torch.bfloat16, DEV)
     vn = synth.randn((B, 8, 128), g, 0.5, torch.bfloat16, DEV)
     seq, bt = lay.ctx.to(DEV), lay.block_table.to(DEV)
+    poison_allocator((B, 16, 128))
     out = q3.paged_decode_append(q, kn, vn, kp, vp, seq, bt, SCALE, 0)
     torch.cuda.synchronize()
     assert q3._lib.read_status() == 0
+    assert torch.isfinite(out.float()).all(), "some seat's output was never written"
     pick = torch.linspace(0, B - 1, 24).long()
     for b in pick.tolist():
         n = int(lay.ctx[b]) + 1
@@ -144,6 +147,18 @@ def test_decode_c2_full_size_subset(q3):
         a = torch.matmul(q[b].float().cpu().view(8, 2, 128), K.transpose(0, 1).transpose(-1, -2)) * SCALE
         ref = torch.matmul(torch.softmax(a, -1), V.transpose(0, 1)).reshape(16, 128)
         assert_close_attn(out[b], ref, what=f"c2 seat {b}")
+
+
+def test_workspace_reuse_across_batches_and_splits(q3):
+    """One workspace serves launches of any batch and split count in any order: a launch that leaves partials behind
+    (many splits, small batch) must not disturb the ticket counters of a later, larger launch."""
+    seqs = [(3, 1000), (40, 0), (5, 300), (64, 0), (2, 7), (64, 148)]
+    for i, (B, splits) in enumerate(seqs):
+        lay = synth.paged_layout(60 + i, B=B, ctx_lo=1, ctx_hi=600, page=16, pages_per_seat=40)
+        d = synth.decode_case(60 + i, lay, scale=0.5)
+        out, _ = _run_decode(q3, lay, d, append=False, num_splits=splits)
+        ref, _, _ = _oracle(lay, d, append=False)
+        assert_close_attn(out, ref, what=f"launch {i} (B {B}, splits {splits})")
 
 
 def test_kv_append_slots_bit_exact(q3):
@@ -204,6 +219,7 @@ def test_flash_api_dropin_matches_oracle(q3):
     lay = synth.c1_layout(1)
     d = synth.decode_case(1, lay)
     dd = _to(d)
+    poison_allocator((4, 16, 128))
     out = q3.flash_attn_with_kvcache(dd["q"].unsqueeze(1), dd["k_pool"], dd["v_pool"], cache_seqlens=lay.ctx.to(DEV),
                                      block_table=lay.block_table.to(DEV), softmax_scale=SCALE, causal=True)
     ref, _, _ = _oracle(lay, d, append=False)
