@@ -314,7 +314,8 @@ def main():
             traffic = None
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "traffic": traffic, "peak_source": peak_kind, "bytes_per_launch": bytes_launch, "launch_us": launch_s * 1e6,
-            "kernel": "q3::paged_decode_kernel (fused append)"}
+            "kernel": "q3::paged_decode_kernel (fused append)",
+            "resident_ctas_per_sm": int(q3attn._lib.load().q3_paged_decode_resident_ctas(a.variant))}
 
     # ---------------- end to end through the public API with host buffers
     e2e = None

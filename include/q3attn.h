@@ -27,7 +27,7 @@ extern "C" {
 #define Q3_OK 0
 #define Q3_ERR_INVALID 1      /* null pointer, negative size, inconsistent strides */
 #define Q3_ERR_UNSUPPORTED 2  /* head counts / head_dim / slot count outside the compiled family */
-#define Q3_ERR_ALIGNMENT 3    /* a pointer or stride breaks the 16-byte (pools, rows) or 8-byte (q/out) rule */
+#define Q3_ERR_ALIGNMENT 3    /* a pointer or stride breaks the 16-byte (pools, new rows, decode q) or 8-byte rule */
 #define Q3_ERR_WORKSPACE 4    /* workspace missing or smaller than q3_paged_decode_workspace_bytes() */
 #define Q3_ERR_CUDA 5         /* a CUDA runtime call failed; see q3_last_cuda_error() */
 
@@ -66,9 +66,12 @@ int q3_paged_decode(const void* q, int64_t q_batch_stride,
                     void* out, int64_t out_batch_stride,
                     void* workspace, size_t workspace_bytes, int32_t num_splits,
                     void* stream);
-/* Kernel variant used by q3_paged_decode: 0 = 16-token chunks x 3 stages (1 CTA/SM, default),
- * 1 = 8-token chunks x 3 stages (2 CTAs/SM), 2 = 16-token chunks x 2 stages. Returns the previous value. */
+/* Kernel variant used by q3_paged_decode: 0 = 8-token chunks x 3 stages, two CTAs per SM (default),
+ * 1 = 16-token chunks x 3 stages, one CTA per SM, 2 = 8-token chunks x 2 stages, two CTAs per SM.
+ * Returns the previous value. */
 int q3_set_decode_variant(int variant);
+/* CTAs of the given decode variant that the runtime can keep resident on one SM of the current device. */
+int q3_paged_decode_resident_ctas(int variant);
 
 /* ---------------------------------------------------------------- K/V append into pages
  * Replaces kc[l].view(-1, nkv, hd).index_copy_(0, slot, k) (and the same for V): engine/talker.py:72-73 and 161-162,

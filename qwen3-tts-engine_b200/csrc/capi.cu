@@ -144,6 +144,8 @@ int q3_set_decode_variant(int variant) {
   return prev;
 }
 
+int q3_paged_decode_resident_ctas(int variant) { return q3::decode_occupancy(variant); }
+
 size_t q3_paged_decode_workspace_bytes(int32_t batch, int32_t num_splits) {
   int dev = 0;
   if (batch < 0 || current_device(&dev) != Q3_OK) return 0;
@@ -168,7 +170,7 @@ int q3_paged_decode(const void* q, int64_t q_batch_stride, const void* k_new, co
       out_batch_stride < q3::kQHeads * q3::kHeadDim)
     return Q3_ERR_INVALID;
   if (static_cast<long long>(max_pages_per_seat) * page_size > (1ll << 30)) return Q3_ERR_INVALID;
-  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 8) || !aligned(out, 8) || (q_batch_stride % 4) ||
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(q, 16) || !aligned(out, 8) || (q_batch_stride % 8) ||
       (out_batch_stride % 4))
     return Q3_ERR_ALIGNMENT;
   if (k_new && (!aligned(k_new, 16) || !aligned(v_new, 16) || (kv_new_batch_stride % 8) ||

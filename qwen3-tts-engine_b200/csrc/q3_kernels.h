@@ -33,6 +33,7 @@ struct DecodeArgs {
 
 int decode_rows_per_chunk(int variant);
 int decode_ctas_per_sm(int variant);
+int decode_occupancy(int variant);   // resident CTAs per SM measured by the runtime (-1 on error)
 cudaError_t launch_paged_decode(const DecodeArgs& a, int grid, int variant, cudaStream_t stream);
 
 struct AppendArgs {

@@ -226,6 +226,7 @@ def _(q, k, v, K, V, slot, softmax_scale):
 
 
 def set_decode_variant(variant: int) -> int:
-    """Select the decode kernel variant (0: 16-token chunks x 3 stages; 1: 8-token x 3, two CTAs/SM; 2: 16 x 2)."""
+    """Select the decode kernel variant (0: 8-token chunks x 3 stages, two CTAs/SM; 1: 16-token x 3, one CTA/SM;
+    2: 8-token x 2, two CTAs/SM)."""
     _ws.clear()
     return int(_lib.load().q3_set_decode_variant(int(variant)))
