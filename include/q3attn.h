@@ -30,6 +30,7 @@ extern "C" {
 #define Q3_ERR_ALIGNMENT 3    /* a pointer or stride breaks the 16-byte (pools, new rows, decode q) or 8-byte rule */
 #define Q3_ERR_WORKSPACE 4    /* workspace missing or smaller than q3_paged_decode_workspace_bytes() */
 #define Q3_ERR_CUDA 5         /* a CUDA runtime call failed; see q3_last_cuda_error() */
+#define Q3_ERR_SCRATCH_LIMIT 6  /* q3_paged_decode_noalloc: batch / split count beyond its fixed 16 MiB scratch */
 
 /* Status bits a kernel may set on the device (read with q3_read_status). */
 #define Q3_STATUS_WAIT_TIMEOUT 1u  /* a pipeline wait gave up (kernel returned early; outputs invalid) */
@@ -72,6 +73,23 @@ int q3_paged_decode(const void* q, int64_t q_batch_stride,
 int q3_set_decode_variant(int variant);
 /* CTAs of the given decode variant that the runtime can keep resident on one SM of the current device. */
 int q3_paged_decode_resident_ctas(int variant);
+
+/* Same as q3_paged_decode, for callers that cannot allocate device memory (no workspace argument). No counterpart in
+ * the reference: it exists for hosts whose device memory comes from an arena they do not own, or whose calls must not
+ * allocate. The split-K scratch lives in a 16 MiB array compiled into the library, held by every GPU that loads it
+ * until exit; calls whose workspace would exceed it (roughly batch + CTAs > 2000) return Q3_ERR_SCRATCH_LIMIT before
+ * launching anything. The first call on a device looks up the array's device address (do it before any stream
+ * capture). Every call clears the counters it uses on its stream; calls that overlap on the GPU share the array and
+ * race. */
+int q3_paged_decode_noalloc(const void* q, int64_t q_batch_stride,
+                            const void* k_new, const void* v_new, int64_t kv_new_batch_stride,
+                            void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,
+                            const int32_t* cache_seqlens,
+                            const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
+                            int32_t batch, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                            float softmax_scale,
+                            void* out, int64_t out_batch_stride, int32_t num_splits,
+                            void* stream);
 
 /* ---------------------------------------------------------------- K/V append into pages
  * Replaces kc[l].view(-1, nkv, hd).index_copy_(0, slot, k) (and the same for V): engine/talker.py:72-73 and 161-162,

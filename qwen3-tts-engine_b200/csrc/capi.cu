@@ -110,6 +110,7 @@ const char* q3_error_string(int code) {
     case Q3_ERR_ALIGNMENT: return "misaligned pointer or stride";
     case Q3_ERR_WORKSPACE: return "workspace missing or too small";
     case Q3_ERR_CUDA: return "CUDA runtime error";
+    case Q3_ERR_SCRATCH_LIMIT: return "batch or split count beyond the fixed scratch of q3_paged_decode_noalloc";
     default: return "unknown error";
   }
 }

@@ -8,7 +8,7 @@ import os
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libq3attn.so")
 
-Q3_OK, Q3_ERR_INVALID, Q3_ERR_UNSUPPORTED, Q3_ERR_ALIGNMENT, Q3_ERR_WORKSPACE, Q3_ERR_CUDA = range(6)
+Q3_OK, Q3_ERR_INVALID, Q3_ERR_UNSUPPORTED, Q3_ERR_ALIGNMENT, Q3_ERR_WORKSPACE, Q3_ERR_CUDA, Q3_ERR_SCRATCH_LIMIT = range(7)
 STATUS_WAIT_TIMEOUT, STATUS_BAD_PAGE, STATUS_BAD_LENGTH = 1, 2, 4
 
 _P, _I32, _I64, _F32, _SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
@@ -23,6 +23,8 @@ SIGNATURES = {
     "q3_paged_decode_workspace_bytes": (_SZ, [_I32, _I32]),
     "q3_paged_decode": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P, _I32, _I32, _P, _P, _I64, _I32,
                                        _I32, _I32, _I32, _I32, _F32, _P, _I64, _P, _SZ, _I32, _P]),
+    "q3_paged_decode_noalloc": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P, _I32, _I32, _P, _P, _I64, _I32,
+                                               _I32, _I32, _I32, _I32, _F32, _P, _I64, _I32, _P]),
     "q3_set_decode_variant": (ctypes.c_int, [ctypes.c_int]),
     "q3_paged_decode_resident_ctas": (ctypes.c_int, [ctypes.c_int]),
     "q3_kv_append_slots": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _I32, _I32, _P, _I32, _P]),
