@@ -149,6 +149,26 @@ def test_decode_c2_full_size_subset(q3):
         assert_close_attn(out[b], ref, what=f"c2 seat {b}")
 
 
+@pytest.mark.parametrize("variant", [0, 1, 2])
+def test_decode_every_kernel_variant(q3, variant):
+    """Every decode kernel variant (8/16-token chunks, 2/3 stages) against the oracle on edge lengths with 16-token
+    pages, a 1-token page layout and 256-token pages, with and without the fused append."""
+    prev = q3.set_decode_variant(variant)
+    try:
+        for page, append in ((16, True), (16, False), (1, True), (256, False)):
+            pps = (512 + page - 1) // page
+            ctx = [c - 1 if append else c for c in EDGE_CTX] + ([pps * page - 1] if append else [pps * page])
+            lay = _layout(len(ctx), ctx, page, pps, num_pages=len(ctx) * pps + 3, seed=7 + page)
+            d = synth.decode_case(200 + page, lay, scale=0.5)
+            out, dd = _run_decode(q3, lay, d, append, num_splits=37)
+            ref, kp, vp = _oracle(lay, d, append)
+            assert_close_attn(out, ref, what=f"variant {variant} page {page} append {append}")
+            if append:
+                assert bits_equal(dd["k_pool"], kp) and bits_equal(dd["v_pool"], vp)
+    finally:
+        q3.set_decode_variant(prev)
+
+
 def test_workspace_reuse_across_batches_and_splits(q3):
     """One workspace serves launches of any batch and split count in any order: a launch that leaves partials behind
     (many splits, small batch) must not disturb the ticket counters of a later, larger launch."""
