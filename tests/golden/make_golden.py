@@ -189,17 +189,26 @@ def gen_frames(talker, code_predictor):
         T = ref_talker(talker, code_predictor, W, n_seats, seat_len, bucket, st)
         live = st["live"]
         T.s_seat[:n_live] = live
-        codes, hx = [], []
+        codes, hs = [], []
+        dec = T._decode
+        T.decode = lambda *args: hs.append(dec(*args)) or hs[-1]   # record the talker hidden of each frame
         with torch.inference_mode():
             for f in range(frames):
                 T.pos[n_seats] = 0
                 T._frame(bucket)
                 codes.append(T.o_codes[:n_live].clone())
+            # continuous values of frame 1 for the live rows: talker hidden, raw codebook-0 logits, and the 15 CP logits
+            # teacher-forced on the frame's own codes (CodePredictor.tf_logits, engine/code_predictor.py:74-82)
+            h1 = hs[0][:n_live].clone()
+            lg1 = torch.nn.functional.linear(h1, W.codec_head).float()
+            cp1 = T.cp.tf_logits(h1, codes[0])
         # the rows the first frame appended (placement pin): K of layer 0 at each live seat's first new position
         slot0 = live * seat_len + st["ctx"][live]
         krow0 = T.kc[0].view(-1, 8, 128)[slot0]
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), codes=torch.stack(codes).numpy(), live=live.numpy(),
                             x_in=T.x_in[live].numpy(), pos=T.pos.numpy(), ngen=T.ngen.numpy(), krow0=krow0.numpy(),
+                            h1=h1.numpy(), c0_logits1=lg1.numpy().astype(np.float16),
+                            cp_tf_logits1=cp1.numpy().astype(np.float16),
                             digest=np.array(digest(st["kv"][:, :, :, :8], st["x_in"], W.layers[0].qkv, W.cp_head[3])))
         print(f"[golden] {name}: codes {tuple(torch.stack(codes).shape)}", flush=True)
 
@@ -207,8 +216,13 @@ def gen_frames(talker, code_predictor):
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     talker, arrivals, code_predictor = ref_modules()
-    gen_decode(talker)
-    gen_prefill(arrivals)
-    gen_cp(code_predictor)
-    gen_frames(talker, code_predictor)
+    only = sys.argv[1:]
+    if not only or "decode" in only:
+        gen_decode(talker)
+    if not only or "prefill" in only:
+        gen_prefill(arrivals)
+    if not only or "cp" in only:
+        gen_cp(code_predictor)
+    if not only or "frames" in only:
+        gen_frames(talker, code_predictor)
     print("[golden] done", flush=True)
