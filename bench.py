@@ -70,6 +70,15 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def reduce_max(x, pg, device):
+    """Max of a per-rank timing over all ranks (pg = torch.distributed, or None for one process)."""
+    if pg is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
 def layout_for_rank(seed, rank, seats):
     """Rank r's seats: ctx U[200,1200] and a shuffled local page table (rank 0 == the config-2 layout)."""
     from q3attn import synth
@@ -271,11 +280,7 @@ def main():
         torch.cuda.synchronize()
 
     def max_over_ranks(x):
-        if pg is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_max(x, pg, dev)
 
     # ---------------- device-resident timing
     for _ in range(a.warmup):
