@@ -109,6 +109,23 @@ int q3_kv_append_paged(const void* k, const void* v, int64_t row_stride,
                        const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
                        int32_t n_rows, void* stream);
 
+/* ---------------------------------------------------------------- prefill attention (tcgen05 tensor cores)
+ * Replaces flash_attn_varlen_func(q, k, v, cu, cu, max, max, softmax_scale, causal=True) (engine/talker.py:169) and
+ * flash_attn_func(q, K, V, softmax_scale, causal=True) over a cached prefix (engine/arrivals.py:148), and fuses the
+ * page writes of engine/talker.py:161-162 / engine/arrivals.py:144-145 when write_kv is set.
+ * Sequence i: query rows [cu_seqlens_q[i], cu_seqlens_q[i+1]) (R_i), new key rows [cu_seqlens_k[i], cu_seqlens_k[i+1])
+ * (N_i >= R_i) of k/v [Tk, 8, 128], and prefix_lens[i] keys already in the pages of block-table row seat_ids[i]
+ * (prefix_lens NULL: none; seat_ids NULL: row i). Keys are indexed prefix first; with causal, query j sees keys
+ * 0 .. prefix + N - R + j (bottom-right alignment). write_kv: the new rows also go to positions prefix + r of the
+ * seat's pages. max_seqlen_q must be >= every R_i. Output rows [Tq, 16, 128] bf16. */
+int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v, int64_t kv_row_stride,
+               const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t num_seqs, int32_t max_seqlen_q,
+               const int32_t* prefix_lens, const int32_t* seat_ids,
+               void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,
+               const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
+               int32_t write_kv, int32_t causal, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+               float softmax_scale, void* out, int64_t out_row_stride, void* stream);
+
 /* ---------------------------------------------------------------- code-predictor attention
  * Replaces cp_attn(q, K, V, n_live, scale) (engine/cp_attn.py:33-39), i.e. the attention expression of
  * CodePredictor._post (engine/code_predictor.py:46-47): q [B,16,128] over slots 0..n_live-1 of K/V [B,8,S,128];

@@ -313,4 +313,58 @@ int q3_cp_step(const void* q, int64_t q_batch_stride, const void* k_new, const v
                    v_head_stride, v_slot_stride, batch, n_slots, slot + 1, softmax_scale, out, out_batch_stride, stream);
 }
 
+int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v, int64_t kv_row_stride,
+               const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t num_seqs, int32_t max_seqlen_q,
+               const int32_t* prefix_lens, const int32_t* seat_ids, void* k_pool, void* v_pool, int32_t num_pages,
+               int32_t page_size, const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
+               int32_t write_kv, int32_t causal, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+               float softmax_scale, void* out, int64_t out_row_stride, void* stream) {
+  int rc = check_family(num_heads, num_kv_heads, head_dim);
+  if (rc != Q3_OK) return rc;
+  if (num_seqs < 0 || max_seqlen_q < 0) return Q3_ERR_INVALID;
+  if (num_seqs == 0) return Q3_OK;
+  if (!q || !k || !v || !cu_seqlens_q || !cu_seqlens_k || !out) return Q3_ERR_INVALID;
+  if (q_row_stride < q3::kQHeads * q3::kHeadDim || out_row_stride < q3::kQHeads * q3::kHeadDim ||
+      kv_row_stride < q3::kKvHeads * q3::kHeadDim)
+    return Q3_ERR_INVALID;
+  const bool paged = (prefix_lens != nullptr) || write_kv;
+  if (paged && (!k_pool || !v_pool || !block_table || num_pages <= 0 || page_size <= 0 || max_pages_per_seat <= 0 ||
+                block_table_stride < max_pages_per_seat))
+    return Q3_ERR_INVALID;
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16) || (q_row_stride % 8) ||
+      (kv_row_stride % 8) || (out_row_stride % 8) || (paged && (!aligned(k_pool, 16) || !aligned(v_pool, 16))))
+    return Q3_ERR_ALIGNMENT;
+  if (static_cast<long long>(max_seqlen_q + 63) / 64 > 65535 || num_seqs > 65535) return Q3_ERR_INVALID;
+  int dev = 0;
+  if ((rc = current_device(&dev)) != Q3_OK) return rc;
+  uint32_t* st = nullptr;
+  if ((rc = status_ptr(dev, &st)) != Q3_OK) return rc;
+  q3::PrefillArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_stride = q_row_stride;
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.kv_stride = kv_row_stride;
+  a.cu_q = cu_seqlens_q;
+  a.cu_k = cu_seqlens_k;
+  a.num_seqs = num_seqs;
+  a.max_seqlen_q = max_seqlen_q;
+  a.prefix_lens = prefix_lens;
+  a.seat_ids = seat_ids;
+  a.k_pool = static_cast<__nv_bfloat16*>(k_pool);
+  a.v_pool = static_cast<__nv_bfloat16*>(v_pool);
+  a.num_pages = num_pages;
+  a.page_size = page_size;
+  a.block_table = block_table;
+  a.bt_stride = block_table_stride;
+  a.max_pages = max_pages_per_seat;
+  a.write_kv = write_kv ? 1 : 0;
+  a.causal = causal ? 1 : 0;
+  a.scale_log2 = softmax_scale * q3::kLog2e;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_stride = out_row_stride;
+  a.status = st;
+  return record(q3::launch_prefill(a, static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

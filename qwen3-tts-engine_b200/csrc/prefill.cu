@@ -1,0 +1,389 @@
+// Prompt prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+// Replaces the prefill attention calls of the engine:
+//   flash_attn_varlen_func(q, k, v, cu, cu, max, max, softmax_scale, causal=True)   engine/talker.py:169
+//   flash_attn_func(q [S,R,16,128], K [S,k+R,8,128], V, softmax_scale, causal=True)  engine/arrivals.py:148
+// and a chunked prefill whose cached prefix lives in the paged K/V pool, with the new rows written into the pages
+// (the index_copy_ page writes of engine/talker.py:161-162 and engine/arrivals.py:144-145 fused into the launch).
+//
+// Sequence i has R_i query rows, N_i new key rows (N_i >= R_i) and P_i cached prefix keys in its pages; its L_i =
+// P_i + N_i keys are indexed prefix first. Query j (0-based) sees keys 0 .. L_i - R_i + j (causal aligned to the bottom
+// right, flash-attention's convention; with P = 0 and N = R it is the plain causal prefill).
+//
+// One CTA = (64-position query tile, KV head h, sequence). Its 128 accumulator rows are the 64 positions of q head 2h
+// (rows 0-63) and of q head 2h+1 (rows 64-127): both heads share the K/V tiles. Per 64-key tile:
+//   S[128 x 64]  = Q[128 x 128] K^T        8 x tcgen05.mma kind::f16 (M128 N64 K16), fp32 accumulator in TMEM
+//   softmax                                 thread t owns TMEM lane t = accumulator row t (tcgen05.ld), no shuffles
+//   O[128 x 128] += P[128 x 64] V[64 x 128]  4 x tcgen05.mma (M128 N128 K16), V as an MN-major operand, O in TMEM
+// O is rescaled only when a row's running max grows by more than 2^8 (P then stays below 256, exact in fp32 sums and
+// representable in bf16); the final division uses the same maxima, so the result is the exact softmax. Operands sit in
+// shared memory in the canonical no-swizzle core-matrix layout (8 rows x 16 bytes per core matrix) described by the
+// UMMA shared-memory descriptors below. A single thread issues the MMAs; tcgen05.commit arrives on an mbarrier that
+// the other threads wait on (bounded waits).
+#include "q3_common.cuh"
+#include "q3_kernels.h"
+
+namespace q3 {
+
+constexpr int kPfThreads = 128;              // one warpgroup: thread t <-> TMEM lane t
+constexpr int kPfQRows = 64;                 // query positions per tile (x 2 q heads = 128 MMA rows)
+constexpr int kPfKeys = 64;                  // keys per tile
+constexpr int kPfTmemCols = 256;             // S (64 columns) + O (128 columns), rounded to a power of two
+constexpr uint32_t kPfSCol = 0, kPfOCol = 128;
+
+struct PfSmem {
+  static constexpr int kQ = 0;                               // 128 rows x 128 dims, K-major   32 KB
+  static constexpr int kK = kQ + 128 * 256;                  // 64 keys x 128 dims, K-major    16 KB
+  static constexpr int kV = kK + kPfKeys * 256;              // 128 dims x 64 keys, MN-major   16 KB
+  static constexpr int kP = kV + kPfKeys * 256;              // 128 rows x 64 keys, K-major    16 KB
+  static constexpr int kBar = kP + 128 * kPfKeys * 2;        // bar_s, bar_o
+  static constexpr int kTmemSlot = kBar + 16;
+  static constexpr int kBytes = kTmemSlot + 16;
+};
+
+// ---------------------------------------------------------------- UMMA descriptors
+// Shared-memory matrix descriptor, no swizzle: start address, leading and stride byte offsets (all >> 4), version 1.
+__device__ __forceinline__ uint64_t umma_smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3fff);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3fff) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3fff) << 32;
+  d |= static_cast<uint64_t>(1) << 46;                       // descriptor version for sm_100
+  return d;                                                  // base offset 0, lbo mode 0, layout type 0 (no swizzle)
+}
+
+// Instruction descriptor of kind::f16: bf16 A and B, fp32 D, M x N, A/B major-ness (0 = K-major, 1 = MN-major).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int a_mn_major, int b_mn_major) {
+  return (1u << 4)                                           // D format: f32
+         | (1u << 7)                                         // A format: bf16
+         | (1u << 10)                                        // B format: bf16
+         | (static_cast<uint32_t>(a_mn_major) << 15) | (static_cast<uint32_t>(b_mn_major) << 16)
+         | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      :
+      : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (warp w reads lanes 32w..32w+31).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+      :
+      : "r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])),
+        "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
+        "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
+        "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
+        "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
+        "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+// Shared-memory offsets of the canonical no-swizzle layouts (element = one bf16).
+//   K-major [rows][128 or 64 k]: core matrix (8 rows x 8 k) = 128 contiguous bytes; k-chunks 128 B apart (LBO),
+//   8-row groups `sbo` bytes apart (SBO).
+__device__ __forceinline__ uint32_t kmajor_off(int row, int kchunk, int sbo) {
+  return (row >> 3) * sbo + kchunk * 128 + (row & 7) * 16;
+}
+//   MN-major V [keys][128 dims] as the B operand (N = dims): core matrix (8 keys x 8 dims) = 128 bytes; key groups
+//   128 B apart (LBO), 8-dim groups 1024 B apart (SBO).
+__device__ __forceinline__ uint32_t v_off(int key, int dchunk) {
+  return dchunk * 1024 + (key >> 3) * 128 + (key & 7) * 16;
+}
+
+struct PfSeq {
+  int q0, R, k0, Nn, P, seat;
+};
+
+__device__ __forceinline__ PfSeq pf_seq(const PrefillArgs& a, int i) {
+  PfSeq s;
+  s.q0 = a.cu_q[i];
+  s.R = a.cu_q[i + 1] - s.q0;
+  s.k0 = a.cu_k[i];
+  s.Nn = a.cu_k[i + 1] - s.k0;
+  s.P = a.prefix_lens ? a.prefix_lens[i] : 0;
+  s.seat = a.seat_ids ? a.seat_ids[i] : i;
+  return s;
+}
+
+// Row of the paged pool holding token `tok` of `seat` (bounds-checked page id).
+__device__ __forceinline__ long long pf_pool_row(const PrefillArgs& a, int seat, int tok) {
+  const int pidx = tok / a.page_size;
+  int pg = (pidx < a.max_pages) ? a.block_table[static_cast<long long>(seat) * a.bt_stride + pidx] : -1;
+  if (pg < 0 || pg >= a.num_pages) {
+    atomicOr(a.status, kStatusBadPage);
+    pg = 0;
+  }
+  return static_cast<long long>(pg) * a.page_size + (tok - pidx * a.page_size);
+}
+
+// Address of head h of key `kk` (combined index: prefix first, then new rows) in K (which = 0) or V (which = 1).
+__device__ __forceinline__ const __nv_bfloat16* pf_key_ptr(const PrefillArgs& a, const PfSeq& s, int h, int kk, int which) {
+  if (kk < s.P) {
+    const long long row = pf_pool_row(a, s.seat, kk);
+    return (which ? a.v_pool : a.k_pool) + row * (kKvHeads * kHeadDim) + h * kHeadDim;
+  }
+  return (which ? a.v : a.k) + static_cast<long long>(s.k0 + kk - s.P) * a.kv_stride + h * kHeadDim;
+}
+
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int qt = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
+  const PfSeq s = pf_seq(a, seq);
+  const int ntq = s.R > 0 ? (s.R + kPfQRows - 1) / kPfQRows : 1;
+  if (qt >= ntq) return;                                     // uniform; nothing allocated yet
+
+  // ---- fused page write: head h of new rows r with r % ntq == qt go to positions P + r of the seat's pages
+  if (a.write_kv) {
+    for (int r = qt; r < s.Nn; r += ntq) {
+      const long long prow = pf_pool_row(a, s.seat, s.P + r);
+      const long long src = static_cast<long long>(s.k0 + r) * a.kv_stride + h * kHeadDim;
+      const long long dst = prow * (kKvHeads * kHeadDim) + h * kHeadDim;
+      if (tid < 16)
+        reinterpret_cast<uint4*>(a.k_pool + dst)[tid] = __ldg(reinterpret_cast<const uint4*>(a.k + src) + tid);
+      else if (tid < 32)
+        reinterpret_cast<uint4*>(a.v_pool + dst)[tid - 16] = __ldg(reinterpret_cast<const uint4*>(a.v + src) + tid - 16);
+    }
+  }
+  if (s.R == 0) return;
+
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + PfSmem::kBar);
+  uint64_t* bar_o = bar_s + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PfSmem::kTmemSlot);
+  const uint32_t sQ = smem_addr(smem + PfSmem::kQ), sK = smem_addr(smem + PfSmem::kK);
+  const uint32_t sV = smem_addr(smem + PfSmem::kV), sP = smem_addr(smem + PfSmem::kP);
+
+  if (warp == 0) {   // TMEM: 256 columns (at most two CTAs per SM fit by shared memory, so 512 columns suffice)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(kPfTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    fence_mbar_init();
+  }
+
+  // ---- Q tile: thread t loads accumulator row t = (q head 2h + t/64, position 64*qt + t%64)
+  const int row_g = tid >> 6, row_j = qt * kPfQRows + (tid & 63);
+  const bool row_valid = row_j < s.R;
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(a.q + static_cast<long long>(s.q0 + (row_valid ? row_j : 0)) * a.q_stride +
+                                                      (2 * h + row_g) * kHeadDim);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const uint4 w = row_valid ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(smem + PfSmem::kQ + kmajor_off(tid, c, 2048)) = w;
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem + kPfSCol, t_o = tmem + kPfOCol;
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;   // this warp's TMEM lanes
+
+  const int L = s.P + s.Nn;
+  const int shift = L - s.R;                                 // query j sees keys <= shift + j
+  const int last_row = min(s.R - 1, qt * kPfQRows + kPfQRows - 1);
+  const int key_end = a.causal ? min(L, shift + last_row + 1) : L;
+  const int ntk = key_end > 0 ? (key_end + kPfKeys - 1) / kPfKeys : 0;
+  const int my_limit = a.causal ? shift + row_j : L - 1;     // last visible key of this row
+
+  constexpr uint32_t kIdescQK = umma_idesc_bf16(128, kPfKeys, 0, 0);
+  constexpr uint32_t kIdescPV = umma_idesc_bf16(128, kHeadDim, 0, 1);
+  float m_run = -INFINITY, l_run = 0.f;
+  bool ok = true;
+  for (int kt = 0; kt < ntk && ok; ++kt) {
+    // ---- K and V tiles: thread t loads half (t/64) of key kt*64 + t%64
+    {
+      const int kk_local = tid & 63, half = tid >> 6, kk = kt * kPfKeys + kk_local;
+      const bool kv_ok = kk < L;
+      const uint4* ks = kv_ok ? reinterpret_cast<const uint4*>(pf_key_ptr(a, s, h, kk, 0)) + half * 8 : nullptr;
+      const uint4* vs = kv_ok ? reinterpret_cast<const uint4*>(pf_key_ptr(a, s, h, kk, 1)) + half * 8 : nullptr;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 kw = kv_ok ? __ldg(ks + c) : make_uint4(0, 0, 0, 0);
+        const uint4 vw = kv_ok ? __ldg(vs + c) : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(smem + PfSmem::kK + kmajor_off(kk_local, half * 8 + c, 2048)) = kw;
+        *reinterpret_cast<uint4*>(smem + PfSmem::kV + v_off(kk_local, half * 8 + c)) = vw;
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // ---- S = Q K^T
+    if (tid == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(t_s, umma_smem_desc(sQ + ks * 256, 128, 2048), umma_smem_desc(sK + ks * 256, 128, 2048), kIdescQK,
+                  ks > 0 ? 1u : 0u);
+      umma_commit(bar_s);
+    }
+    if (!mbar_wait_bounded(bar_s, kt & 1)) {
+      atomicOr(a.status, kStatusWaitTimeout);
+      ok = false;
+    }
+    ok = __syncthreads_and(ok);                              // every thread leaves the loop together on a timeout
+    if (!ok) break;
+    tc_fence_after();
+    // ---- softmax of this thread's row (exp2 domain, lazy max)
+    float sv[2][32];
+    tmem_ld32(t_s + lane_base, sv[0]);
+    tmem_ld32(t_s + lane_base + 32, sv[1]);
+    tc_wait_ld();
+    float cmax = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int kk = kt * kPfKeys + u * 32 + i;
+        const bool vis = row_valid ? (kk <= my_limit && kk < L) : (kk < L);
+        sv[u][i] = vis ? sv[u][i] * a.scale_log2 : -INFINITY;
+        cmax = fmaxf(cmax, sv[u][i]);
+      }
+    // the running max moves (and O is rescaled) only when it would grow by more than 8 (a factor 256 in P)
+    const bool grow = cmax > m_run + 8.f || (m_run == -INFINITY && cmax > -INFINITY);
+    const float m_new = grow ? cmax : m_run;
+    const float alpha = grow ? exp2f(m_run - m_new) : 1.f;   // 0 on the first visible tile
+    float lsum = 0.f;
+    uint32_t pk[32];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const float p0 = m_new == -INFINITY ? 0.f : exp2f(sv[u][i] - m_new);
+        const float p1 = m_new == -INFINITY ? 0.f : exp2f(sv[u][i + 1] - m_new);
+        lsum += p0 + p1;
+        pk[u * 16 + i / 2] = pack_bf16x2(p0, p1);
+      }
+    l_run = l_run * alpha + lsum;
+    m_run = m_new;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(smem + PfSmem::kP + kmajor_off(tid, c, 1024)) =
+          make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+    // ---- rescale O where a max moved (O holds the finished previous tiles; tile 0 starts O from zero instead)
+    if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float ov[32];
+        tmem_ld32(t_o + lane_base + c * 32, ov);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+        tmem_st32(t_o + lane_base + c * 32, ov);
+      }
+      tc_wait_st();
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // ---- O += P V
+    if (tid == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(t_o, umma_smem_desc(sP + ks * 256, 128, 1024), umma_smem_desc(sV + ks * 256, 128, 1024), kIdescPV,
+                  (kt > 0 || ks > 0) ? 1u : 0u);
+      umma_commit(bar_o);
+    }
+    if (!mbar_wait_bounded(bar_o, kt & 1)) {
+      atomicOr(a.status, kStatusWaitTimeout);
+      ok = false;
+    }
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+  }
+
+  // ---- epilogue: O / l -> bf16 rows (a row that sees no key gets zeros, as flash-attention writes). The TMEM loads
+  //      are warp-collective, so every thread takes part; only rows of the sequence store.
+  if (ok) {
+    __nv_bfloat16* dst = a.out + static_cast<long long>(s.q0 + (row_valid ? row_j : 0)) * a.out_stride +
+                         (2 * h + row_g) * kHeadDim;
+    const float inv = (ntk > 0 && l_run > 0.f) ? 1.f / l_run : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float ov[32];
+      if (ntk > 0) {
+        tmem_ld32(t_o + lane_base + c * 32, ov);
+        tc_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ov[i] = 0.f;
+      }
+      if (row_valid) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(ov[i] * inv, ov[i + 1] * inv);
+          w.y = pack_bf16x2(ov[i + 2] * inv, ov[i + 3] * inv);
+          w.z = pack_bf16x2(ov[i + 4] * inv, ov[i + 5] * inv);
+          w.w = pack_bf16x2(ov[i + 6] * inv, ov[i + 7] * inv);
+          reinterpret_cast<uint4*>(dst + c * 32 + i)[0] = w;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols));
+  }
+}
+
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PfSmem::kBytes);
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  if (a.num_seqs == 0) return cudaSuccess;
+  const int qtiles = a.max_seqlen_q > 0 ? (a.max_seqlen_q + kPfQRows - 1) / kPfQRows : 1;
+  dim3 grid(qtiles, kKvHeads, a.num_seqs);
+  prefill_kernel<<<grid, kPfThreads, PfSmem::kBytes, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace q3

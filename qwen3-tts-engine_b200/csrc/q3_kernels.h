@@ -76,4 +76,33 @@ struct CpArgs {
 
 cudaError_t launch_cp_attn(const CpArgs& a, cudaStream_t stream);
 
+struct PrefillArgs {
+  const __nv_bfloat16* q;          // [Tq, 16, 128] rows, row stride q_stride (elements)
+  long long q_stride;
+  const __nv_bfloat16* k;          // [Tk, 8, 128] new key rows, row stride kv_stride
+  const __nv_bfloat16* v;
+  long long kv_stride;
+  const int32_t* cu_q;             // [num_seqs + 1] query row offsets
+  const int32_t* cu_k;             // [num_seqs + 1] new key row offsets (N_i >= R_i)
+  int num_seqs;
+  int max_seqlen_q;
+  const int32_t* prefix_lens;      // [num_seqs] keys already in the seat's pages ahead of the new ones, or nullptr
+  const int32_t* seat_ids;         // [num_seqs] block-table row per sequence, or nullptr (row i)
+  __nv_bfloat16* k_pool;           // [num_pages, page_size, 8, 128] (needed with a prefix or write_kv)
+  __nv_bfloat16* v_pool;
+  int num_pages;
+  int page_size;
+  const int32_t* block_table;
+  long long bt_stride;
+  int max_pages;
+  int write_kv;                    // write the new K/V rows into the pages at prefix_len + r
+  int causal;
+  float scale_log2;
+  __nv_bfloat16* out;              // [Tq, 16, 128] rows, row stride out_stride
+  long long out_stride;
+  uint32_t* status;
+};
+
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
+
 }  // namespace q3

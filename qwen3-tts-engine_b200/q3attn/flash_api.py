@@ -51,3 +51,32 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None
     else:
         out = ops.paged_decode(q3, k_cache, v_cache, cache_seqlens, block_table, scale, int(num_splits))
     return out.view(B, 1, NH, HD)
+
+
+def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, dropout_p=0.0,
+                           softmax_scale=None, causal=False, window_size=(-1, -1), softcap=0.0, alibi_slopes=None,
+                           deterministic=False, return_attn_probs=False, block_table=None):
+    """Packed varlen attention, the call at engine/talker.py:169. q [Tq,16,128], k/v [Tk,8,128], cu_seqlens int32;
+    causal masks are aligned to the bottom right (flash-attention's convention). Returns [Tq, 16, 128] bf16."""
+    _unsupported(dropout_p=dropout_p != 0.0, window_size=tuple(window_size) != (-1, -1), softcap=softcap != 0.0,
+                 alibi_slopes=alibi_slopes is not None, return_attn_probs=return_attn_probs,
+                 block_table=block_table is not None)
+    scale = float(softmax_scale) if softmax_scale is not None else HD ** -0.5
+    return ops.prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q), scale, bool(causal))
+
+
+def flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None, causal=False, window_size=(-1, -1), softcap=0.0,
+                    alibi_slopes=None, deterministic=False, return_attn_probs=False):
+    """Batched attention, the call at engine/arrivals.py:148: q [S,R,16,128] over k/v [S,n,8,128] (n >= R), causal
+    aligned to the bottom right (query i sees the n-R prefix keys and the new keys <= i). Returns [S, R, 16, 128]."""
+    _unsupported(dropout_p=dropout_p != 0.0, window_size=tuple(window_size) != (-1, -1), softcap=softcap != 0.0,
+                 alibi_slopes=alibi_slopes is not None, return_attn_probs=return_attn_probs)
+    S, R = q.shape[0], q.shape[1]
+    n = k.shape[1]
+    dev = q.device
+    cu_q = torch.arange(S + 1, dtype=torch.int32, device=dev) * R
+    cu_k = torch.arange(S + 1, dtype=torch.int32, device=dev) * n
+    scale = float(softmax_scale) if softmax_scale is not None else HD ** -0.5
+    o = ops.prefill(q.reshape(S * R, NH, HD), k.reshape(S * n, NKV, HD), v.reshape(S * n, NKV, HD), cu_q, cu_k, R,
+                    scale, bool(causal))
+    return o.view(S, R, NH, HD)

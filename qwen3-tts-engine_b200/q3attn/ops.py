@@ -225,6 +225,76 @@ def _(q, k, v, K, V, slot, softmax_scale):
     return q.new_empty(q.shape[0], NH * HD)
 
 
+def _prefill_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale, causal, k_cache=None,
+                  v_cache=None, prefix_lens=None, seat_ids=None, block_table=None, write_kv=False):
+    lib = _lib.load()
+    _check_cuda_bf16("q", q)
+    _check_cuda_bf16("k", k)
+    _check_cuda_bf16("v", v)
+    _need(q.dim() == 3 and q.shape[1] == NH and q.shape[2] == HD and q.stride(2) == 1 and q.stride(1) == HD,
+          "q must be packed rows [T, 16, 128]")
+    _need(k.dim() == 3 and k.shape[1] == NKV and k.shape[2] == HD and k.stride(2) == 1 and k.stride(1) == HD
+          and v.shape == k.shape and v.stride() == k.stride(), "k/v must be packed rows [T, 8, 128] with equal strides")
+    for name, t in (("cu_seqlens_q", cu_seqlens_q), ("cu_seqlens_k", cu_seqlens_k)):
+        _need(t.dtype == torch.int32 and t.is_cuda and t.dim() == 1 and t.is_contiguous(), f"{name}: contiguous int32")
+    n = cu_seqlens_q.numel() - 1
+    _need(cu_seqlens_k.numel() == n + 1, "cu_seqlens_q and cu_seqlens_k describe different sequence counts")
+    out = torch.empty(q.shape[0], NH, HD, dtype=torch.bfloat16, device=q.device)
+    paged = k_cache is not None
+    if paged:
+        _check_cuda_bf16("k_cache", k_cache)
+        _check_cuda_bf16("v_cache", v_cache)
+        _need(k_cache.dim() == 4 and k_cache.is_contiguous() and v_cache.shape == k_cache.shape and v_cache.is_contiguous(),
+              "caches must be contiguous [num_pages, page_size, 8, 128]")
+        _need(block_table is not None and block_table.dtype == torch.int32 and block_table.stride(1) == 1,
+              "block_table must be int32 [seats, max_pages]")
+    pl = None if prefix_lens is None else prefix_lens.to(device=q.device, dtype=torch.int32).contiguous()
+    si = None if seat_ids is None else seat_ids.to(device=q.device, dtype=torch.int32).contiguous()
+    if n == 0 or q.shape[0] == 0:
+        return out
+    with torch.cuda.device(q.device):
+        rc = lib.q3_prefill(
+            q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k.stride(0), cu_seqlens_q.data_ptr(),
+            cu_seqlens_k.data_ptr(), n, int(max_seqlen_q), _ptr(pl), _ptr(si),
+            _ptr(k_cache) if paged else None, _ptr(v_cache) if paged else None,
+            k_cache.shape[0] if paged else 0, k_cache.shape[1] if paged else 0,
+            _ptr(block_table) if paged else None, block_table.stride(0) if paged else 0,
+            block_table.shape[1] if paged else 0, int(bool(write_kv)), int(bool(causal)), NH, NKV, HD,
+            float(softmax_scale), out.data_ptr(), out.stride(0), _stream(q.device))
+    _lib.check(rc, "q3_prefill")
+    return out
+
+
+@torch.library.custom_op("q3attn::prefill", mutates_args=())
+def prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor,
+            max_seqlen_q: int, softmax_scale: float, causal: bool = True) -> torch.Tensor:
+    """Packed varlen prefill attention: q rows [T, 16, 128] of each sequence over its k/v rows [T', 8, 128]
+    (N_i >= R_i keys, causal aligned to the bottom right) -> [T, 16, 128] bf16."""
+    return _prefill_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale, causal)
+
+
+@prefill.register_fake
+def _(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale, causal=True):
+    return q.new_empty(q.shape[0], NH, HD)
+
+
+@torch.library.custom_op("q3attn::prefill_paged", mutates_args=("k_cache", "v_cache"))
+def prefill_paged(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor, max_seqlen_q: int, prefix_lens: torch.Tensor,
+                  seat_ids: torch.Tensor, block_table: torch.Tensor, softmax_scale: float, causal: bool = True,
+                  write_kv: bool = True) -> torch.Tensor:
+    """Chunked prefill into pages: sequence i's new k/v rows go to positions prefix_lens[i].. of seat seat_ids[i]
+    (write_kv) and its queries attend over the cached prefix (read through the block table) plus the new rows."""
+    return _prefill_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale, causal, k_cache, v_cache,
+                         prefix_lens, seat_ids, block_table, write_kv)
+
+
+@prefill_paged.register_fake
+def _(q, k, v, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, prefix_lens, seat_ids, block_table,
+      softmax_scale, causal=True, write_kv=True):
+    return q.new_empty(q.shape[0], NH, HD)
+
+
 def set_decode_variant(variant: int) -> int:
     """Select the decode kernel variant (0: 8-token chunks x 3 stages, two CTAs/SM; 1: 16-token x 3, one CTA/SM;
     2: 8-token x 2, two CTAs/SM)."""
