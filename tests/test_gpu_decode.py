@@ -149,7 +149,7 @@ def test_decode_c2_full_size_subset(q3):
         assert_close_attn(out[b], ref, what=f"c2 seat {b}")
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4])
 def test_decode_every_kernel_variant(q3, variant):
     """Every decode kernel variant (8/16-token chunks, 2/3 stages) against the oracle on edge lengths with 16-token
     pages, a 1-token page layout and 256-token pages, with and without the fused append."""
