@@ -148,6 +148,43 @@ int q3_cp_step(const void* q, int64_t q_batch_stride,
                int32_t batch, int32_t n_slots, int32_t slot, float softmax_scale,
                void* out, int64_t out_batch_stride, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * Attention layers from the QKV projection, with the q/k RMSNorm and rotate-half RoPE of engine/ops.py:51-60 fused
+ * into the attention kernels (bf16 rounding points of the reference's eager source: normalise in fp32 and round,
+ * times the weight and round, x*cos and rot(x)*sin each rounded, their sum rounded).
+ * qkv rows are [q (16x128) | k (8x128) | v (8x128)] bf16, qkv_row_stride elements apart (16-byte aligned rows). */
+typedef struct q3_qk_norm_rope {
+  const void* q_norm_weight;   /* [128] bf16 (w.qn) */
+  const void* k_norm_weight;   /* [128] bf16 (w.kn) */
+  const void* cos;             /* [rows, 128] bf16: row b serves batch row b ... */
+  const void* sin;
+  int64_t rope_row_stride;     /* ... rows rope_row_stride elements apart; 0 = one row for every batch row */
+  float eps;                   /* 1e-6 in the reference (ops.py:51) */
+} q3_qk_norm_rope;
+
+/* One talker attention layer after the QKV GEMM: engine/talker.py:69-77 (q = rope(rms(q, qn)), k = rope(rms(k, kn)),
+ * the k/v index_copy_ into the pools at position cache_seqlens[b], flash_attn_with_kvcache over cache + new row).
+ * cos/sin row b must be the rotary row of position cache_seqlens[b] (W.cos[pos], talker.py:111). Pools, table,
+ * workspace (q3_paged_decode_workspace_bytes) and errors as q3_paged_decode; always the default configuration. */
+int q3_paged_decode_qkv(const void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rope* norm_rope,
+                        void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,
+                        const int32_t* cache_seqlens,
+                        const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
+                        int32_t batch, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                        float softmax_scale,
+                        void* out, int64_t out_batch_stride,
+                        void* workspace, size_t workspace_bytes, int32_t num_splits,
+                        void* stream);
+/* One code-predictor (step, layer) after the QKV GEMM: engine/code_predictor.py:40-41 (q/k norm + RoPE with
+ * cp_cos/cp_sin[p]), :58 (slot-p write) and :46-47 (attention over slots 0..p), in one launch. K/V strides as
+ * q3_cp_step. */
+int q3_cp_step_qkv(const void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rope* norm_rope,
+                   void* K, void* V,
+                   int64_t k_batch_stride, int64_t k_head_stride, int64_t k_slot_stride,
+                   int64_t v_batch_stride, int64_t v_head_stride, int64_t v_slot_stride,
+                   int32_t batch, int32_t n_slots, int32_t slot, float softmax_scale,
+                   void* out, int64_t out_batch_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

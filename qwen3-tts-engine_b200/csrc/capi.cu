@@ -56,9 +56,9 @@ int check_family(int32_t nh, int32_t nkv, int32_t hd) {
   return (nh == q3::kQHeads && nkv == q3::kKvHeads && hd == q3::kHeadDim) ? Q3_OK : Q3_ERR_UNSUPPORTED;
 }
 
-long long decode_grid(int dev, int32_t batch, int32_t num_splits, int32_t max_pages, int32_t page_size) {
-  const int rows = q3::decode_rows_per_chunk(g_decode_variant);
-  long long G = num_splits > 0 ? num_splits : static_cast<long long>(sm_count(dev)) * q3::decode_ctas_per_sm(g_decode_variant);
+long long decode_grid(int dev, int32_t batch, int32_t num_splits, int32_t max_pages, int32_t page_size, int variant) {
+  const int rows = q3::decode_rows_per_chunk(variant);
+  long long G = num_splits > 0 ? num_splits : static_cast<long long>(sm_count(dev)) * q3::decode_ctas_per_sm(variant);
   const long long max_chunks = static_cast<long long>(batch) * ((static_cast<long long>(max_pages) * page_size + rows - 1) / rows);
   if (max_pages > 0 && page_size > 0 && G > max_chunks) G = max_chunks;
   return G < 1 ? 1 : G;
@@ -150,23 +150,41 @@ int q3_paged_decode_resident_ctas(int variant) { return q3::decode_occupancy(var
 size_t q3_paged_decode_workspace_bytes(int32_t batch, int32_t num_splits) {
   int dev = 0;
   if (batch < 0 || current_device(&dev) != Q3_OK) return 0;
-  // Upper bound over all block-table shapes: the grid is at most SMs x CTAs/SM (or num_splits).
-  const long long G = decode_grid(dev, batch, num_splits, 0, 0);
+  // Upper bound over all block-table shapes and kernel configurations (the selected variant, and the default one that
+  // q3_paged_decode_qkv always uses): the grid is at most SMs x CTAs/SM (or num_splits).
+  long long G = decode_grid(dev, batch, num_splits, 0, 0, g_decode_variant);
+  const long long G0 = decode_grid(dev, batch, num_splits, 0, 0, 0);
+  if (G0 > G) G = G0;
   return ws_bytes_needed(batch, G);
 }
 
-int q3_paged_decode(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
-                    int64_t kv_new_batch_stride, void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,
-                    const int32_t* cache_seqlens, const int32_t* block_table, int64_t block_table_stride,
-                    int32_t max_pages_per_seat, int32_t batch, int32_t num_heads, int32_t num_kv_heads,
-                    int32_t head_dim, float softmax_scale, void* out, int64_t out_batch_stride, void* workspace,
-                    size_t workspace_bytes, int32_t num_splits, void* stream) {
+namespace {
+
+bool norm_rope_ok(const q3_qk_norm_rope* nr) {
+  return nr->q_norm_weight && nr->k_norm_weight && nr->cos && nr->sin && nr->rope_row_stride >= 0 &&
+         nr->eps >= 0.f;
+}
+
+bool norm_rope_aligned(const q3_qk_norm_rope* nr) {
+  return aligned(nr->q_norm_weight, 8) && aligned(nr->k_norm_weight, 8) && aligned(nr->cos, 8) &&
+         aligned(nr->sin, 8) && (nr->rope_row_stride % 4) == 0;
+}
+
+// q3_paged_decode and q3_paged_decode_qkv: validation, workspace carving and launch. With nr set, q and k_new are raw
+// projections and the kernel applies RMSNorm + RoPE (default configuration only).
+int decode_common(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
+                  int64_t kv_new_batch_stride, const q3_qk_norm_rope* nr, void* k_pool, void* v_pool,
+                  int32_t num_pages, int32_t page_size, const int32_t* cache_seqlens, const int32_t* block_table,
+                  int64_t block_table_stride, int32_t max_pages_per_seat, int32_t batch, int32_t num_heads,
+                  int32_t num_kv_heads, int32_t head_dim, float softmax_scale, void* out, int64_t out_batch_stride,
+                  void* workspace, size_t workspace_bytes, int32_t num_splits, void* stream) {
   int rc = check_family(num_heads, num_kv_heads, head_dim);
   if (rc != Q3_OK) return rc;
   if (batch < 0 || num_pages <= 0 || page_size <= 0 || max_pages_per_seat <= 0 || num_splits < 0) return Q3_ERR_INVALID;
   if (batch == 0) return Q3_OK;
   if (!q || !k_pool || !v_pool || !cache_seqlens || !block_table || !out) return Q3_ERR_INVALID;
   if ((k_new == nullptr) != (v_new == nullptr)) return Q3_ERR_INVALID;
+  if (nr && (!k_new || !norm_rope_ok(nr))) return Q3_ERR_INVALID;
   if (block_table_stride < max_pages_per_seat || q_batch_stride < q3::kQHeads * q3::kHeadDim ||
       out_batch_stride < q3::kQHeads * q3::kHeadDim)
     return Q3_ERR_INVALID;
@@ -177,9 +195,11 @@ int q3_paged_decode(const void* q, int64_t q_batch_stride, const void* k_new, co
   if (k_new && (!aligned(k_new, 16) || !aligned(v_new, 16) || (kv_new_batch_stride % 8) ||
                 kv_new_batch_stride < q3::kKvHeads * q3::kHeadDim))
     return Q3_ERR_ALIGNMENT;
+  if (nr && !norm_rope_aligned(nr)) return Q3_ERR_ALIGNMENT;
   int dev = 0;
   if ((rc = current_device(&dev)) != Q3_OK) return rc;
-  const long long G = decode_grid(dev, batch, num_splits, max_pages_per_seat, page_size);
+  const int variant = nr ? 0 : g_decode_variant;
+  const long long G = decode_grid(dev, batch, num_splits, max_pages_per_seat, page_size, variant);
   if (G > (1ll << 30)) return Q3_ERR_INVALID;
   const WsLayout w = ws_layout(workspace_bytes, batch, G);
   if (!workspace || !w.fits || !aligned(workspace, 256)) return Q3_ERR_WORKSPACE;
@@ -209,7 +229,50 @@ int q3_paged_decode(const void* q, int64_t q_batch_stride, const void* k_new, co
   a.ws_ml = reinterpret_cast<float*>(ws + w.ml);
   a.ws_o = reinterpret_cast<float*>(ws + w.o);
   a.status = st;
-  return record(q3::launch_paged_decode(a, static_cast<int>(G), g_decode_variant, static_cast<cudaStream_t>(stream)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (nr) {
+    a.qn_w = static_cast<const __nv_bfloat16*>(nr->q_norm_weight);
+    a.kn_w = static_cast<const __nv_bfloat16*>(nr->k_norm_weight);
+    a.rope_cos = static_cast<const __nv_bfloat16*>(nr->cos);
+    a.rope_sin = static_cast<const __nv_bfloat16*>(nr->sin);
+    a.rope_stride = nr->rope_row_stride;
+    a.eps = nr->eps;
+    return record(q3::launch_paged_decode_fused(a, static_cast<int>(G), s));
+  }
+  return record(q3::launch_paged_decode(a, static_cast<int>(G), variant, s));
+}
+
+}  // namespace
+
+int q3_paged_decode(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
+                    int64_t kv_new_batch_stride, void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,
+                    const int32_t* cache_seqlens, const int32_t* block_table, int64_t block_table_stride,
+                    int32_t max_pages_per_seat, int32_t batch, int32_t num_heads, int32_t num_kv_heads,
+                    int32_t head_dim, float softmax_scale, void* out, int64_t out_batch_stride, void* workspace,
+                    size_t workspace_bytes, int32_t num_splits, void* stream) {
+  return decode_common(q, q_batch_stride, k_new, v_new, kv_new_batch_stride, nullptr, k_pool, v_pool, num_pages,
+                       page_size, cache_seqlens, block_table, block_table_stride, max_pages_per_seat, batch, num_heads,
+                       num_kv_heads, head_dim, softmax_scale, out, out_batch_stride, workspace, workspace_bytes,
+                       num_splits, stream);
+}
+
+int q3_paged_decode_qkv(const void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rope* norm_rope, void* k_pool,
+                        void* v_pool, int32_t num_pages, int32_t page_size, const int32_t* cache_seqlens,
+                        const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
+                        int32_t batch, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float softmax_scale,
+                        void* out, int64_t out_batch_stride, void* workspace, size_t workspace_bytes,
+                        int32_t num_splits, void* stream) {
+  if (!norm_rope) return Q3_ERR_INVALID;
+  int rc = check_family(num_heads, num_kv_heads, head_dim);
+  if (rc != Q3_OK) return rc;
+  if (qkv_row_stride < (q3::kQHeads + 2 * q3::kKvHeads) * q3::kHeadDim) return Q3_ERR_INVALID;
+  const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(qkv);
+  const __nv_bfloat16* k_new = base ? base + q3::kQHeads * q3::kHeadDim : nullptr;
+  const __nv_bfloat16* v_new = base ? base + (q3::kQHeads + q3::kKvHeads) * q3::kHeadDim : nullptr;
+  return decode_common(qkv, qkv_row_stride, k_new, v_new, qkv_row_stride, norm_rope, k_pool, v_pool, num_pages,
+                       page_size, cache_seqlens, block_table, block_table_stride, max_pages_per_seat, batch, num_heads,
+                       num_kv_heads, head_dim, softmax_scale, out, out_batch_stride, workspace, workspace_bytes,
+                       num_splits, stream);
 }
 
 static int append_common(q3::AppendArgs& a, const void* k, const void* v, int64_t row_stride, void* k_pool,
@@ -310,6 +373,28 @@ int q3_cp_step(const void* q, int64_t q_batch_stride, const void* k_new, const v
   a.v_new = static_cast<const __nv_bfloat16*>(v_new);
   a.kv_new_stride = kv_new_batch_stride;
   return cp_common(a, q, q_batch_stride, K, V, k_batch_stride, k_head_stride, k_slot_stride, v_batch_stride,
+                   v_head_stride, v_slot_stride, batch, n_slots, slot + 1, softmax_scale, out, out_batch_stride, stream);
+}
+
+int q3_cp_step_qkv(const void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rope* norm_rope, void* K, void* V,
+                   int64_t k_batch_stride, int64_t k_head_stride, int64_t k_slot_stride, int64_t v_batch_stride,
+                   int64_t v_head_stride, int64_t v_slot_stride, int32_t batch, int32_t n_slots, int32_t slot,
+                   float softmax_scale, void* out, int64_t out_batch_stride, void* stream) {
+  if (!norm_rope || !norm_rope_ok(norm_rope)) return Q3_ERR_INVALID;
+  if (qkv_row_stride < (q3::kQHeads + 2 * q3::kKvHeads) * q3::kHeadDim) return Q3_ERR_INVALID;
+  if (!norm_rope_aligned(norm_rope)) return Q3_ERR_ALIGNMENT;
+  const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(qkv);
+  q3::CpArgs a{};
+  a.k_new = base ? base + q3::kQHeads * q3::kHeadDim : nullptr;
+  a.v_new = base ? base + (q3::kQHeads + q3::kKvHeads) * q3::kHeadDim : nullptr;
+  a.kv_new_stride = qkv_row_stride;
+  a.qn_w = static_cast<const __nv_bfloat16*>(norm_rope->q_norm_weight);
+  a.kn_w = static_cast<const __nv_bfloat16*>(norm_rope->k_norm_weight);
+  a.rope_cos = static_cast<const __nv_bfloat16*>(norm_rope->cos);
+  a.rope_sin = static_cast<const __nv_bfloat16*>(norm_rope->sin);
+  a.rope_stride = norm_rope->rope_row_stride;
+  a.eps = norm_rope->eps;
+  return cp_common(a, qkv, qkv_row_stride, K, V, k_batch_stride, k_head_stride, k_slot_stride, v_batch_stride,
                    v_head_stride, v_slot_stride, batch, n_slots, slot + 1, softmax_scale, out, out_batch_stride, stream);
 }
 

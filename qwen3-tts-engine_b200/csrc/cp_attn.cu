@@ -8,13 +8,16 @@
 //
 // One CTA per seat, one warp per KV head; lane l owns dims 4l..4l+3 of both q heads of the group. All K and V rows are
 // loaded up front (at most 16 x 8 bytes each per lane) so the whole step costs one round of memory latency. With k_new
-// given, the new row is stored to slot n_live-1 and used from registers.
+// given, the new row is stored to slot n_live-1 and used from registers. With the norm weights given (q3_cp_step_qkv,
+// the kernel instantiated with FUSE), q and k_new are raw projections: both q heads and the new k row get RMSNorm +
+// RoPE here (code_predictor.py:40-41).
 #include "q3_common.cuh"
 #include "q3_kernels.h"
 
 namespace q3 {
 
-__global__ void __launch_bounds__(256) cp_attn_kernel(const CpArgs a) {
+template <bool FUSE>
+__global__ void __launch_bounds__(256, FUSE ? 2 : 0) cp_attn_kernel(const CpArgs a) {
   __shared__ float pbuf[kKvHeads][32];
   const int b = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = a.n_live, pnew = n - 1;
@@ -44,6 +47,17 @@ __global__ void __launch_bounds__(256) cp_attn_kernel(const CpArgs a) {
         vw[s] = *reinterpret_cast<const uint2*>(vb + s * a.sv_s);
       }
     }
+  }
+  if constexpr (FUSE) {   // fused q/k RMSNorm + RoPE
+    const long long ro = static_cast<long long>(b) * a.rope_stride;
+    const __nv_bfloat16* cs = a.rope_cos + ro;
+    const __nv_bfloat16* sn = a.rope_sin + ro;
+    q0 = rms_rope_head(q0, a.qn_w, cs, sn, a.eps, lane);
+    q1 = rms_rope_head(q1, a.qn_w, cs, sn, a.eps, lane);
+    kn = float4_to_bf16x4(rms_rope_head(bf16x4_to_float4(kn), a.kn_w, cs, sn, a.eps, lane));
+#pragma unroll
+    for (int s = 0; s < 16; ++s)
+      if (s == pnew) kw[s] = kn;
   }
   if (append) {
     *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(kb) + pnew * a.sk_s) = kn;
@@ -96,7 +110,10 @@ __global__ void __launch_bounds__(256) cp_attn_kernel(const CpArgs a) {
 
 cudaError_t launch_cp_attn(const CpArgs& a, cudaStream_t stream) {
   if (a.B == 0) return cudaSuccess;
-  cp_attn_kernel<<<a.B, 256, 0, stream>>>(a);
+  if (a.qn_w != nullptr)
+    cp_attn_kernel<true><<<a.B, 256, 0, stream>>>(a);
+  else
+    cp_attn_kernel<false><<<a.B, 256, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -29,7 +29,7 @@
 
 namespace q3 {
 
-template <int ROWS, int NSTAGES>
+template <int ROWS, int NSTAGES, bool FUSE = false>
 struct DecodeSmemLayout {
   static constexpr int kStageBytes = ROWS * kRowBytes;                  // K (or V) of one chunk
   static constexpr int kKOff = 0;
@@ -38,12 +38,16 @@ struct DecodeSmemLayout {
   static constexpr int kDoneOff = kBarOff + NSTAGES * 8;                // done[NSTAGES] reader tickets
   static constexpr int kPOff = kDoneOff + ((NSTAGES * 4 + 15) / 16) * 16;   // per-warp probabilities [ROWS][2]
   static constexpr int kMiscOff = kPOff + kDecodeWarps * 2 * ROWS * 4;
-  static constexpr int kBytes = kMiscOff + 64;
+  // FUSE: per-warp normalised q [2][128] bf16, read back with 16-byte loads, so 16-byte (here 128-byte) aligned
+  static constexpr int kQOff = ((kMiscOff + 64 + 127) / 128) * 128;
+  static constexpr int kBytes = kQOff + (FUSE ? kDecodeWarps * 2 * kHeadBytes : 0);
+  static_assert(kQOff % 16 == 0 && kKOff % 16 == 0 && kVOff % 16 == 0 && kStageBytes % 16 == 0,
+                "16-byte shared-memory accesses need 16-byte aligned regions");
 };
 
-template <int ROWS, int NSTAGES, int MIN_CTAS>
+template <int ROWS, int NSTAGES, int MIN_CTAS, bool FUSE = false>
 __global__ void __maxnreg__(decode_max_regs<MIN_CTAS>()) paged_decode_kernel(const DecodeArgs a) {
-  using SL = DecodeSmemLayout<ROWS, NSTAGES>;
+  using SL = DecodeSmemLayout<ROWS, NSTAGES, FUSE>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL::kBarOff);
   unsigned* done = reinterpret_cast<unsigned*>(smem + SL::kDoneOff);
@@ -104,12 +108,27 @@ __global__ void __maxnreg__(decode_max_regs<MIN_CTAS>()) paged_decode_kernel(con
     // ---- a seat's chunks within this CTA: load its q (rotated, pre-scaled), reset the running state
     float2 qv[2][P][4];                         // [head][piece (rotated)][pair] pre-scaled by scale*log2(e)
     {
-      const __nv_bfloat16* qb = a.q + static_cast<long long>(cur.seat) * a.q_stride + (2 * h) * kHeadDim + my_part * DPL;
+      const __nv_bfloat16* qrow = a.q + static_cast<long long>(cur.seat) * a.q_stride + (2 * h) * kHeadDim;
+      if constexpr (FUSE) {
+        // raw projection -> RMSNorm + RoPE of both q heads (4 dims per lane), staged in this warp's shared slot
+        const long long ro = static_cast<long long>(cur.seat) * a.rope_stride;
+        uint2* qs = reinterpret_cast<uint2*>(smem + SL::kQOff + warp * 2 * kHeadBytes);
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const float4 x = bf16x4_to_float4(*reinterpret_cast<const uint2*>(qrow + g * kHeadDim + 4 * lane));
+          qs[g * 32 + lane] =
+              float4_to_bf16x4(rms_rope_head(x, a.qn_w, a.rope_cos + ro, a.rope_sin + ro, a.eps, lane));
+        }
+        __syncwarp();
+        qrow = reinterpret_cast<const __nv_bfloat16*>(qs);
+      }
+      const __nv_bfloat16* qb = qrow + my_part * DPL;
 #pragma unroll
       for (int g = 0; g < 2; ++g) {
 #pragma unroll
         for (int pc = 0; pc < P; ++pc) {
-          const uint4 w = __ldg(reinterpret_cast<const uint4*>(qb + g * kHeadDim + ((pc + rot) % P) * 8));
+          const uint4* src = reinterpret_cast<const uint4*>(qb + g * kHeadDim + ((pc + rot) % P) * 8);
+          const uint4 w = FUSE ? *src : __ldg(src);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = bf16x2_to_float2(word_of(w, e));
@@ -228,6 +247,18 @@ __global__ void __maxnreg__(decode_max_regs<MIN_CTAS>()) paged_decode_kernel(con
       const int rows = min(ROWS, cur.len - tok0);
       uint8_t* kst = smem + SL::kKOff + stage * SL::kStageBytes;
       uint8_t* vst = smem + SL::kVOff + stage * SL::kStageBytes;
+      if constexpr (FUSE) {
+        if (tok0 + rows == cur.len) {
+          // the new token's raw k row (copied from the projection): RMSNorm + RoPE of head h in place, before it is
+          // scored and appended; the generic-proxy write is fenced against the stage's next bulk refill
+          uint2* kr = reinterpret_cast<uint2*>(kst + (rows - 1) * kRowBytes + h * kHeadBytes) + lane;
+          const long long ro = static_cast<long long>(cur.seat) * a.rope_stride;
+          *kr = float4_to_bf16x4(
+              rms_rope_head(bf16x4_to_float4(*kr), a.kn_w, a.rope_cos + ro, a.rope_sin + ro, a.eps, lane));
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+      }
       float a0, a1;
       softmax(score(kst), rows, a0, a1);
       scale_out(a0, a1);
@@ -259,10 +290,10 @@ __global__ void __maxnreg__(decode_max_regs<MIN_CTAS>()) paged_decode_kernel(con
 }
 
 // ------------------------------------------------------------------ host-side launch
-template <int ROWS, int NSTAGES, int MIN_CTAS>
+template <int ROWS, int NSTAGES, int MIN_CTAS, bool FUSE = false>
 static cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t stream) {
-  using SL = DecodeSmemLayout<ROWS, NSTAGES>;
-  auto kern = paged_decode_kernel<ROWS, NSTAGES, MIN_CTAS>;
+  using SL = DecodeSmemLayout<ROWS, NSTAGES, FUSE>;
+  auto kern = paged_decode_kernel<ROWS, NSTAGES, MIN_CTAS, FUSE>;
   static thread_local int configured_device = -1;   // attribute set once per (thread, device), before any capture
   int dev = 0;
   cudaGetDevice(&dev);
@@ -306,6 +337,10 @@ int decode_occupancy(int variant) {
 int decode_rows_per_chunk(int variant) { return variant == 1 ? 16 : 8; }
 
 int decode_ctas_per_sm(int variant) { return variant == 1 ? 1 : 2; }
+
+cudaError_t launch_paged_decode_fused(const DecodeArgs& a, int grid, cudaStream_t stream) {
+  return launch_decode<8, 3, 2, true>(a, grid, stream);
+}
 
 cudaError_t launch_paged_decode(const DecodeArgs& a, int grid, int variant, cudaStream_t stream) {
   switch (variant) {

@@ -54,6 +54,36 @@ __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// ---------------------------------------------------------------- q/k RMSNorm + rotate-half RoPE of one head
+// One head of 128 dims held 4 dims per lane (lane l: dims 4l..4l+3), x = the raw head as floats (bf16 values).
+// Arithmetic and rounding points of engine/ops.py:51-60 run in bf16:
+//   xn  = bf16(x * rsqrt(mean(x^2) + eps))                      normalise in fp32, cast back     (ops.py:53-54)
+//   y   = bf16(w * xn)                                                                          (ops.py:55)
+//   out = bf16(bf16(y * cos) + bf16(rot(y) * sin)),  rot(y)[d] = -y[d + 64] (d < 64), y[d - 64]  (ops.py:58-60)
+// Dims d and d + 64 live in lanes l and l + 16, so rot() is one shuffle. w, cs, sn point at [128] bf16 rows.
+__device__ __forceinline__ float4 rms_rope_head(float4 x, const __nv_bfloat16* w, const __nv_bfloat16* cs,
+                                               const __nv_bfloat16* sn, float eps, int lane) {
+  float ss = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss * (1.f / kHeadDim) + eps);
+  const float4 wv = bf16x4_to_float4(*reinterpret_cast<const uint2*>(w + 4 * lane));
+  float4 y;
+  y.x = round_bf16(wv.x * round_bf16(x.x * r));
+  y.y = round_bf16(wv.y * round_bf16(x.y * r));
+  y.z = round_bf16(wv.z * round_bf16(x.z * r));
+  y.w = round_bf16(wv.w * round_bf16(x.w * r));
+  const float sg = lane < 16 ? -1.f : 1.f;
+  const float4 rt = make_float4(sg * __shfl_xor_sync(0xffffffffu, y.x, 16), sg * __shfl_xor_sync(0xffffffffu, y.y, 16),
+                                sg * __shfl_xor_sync(0xffffffffu, y.z, 16), sg * __shfl_xor_sync(0xffffffffu, y.w, 16));
+  const float4 c = bf16x4_to_float4(*reinterpret_cast<const uint2*>(cs + 4 * lane));
+  const float4 s = bf16x4_to_float4(*reinterpret_cast<const uint2*>(sn + 4 * lane));
+  return make_float4(round_bf16(round_bf16(y.x * c.x) + round_bf16(rt.x * s.x)),
+                     round_bf16(round_bf16(y.y * c.y) + round_bf16(rt.y * s.y)),
+                     round_bf16(round_bf16(y.z * c.z) + round_bf16(rt.z * s.z)),
+                     round_bf16(round_bf16(y.w * c.w) + round_bf16(rt.w * s.w)));
+}
+
 // ---------------------------------------------------------------- shared-memory barriers and bulk copies
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -29,12 +29,21 @@ struct DecodeArgs {
   float* ws_ml;                    // [(G + B), 8, 2, 2] fp32 (running max, running sum)
   uint32_t* counters;              // [B, 8] zero between launches
   uint32_t* status;
+  // Fused q/k RMSNorm + RoPE (the kernel instantiated with FUSE): q rows and k_new rows are raw projections.
+  const __nv_bfloat16* qn_w = nullptr;     // [128]
+  const __nv_bfloat16* kn_w = nullptr;     // [128]
+  const __nv_bfloat16* rope_cos = nullptr; // row b at b * rope_stride, [128] each
+  const __nv_bfloat16* rope_sin = nullptr;
+  long long rope_stride = 0;
+  float eps = 1e-6f;
 };
 
 int decode_rows_per_chunk(int variant);
 int decode_ctas_per_sm(int variant);
 int decode_occupancy(int variant);   // resident CTAs per SM measured by the runtime (-1 on error)
 cudaError_t launch_paged_decode(const DecodeArgs& a, int grid, int variant, cudaStream_t stream);
+// Default configuration (variant 0) with the q/k RMSNorm + RoPE fused in (a.qn_w etc. set, k_new required).
+cudaError_t launch_paged_decode_fused(const DecodeArgs& a, int grid, cudaStream_t stream);
 
 struct AppendArgs {
   const __nv_bfloat16* k_rows;     // [n_rows, row_elems] with row stride rows_stride (elements)
@@ -72,6 +81,13 @@ struct CpArgs {
   float scale_log2;
   __nv_bfloat16* out;              // [B, 16*128] rows, batch stride out_stride
   long long out_stride;
+  // Fused q/k RMSNorm + RoPE (nullptr: q and k_new are used as given); k_new required when set.
+  const __nv_bfloat16* qn_w = nullptr;
+  const __nv_bfloat16* kn_w = nullptr;
+  const __nv_bfloat16* rope_cos = nullptr;
+  const __nv_bfloat16* rope_sin = nullptr;
+  long long rope_stride = 0;
+  float eps = 1e-6f;
 };
 
 cudaError_t launch_cp_attn(const CpArgs& a, cudaStream_t stream);

@@ -13,6 +13,15 @@ STATUS_WAIT_TIMEOUT, STATUS_BAD_PAGE, STATUS_BAD_LENGTH = 1, 2, 4
 
 _P, _I32, _I64, _F32, _SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 
+
+class QkNormRope(ctypes.Structure):
+    """struct q3_qk_norm_rope (include/q3attn.h): q/k RMSNorm weights and RoPE rows fused into the attention kernels."""
+    _fields_ = [("q_norm_weight", _P), ("k_norm_weight", _P), ("cos", _P), ("sin", _P),
+                ("rope_row_stride", _I64), ("eps", _F32)]
+
+
+_NR = ctypes.POINTER(QkNormRope)
+
 # name -> (restype, argtypes); every symbol include/q3attn.h declares
 SIGNATURES = {
     "q3_version": (ctypes.c_int, []),
@@ -25,6 +34,8 @@ SIGNATURES = {
                                        _I32, _I32, _I32, _I32, _F32, _P, _I64, _P, _SZ, _I32, _P]),
     "q3_paged_decode_noalloc": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P, _I32, _I32, _P, _P, _I64, _I32,
                                                _I32, _I32, _I32, _I32, _F32, _P, _I64, _I32, _P]),
+    "q3_paged_decode_qkv": (ctypes.c_int, [_P, _I64, _NR, _P, _P, _I32, _I32, _P, _P, _I64, _I32,
+                                           _I32, _I32, _I32, _I32, _F32, _P, _I64, _P, _SZ, _I32, _P]),
     "q3_set_decode_variant": (ctypes.c_int, [ctypes.c_int]),
     "q3_paged_decode_resident_ctas": (ctypes.c_int, [ctypes.c_int]),
     "q3_prefill": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P, _I32, _I32, _P, _P, _P, _P, _I32, _I32, _P, _I64,
@@ -36,6 +47,8 @@ SIGNATURES = {
                                   _P, _I64, _P]),
     "q3_cp_step": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
                                   _I32, _F32, _P, _I64, _P]),
+    "q3_cp_step_qkv": (ctypes.c_int, [_P, _I64, _NR, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
+                                      _I32, _F32, _P, _I64, _P]),
 }
 
 _lib = None

@@ -2,9 +2,11 @@
 
 Mirrors engine/talker.py (Talker: seats, paged K/V, per-seat sampling state, one CUDA graph per batch bucket) and
 engine/code_predictor.py (CodePredictor: 16-slot K/V scratch, 15 sampled steps), with the attention hot path replaced:
-  talker layer  (talker.py:68-79)   K/V append + paged decode in one launch (q3attn.paged_decode_append)
-  CP layer      (code_predictor.py:57-59)  slot-p append + attention in one launch (q3attn.cp_step)
-GEMMs, norms, RoPE and sampling stay PyTorch ops in the reference's order and dtype (engine/ops.py:40-76).
+  talker layer  (talker.py:69-77)   q/k RMSNorm + RoPE, K/V append and paged decode in one launch
+                                    (q3attn.paged_decode_qkv, straight from the QKV projection)
+  CP layer      (code_predictor.py:40-42, 58, 46-47)  q/k RMSNorm + RoPE, slot-p write and attention in one launch
+                                    (q3attn.cp_step_qkv)
+GEMMs, the layer norms, the MLP and sampling stay PyTorch ops in the reference's order and dtype (engine/ops.py:40-76).
 
 Differences from the reference, all in layout, none in the maths: the K/V pools are paged with a configurable page
 size and block table (default 16-token pages; the reference uses 256-token pages and the identity table,
@@ -62,15 +64,12 @@ class CodePredictor:
 
     def _s(self, x, B, p):
         W = self.W
-        nq, nk = self.nh * self.hd, self.nkv * self.hd
         cos, sin = W.cp_cos[p], W.cp_sin[p]
         for l in range(self.L):
             w = W.cp_layers[l]
-            qkv = F.linear(rms(x, w.ln1), w.qkv)                                        # code_predictor.py:39-42
-            q = rope(rms(qkv[:, :nq].view(B, self.nh, self.hd), w.qn), cos, sin)
-            k = rope(rms(qkv[:, nq:nq + nk].view(B, self.nkv, self.hd), w.kn), cos, sin)
-            v = qkv[:, nq + nk:].contiguous().view(B, self.nkv, self.hd)   # k and v share one row stride
-            o = ops.cp_step(q, k, v, self.K[l, :B], self.V[l, :B], p, self.scale)    # code_predictor.py:58, 46-47
+            qkv = F.linear(rms(x, w.ln1), w.qkv)                                        # code_predictor.py:39
+            o = ops.cp_step_qkv(qkv, w.qn, w.kn, cos, sin, self.K[l, :B], self.V[l, :B], p,  # :40-42, 58, 46-47
+                                self.scale)
             x = x + F.linear(o, w.o)
             gu = F.linear(rms(x, w.ln2), w.gu)
             x = x + F.linear(F.silu(gu[..., :self.ffn]) * gu[..., self.ffn:], w.down)
@@ -156,15 +155,13 @@ class Talker:
     def decode(self, x, cos, sin, pos, bt):
         """talker.py:63-80: x [B,H] -> post-norm hidden; appends each row's K/V at position pos and attends over pos+1."""
         B = x.shape[0]
-        nq, nk = self.nh * self.hd, self.nkv * self.hd
+        nq = self.nh * self.hd
         seqlens = pos.to(torch.int32)
         for l in range(len(self.W.layers)):
             w = self.W.layers[l]
-            qkv = F.linear(rms(x, w.ln1), w.qkv)
-            q = rope(rms(qkv[:, :nq].view(B, self.nh, self.hd), w.qn), cos, sin)
-            k = rope(rms(qkv[:, nq:nq + nk].view(B, self.nkv, self.hd), w.kn), cos, sin)
-            v = qkv[:, nq + nk:].contiguous().view(B, self.nkv, self.hd)   # k and v share one row stride
-            o = ops.paged_decode_append(q, k, v, self.kc[l], self.vc[l], seqlens, bt, self.scale, 0)
+            qkv = F.linear(rms(x, w.ln1), w.qkv)                                           # talker.py:68
+            o = ops.paged_decode_qkv(qkv, w.qn, w.kn, cos, sin, self.kc[l], self.vc[l], seqlens, bt,  # :69-77
+                                     self.scale)
             x = x + F.linear(o.reshape(B, nq), w.o)
             x = x + mlp(rms(x, w.ln2), w, self.ffn)
         return rms(x, self.W.norm)

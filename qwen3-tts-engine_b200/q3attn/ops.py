@@ -14,6 +14,7 @@ The decode workspace is a per-(device, stream) buffer allocated outside capture:
 capturing (the engine's warm-up passes do, engine/talker.py:120). Its observable content is unchanged by a call (the
 ticket counters return to zero), so it is not declared as a mutated argument.
 """
+import ctypes
 from typing import Optional
 
 import torch
@@ -120,6 +121,68 @@ def _(q, k, v, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, num_
     return q.new_empty(q.shape[0], NH, HD)
 
 
+def _norm_rope(q_norm_w, k_norm_w, cos, sin, eps, B):
+    """struct q3_qk_norm_rope for [128] bf16 norm weights and cos/sin rows ([B, 128], or [128] / [1, 128] for one row
+    shared by every batch row)."""
+    for n, t in (("q_norm_w", q_norm_w), ("k_norm_w", k_norm_w), ("cos", cos), ("sin", sin)):
+        _check_cuda_bf16(n, t)
+        _need(t.shape[-1] == HD and t.stride(-1) == 1, f"{n} must have a contiguous last dim of 128")
+    _need(q_norm_w.numel() == HD and k_norm_w.numel() == HD, "norm weights must be [128]")
+    c2, s2 = cos.reshape(-1, HD), sin.reshape(-1, HD)
+    _need(c2.shape == s2.shape and c2.stride() == s2.stride() and c2.shape[0] in (1, B),
+          "cos/sin must both be [B, 128] (one row per batch row) or one [128] row")
+    stride = 0 if c2.shape[0] == 1 else c2.stride(0)
+    return _lib.QkNormRope(q_norm_w.data_ptr(), k_norm_w.data_ptr(), c2.data_ptr(), s2.data_ptr(), stride, float(eps))
+
+
+def _qkv_rows(qkv):
+    _check_cuda_bf16("qkv", qkv)
+    _need(qkv.dim() == 2 and qkv.shape[1] == (NH + 2 * NKV) * HD and qkv.stride(1) == 1,
+          "qkv must be [B, 4096] rows: q (16x128) | k (8x128) | v (8x128)")
+    return qkv
+
+
+@torch.library.custom_op("q3attn::paged_decode_qkv", mutates_args=("k_cache", "v_cache"))
+def paged_decode_qkv(qkv: torch.Tensor, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, cos: torch.Tensor,
+                     sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, cache_seqlens: torch.Tensor,
+                     block_table: torch.Tensor, softmax_scale: float, eps: float = 1e-6,
+                     num_splits: int = 0) -> torch.Tensor:
+    """One talker attention layer from the QKV projection (engine/talker.py:69-77): q and k get RMSNorm + RoPE
+    (cos/sin row b = position cache_seqlens[b]), k/v are appended at cache_seqlens[b] through the block table, and q
+    attends over cache_seqlens[b] + 1 tokens -> [B,16,128] bf16. One launch."""
+    lib = _lib.load()
+    qkv = _qkv_rows(qkv)
+    B = qkv.shape[0]
+    _check_cuda_bf16("k_cache", k_cache)
+    _check_cuda_bf16("v_cache", v_cache)
+    _need(k_cache.dim() == 4 and k_cache.shape[2] == NKV and k_cache.shape[3] == HD and k_cache.is_contiguous()
+          and v_cache.shape == k_cache.shape and v_cache.is_contiguous(),
+          "k_cache/v_cache must be contiguous [num_pages, page_size, 8, 128]")
+    _need(cache_seqlens.dtype == torch.int32 and cache_seqlens.is_cuda and cache_seqlens.numel() == B
+          and cache_seqlens.is_contiguous(), "cache_seqlens must be a contiguous int32 CUDA tensor [B]")
+    _need(block_table.dtype == torch.int32 and block_table.dim() == 2 and block_table.shape[0] == B
+          and block_table.stride(1) == 1, "block_table must be int32 [B, max_pages] with unit inner stride")
+    out = torch.empty(B, NH, HD, dtype=torch.bfloat16, device=qkv.device)
+    if B == 0:
+        return out
+    nr = _norm_rope(q_norm_w, k_norm_w, cos, sin, eps, B)
+    ws = workspace(B, num_splits, qkv.device)
+    with torch.cuda.device(qkv.device):
+        rc = lib.q3_paged_decode_qkv(
+            qkv.data_ptr(), qkv.stride(0), ctypes.byref(nr), k_cache.data_ptr(), v_cache.data_ptr(),
+            k_cache.shape[0], k_cache.shape[1], cache_seqlens.data_ptr(), block_table.data_ptr(),
+            block_table.stride(0), block_table.shape[1], B, NH, NKV, HD, float(softmax_scale), out.data_ptr(),
+            out.stride(0), ws.data_ptr(), ws.numel(), int(num_splits), _stream(qkv.device))
+    _lib.check(rc, "q3_paged_decode_qkv")
+    return out
+
+
+@paged_decode_qkv.register_fake
+def _(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, cache_seqlens, block_table, softmax_scale, eps=1e-6,
+      num_splits=0):
+    return qkv.new_empty(qkv.shape[0], NH, HD)
+
+
 def _rows(name, t, n_rows_dims=1):
     _check_cuda_bf16(name, t)
     _need(t.dim() >= 2 and t.shape[-1] == HD and t.shape[-2] == NKV and t.stride(-1) == 1 and t.stride(-2) == HD,
@@ -223,6 +286,36 @@ def cp_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, K: torch.Tensor, 
 @cp_step.register_fake
 def _(q, k, v, K, V, slot, softmax_scale):
     return q.new_empty(q.shape[0], NH * HD)
+
+
+@torch.library.custom_op("q3attn::cp_step_qkv", mutates_args=("K", "V"))
+def cp_step_qkv(qkv: torch.Tensor, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, cos: torch.Tensor,
+                sin: torch.Tensor, K: torch.Tensor, V: torch.Tensor, slot: int, softmax_scale: float,
+                eps: float = 1e-6) -> torch.Tensor:
+    """One code-predictor (step, layer) from the QKV projection (engine/code_predictor.py:40-41, 58, 46-47): q/k
+    RMSNorm + RoPE with the cos/sin row of slot p, K/V slot `slot` written, attention over slots 0..slot ->
+    [B, 2048]. One launch."""
+    lib = _lib.load()
+    qkv = _qkv_rows(qkv)
+    B = qkv.shape[0]
+    _check_cuda_bf16("K", K)
+    _check_cuda_bf16("V", V)
+    _need(K.dim() == 4 and K.shape[0] >= B and K.shape[1] == NKV and K.shape[3] == HD and K.stride(3) == 1
+          and V.shape == K.shape and V.stride(3) == 1, "K/V must be [B, 8, S, 128] with contiguous 128")
+    out = torch.empty(B, NH * HD, dtype=torch.bfloat16, device=qkv.device)
+    nr = _norm_rope(q_norm_w, k_norm_w, cos, sin, eps, B)
+    with torch.cuda.device(qkv.device):
+        rc = lib.q3_cp_step_qkv(qkv.data_ptr(), qkv.stride(0), ctypes.byref(nr), K.data_ptr(), V.data_ptr(),
+                                K.stride(0), K.stride(1), K.stride(2), V.stride(0), V.stride(1), V.stride(2), B,
+                                K.shape[2], int(slot), float(softmax_scale), out.data_ptr(), out.stride(0),
+                                _stream(qkv.device))
+    _lib.check(rc, "q3_cp_step_qkv")
+    return out
+
+
+@cp_step_qkv.register_fake
+def _(qkv, q_norm_w, k_norm_w, cos, sin, K, V, slot, softmax_scale, eps=1e-6):
+    return qkv.new_empty(qkv.shape[0], NH * HD)
 
 
 def _prefill_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale, causal, k_cache=None,

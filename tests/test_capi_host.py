@@ -77,6 +77,45 @@ def test_cp_rejects_bad_slot_counts_before_cuda():
     assert lib.q3_cp_attn(*args, 0, 16, 3, 0.1, 16, 2048, None) == _lib.Q3_OK               # empty batch
 
 
+def _norm_rope(qn=256, kn=512, cos=768, sin=1024, stride=128, eps=1e-6):
+    return _lib.QkNormRope(qn, kn, cos, sin, stride, eps)
+
+
+def _decode_qkv(nr, qkv=4096, stride=4096, batch=2):
+    lib = _lib.load()
+    return lib.q3_paged_decode_qkv(qkv, stride, nr, 8192, 8192 * 4, 10, 16, 64, 64, 4, 4, batch, 16, 8, 128, 0.1,
+                                   8192 * 8, 2048, 8192 * 16, 1 << 20, 0, None)
+
+
+def test_fused_decode_rejects_bad_norm_rope_before_cuda():
+    assert _decode_qkv(None) == _lib.Q3_ERR_INVALID                                        # no norm/rope struct
+    nr = _norm_rope()
+    assert _decode_qkv(ctypes.byref(nr), stride=2048) == _lib.Q3_ERR_INVALID               # row shorter than q|k|v
+    nr = _norm_rope(kn=None)
+    assert _decode_qkv(ctypes.byref(nr)) == _lib.Q3_ERR_INVALID                            # missing k weight
+    nr = _norm_rope(stride=-128)
+    assert _decode_qkv(ctypes.byref(nr)) == _lib.Q3_ERR_INVALID                            # negative rope stride
+    nr = _norm_rope(cos=770)
+    assert _decode_qkv(ctypes.byref(nr)) == _lib.Q3_ERR_ALIGNMENT                          # cos row not 8-byte aligned
+    nr = _norm_rope()
+    assert _decode_qkv(ctypes.byref(nr), batch=0) == _lib.Q3_OK                           # empty batch is a no-op
+
+
+def test_fused_cp_step_rejects_bad_norm_rope_before_cuda():
+    lib = _lib.load()
+    strides = (16384, 2048, 128, 16384, 2048, 128)
+    assert lib.q3_cp_step_qkv(4096, 4096, None, 8192, 8192, *strides, 4, 16, 2, 0.1, 8192, 2048, None) == \
+        _lib.Q3_ERR_INVALID
+    nr = _norm_rope()
+    assert lib.q3_cp_step_qkv(4096, 2048, ctypes.byref(nr), 8192, 8192, *strides, 4, 16, 2, 0.1, 8192, 2048,
+                              None) == _lib.Q3_ERR_INVALID                                  # row shorter than q|k|v
+    assert lib.q3_cp_step_qkv(4096, 4096, ctypes.byref(nr), 8192, 8192, *strides, 4, 16, 16, 0.1, 8192, 2048,
+                              None) == _lib.Q3_ERR_INVALID                                  # slot 16 of 16
+    nr = _norm_rope(sin=1030)
+    assert lib.q3_cp_step_qkv(4096, 4096, ctypes.byref(nr), 8192, 8192, *strides, 4, 16, 2, 0.1, 8192, 2048,
+                              None) == _lib.Q3_ERR_ALIGNMENT
+
+
 def test_append_rejects_bad_arguments_before_cuda():
     lib = _lib.load()
     assert lib.q3_kv_append_slots(16, 16, 1024, 16, 16, 0, 8, 128, 16, 4, None) == _lib.Q3_ERR_INVALID   # no pool
