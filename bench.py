@@ -55,7 +55,9 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--cpu-seats", type=int, default=48)
-    p.add_argument("--workload", choices=["c2", "c3", "c4"], default="c2",
+    p.add_argument("--kernel-breakdown", action="store_true",
+                   help="c5: add the per-kernel device time of one replayed frame (CUPTI via torch.profiler)")
+    p.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2",
                    help="c2: the headline decode step (default); c3: 1.7B decode + chunked-prefill mix; c4: CP steps")
     return p.parse_args()
 
@@ -223,6 +225,136 @@ def config_dict(a, world):
 
 
 # ----------------------------------------------------------------------------------------------------- our arm
+def bench_frame(a):
+    """Config 5 on one GPU: the whole frame step (28-layer talker decode with the fused q/k norm + RoPE + append +
+    paged attention, codebook-0 logits and sampling, the code predictor's 16 steps x 5 layers) for 576 seats on
+    random-init 0.6B weights, ctx U[200,1200], page 16, shuffled page table, greedy (top_k = 1). Device time per frame
+    over CUDA-graph replays (inputs resident; the 80 GB of pools exceed L2), then end to end through Talker.step (seat
+    ids from the host, the frame's codes read back every frame), then the same frame with the q/k norm and RoPE as
+    separate PyTorch ops for comparison."""
+    import q3attn
+    from q3attn import synth, weights
+    from q3attn.frame import Talker
+    rank, local, world = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pg = None
+    if world > 1:        # seats shard with no exchange: the group only carries the start barrier and the max of times
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        pg = dist
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    B, page = a.seats, 16
+    steps = min(a.steps, 40)                      # every frame appends one token per seat: bounded by the pool room
+    seat_len = 1280                               # ctx <= 1200 plus room for 80 appended frames
+    W = weights.cast(weights.random_weights(a.seed, "0.6B", max_pos=seat_len + 16), torch.bfloat16, dev)
+    lay = synth.paged_layout(a.seed + 7919 * rank, B + 1, 200, 1200, page, seat_len // page)
+    gen = torch.Generator(device=dev).manual_seed(a.seed * 1000 + rank)
+
+    def build(fuse):
+        t = Talker(W, B, seat_len=seat_len, buckets=[B], page=page, block_table=lay.block_table, top_k=1,
+                   fuse_qk_norm_rope=fuse)
+        for l in range(len(W.layers)):
+            t.kc[l].normal_(0.0, 0.5, generator=gen)
+            t.vc[l].normal_(0.0, 0.5, generator=gen)
+        t.pos[:B] = lay.ctx[:B].to(dev, torch.int64)
+        t.x_in.normal_(0.0, 1.0, generator=gen)
+        t.capture([B])
+        t.s_seat[:B] = torch.arange(B, device=dev)
+        return t
+
+    def device_ms(t):
+        pos0 = t.pos.clone()
+        g = t.graphs[B]
+        for _ in range(a.warmup):
+            g.replay()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            g.replay()
+        e1.record()
+        e1.synchronize()
+        barrier()
+        t.pos.copy_(pos0)
+        if q3attn._lib.read_status():
+            raise RuntimeError("device status raised during the frame")
+        return reduce_max(e0.elapsed_time(e1) / steps, pg, dev)
+
+    t = build(True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms = device_ms(t)
+    clk = clocks.stop()
+    e2e = None
+    if not a.no_e2e:
+        seats = list(range(B))
+        pos0 = t.pos.clone()
+        for _ in range(a.warmup):
+            t.step(seats).cpu()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            codes = t.step(seats).cpu()
+        e2e_s = reduce_max((time.perf_counter() - t0) / steps, pg, dev)
+        barrier()
+        t.pos.copy_(pos0)
+        assert codes.shape == (B, 16)
+        e2e = {"value": B * world / e2e_s, "unit": "seat-frames/s", "h2d_bytes_per_step": 8 * B,
+               "d2h_bytes_per_step": 8 * 16 * B, "ms_per_frame": e2e_s * 1e3}
+    breakdown = None
+    if a.kernel_breakdown and rank == 0:
+        breakdown = frame_kernel_breakdown(t.graphs[B], t)
+    del t
+    torch.cuda.empty_cache()
+    t = build(False)
+    ms_unfused = device_ms(t)
+    del t
+    torch.cuda.empty_cache()
+    if pg is not None:
+        pg.destroy_process_group()
+    if rank != 0:
+        return
+    print(json.dumps({"metric": "e2e frame seat-frames/s @576 seats/GPU (0.6B random-init, greedy)", "workload": "c5",
+                      "value": B * world / (ms / 1e3), "unit": "seat-frames/s", "n_gpus": world, "steps": steps,
+                      "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16",
+                      "scaling": "weak", "data": "synthetic (random-init weights N(0,0.02); K/V pools N(0,0.5); "
+                      "ctx U[200,1200])",
+                      "config": {"workload": "C5 frame: 28 talker layers + cb0 sampling + 16 CP steps x 5 layers",
+                                 "seats": B, "page_size": page, "seat_len": seat_len, "sampling": "greedy (top_k=1)"},
+                      "e2e": e2e, "unfused_qk_norm_rope_ms_per_frame": ms_unfused,
+                      "fusion_saves_ms_per_frame": ms_unfused - ms, "clocks": clk,
+                      "kernel_breakdown": breakdown}), flush=True)
+
+
+def frame_kernel_breakdown(graph, talker, top=16):
+    """Per-kernel device time of two replays of a captured frame (CUPTI activity records through torch.profiler),
+    as [name, us per frame, launches per frame, share]; the frame's positions are restored afterwards."""
+    from torch.profiler import ProfilerActivity, profile
+    pos0 = talker.pos.clone()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+    talker.pos.copy_(pos0)
+    agg = {}
+    for e in prof.events():
+        if e.device_type.name == "CUDA":
+            n, us = agg.get(e.name, (0, 0.0))
+            agg[e.name] = (n + 1, us + e.device_time_total)
+    total = sum(v[1] for v in agg.values())
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][1])[:top]
+    return {"total_us_per_frame": total / 2, "launches_per_frame": sum(v[0] for v in agg.values()) // 2,
+            "top": [[k[:90], round(v[1] / 2, 1), v[0] // 2, round(v[1] / total, 4)] for k, v in rows]}
+
+
 def bench_aux(a):
     """Configs 3 and 4 (reported in DESIGN, not the headline): device time per layer on one GPU, CUDA events over
     graph replays, inputs resident; L2 is not flushed for c4 (its 38 MB per-layer scratch is L2-resident by design)."""
@@ -314,6 +446,8 @@ def bench_aux(a):
 
 def main():
     a = parse()
+    if a.workload == "c5" and a.impl == "ours":
+        return bench_frame(a)
     if a.workload != "c2" and a.impl == "ours":
         return bench_aux(a)
     if a.impl == "reference":

@@ -33,6 +33,16 @@ def rope(x, cos, sin):
     return x * cos + torch.cat((-x[..., h:], x[..., :h]), dim=-1) * sin
 
 
+def _split_qkv(qkv, w, cos, sin, B, nh, nkv, hd):
+    """q, k, v of one layer with the norms and RoPE as PyTorch ops (engine/talker.py:69-71,
+    engine/code_predictor.py:40-42); k and v come back with one shared row stride."""
+    nq, nk = nh * hd, nkv * hd
+    q = rope(rms(qkv[:, :nq].view(B, nh, hd), w.qn), cos, sin)
+    k = rope(rms(qkv[:, nq:nq + nk].view(B, nkv, hd), w.kn), cos, sin)
+    v = qkv[:, nq + nk:].contiguous().view(B, nkv, hd)
+    return q, k.contiguous(), v
+
+
 def mlp(x, w, ffn: int):
     """engine/ops.py:63-65."""
     gu = F.linear(x, w.gu)
@@ -50,8 +60,9 @@ def sample_topk(logits, temperature: float, k: int, gen):
 class CodePredictor:
     """engine/code_predictor.py:14-72 with the attention and slot write of each (step, layer) in one q3attn.cp_step."""
 
-    def __init__(self, W, max_bs, temperature=0.9, top_k=50):
+    def __init__(self, W, max_bs, temperature=0.9, top_k=50, fuse_qk_norm_rope=True):
         self.W, self.L = W, len(W.cp_layers)
+        self.fuse = fuse_qk_norm_rope
         self.nh, self.nkv, self.hd = 16, 8, W.head_dim
         self.ffn, self.scale = W.cp_ffn, float(W.head_dim) ** -0.5
         self.temperature, self.top_k = temperature, top_k
@@ -68,8 +79,12 @@ class CodePredictor:
         for l in range(self.L):
             w = W.cp_layers[l]
             qkv = F.linear(rms(x, w.ln1), w.qkv)                                        # code_predictor.py:39
-            o = ops.cp_step_qkv(qkv, w.qn, w.kn, cos, sin, self.K[l, :B], self.V[l, :B], p,  # :40-42, 58, 46-47
-                                self.scale)
+            if self.fuse:
+                o = ops.cp_step_qkv(qkv, w.qn, w.kn, cos, sin, self.K[l, :B], self.V[l, :B], p,  # :40-42, 58, 46-47
+                                    self.scale)
+            else:   # the same maths with the q/k norm and RoPE as separate PyTorch ops
+                q, k, v = _split_qkv(qkv, w, cos, sin, B, self.nh, self.nkv, self.hd)
+                o = ops.cp_step(q, k, v, self.K[l, :B], self.V[l, :B], p, self.scale)
             x = x + F.linear(o, w.o)
             gu = F.linear(rms(x, w.ln2), w.gu)
             x = x + F.linear(F.silu(gu[..., :self.ffn]) * gu[..., self.ffn:], w.down)
@@ -108,10 +123,11 @@ class Talker:
     """engine/talker.py:20-138 over paged K/V pools and the q3attn kernels.
 
     block_table: int32 [n_seats + 1, seat_len // page] (the last row is the scratch seat padded rows point at,
-    talker.py:29); default = identity pages."""
+    talker.py:29); default = identity pages. fuse_qk_norm_rope=False runs the q/k norms and RoPE as separate
+    PyTorch ops ahead of the attention kernels (same maths; kept to measure what the fusion saves)."""
 
     def __init__(self, W, n_seats, seat_len=768, buckets=None, page=16, block_table=None, max_text=16,
-                 temperature=0.9, top_k=50, rep_penalty=1.05, min_new=2, seed=0):
+                 temperature=0.9, top_k=50, rep_penalty=1.05, min_new=2, seed=0, fuse_qk_norm_rope=True):
         assert seat_len % page == 0
         self.W = W
         d, dt = W.device, W.dtype
@@ -147,7 +163,9 @@ class Talker:
         self.max_bs = self.buckets[-1]
         self.s_seat = torch.full((self.max_bs,), n_seats, dtype=torch.int64, device=d)
         self.o_codes = torch.zeros(self.max_bs, 16, dtype=torch.int64, device=d)
-        self.cp = CodePredictor(W, self.max_bs, temperature=temperature, top_k=top_k)
+        self.fuse = fuse_qk_norm_rope
+        self.cp = CodePredictor(W, self.max_bs, temperature=temperature, top_k=top_k,
+                                fuse_qk_norm_rope=fuse_qk_norm_rope)
         self.graphs = {}
         self.pool = None
 
@@ -160,8 +178,12 @@ class Talker:
         for l in range(len(self.W.layers)):
             w = self.W.layers[l]
             qkv = F.linear(rms(x, w.ln1), w.qkv)                                           # talker.py:68
-            o = ops.paged_decode_qkv(qkv, w.qn, w.kn, cos, sin, self.kc[l], self.vc[l], seqlens, bt,  # :69-77
-                                     self.scale)
+            if self.fuse:
+                o = ops.paged_decode_qkv(qkv, w.qn, w.kn, cos, sin, self.kc[l], self.vc[l], seqlens, bt,  # :69-77
+                                         self.scale)
+            else:
+                q, k, v = _split_qkv(qkv, w, cos, sin, B, self.nh, self.nkv, self.hd)
+                o = ops.paged_decode_append(q, k, v, self.kc[l], self.vc[l], seqlens, bt, self.scale, 0)
             x = x + F.linear(o.reshape(B, nq), w.o)
             x = x + mlp(rms(x, w.ln2), w, self.ffn)
         return rms(x, self.W.norm)
