@@ -230,8 +230,8 @@ def bench_frame(a):
     paged attention, codebook-0 logits and sampling, the code predictor's 16 steps x 5 layers) for 576 seats on
     random-init 0.6B weights, ctx U[200,1200], page 16, shuffled page table, greedy (top_k = 1). Device time per frame
     over CUDA-graph replays (inputs resident; the 80 GB of pools exceed L2), then end to end through Talker.step (seat
-    ids from the host, the frame's codes read back every frame), then the same frame with the q/k norm and RoPE as
-    separate PyTorch ops for comparison."""
+    ids from the host, the frame's codes read back every frame), then the same frame with the q/k norm + RoPE and the
+    logit processing + sampling as PyTorch ops, for comparison."""
     import q3attn
     from q3attn import synth, weights
     from q3attn.frame import Talker
@@ -259,7 +259,7 @@ def bench_frame(a):
 
     def build(fuse):
         t = Talker(W, B, seat_len=seat_len, buckets=[B], page=page, block_table=lay.block_table, top_k=1,
-                   fuse_qk_norm_rope=fuse)
+                   fuse_qk_norm_rope=fuse, fused_sampler=fuse)
         for l in range(len(W.layers)):
             t.kc[l].normal_(0.0, 0.5, generator=gen)
             t.vc[l].normal_(0.0, 0.5, generator=gen)
@@ -328,7 +328,8 @@ def bench_frame(a):
                       "ctx U[200,1200])",
                       "config": {"workload": "C5 frame: 28 talker layers + cb0 sampling + 16 CP steps x 5 layers",
                                  "seats": B, "page_size": page, "seat_len": seat_len, "sampling": "greedy (top_k=1)"},
-                      "e2e": e2e, "unfused_qk_norm_rope_ms_per_frame": ms_unfused,
+                      "e2e": e2e, "unfused_ms_per_frame": ms_unfused,
+                      "unfused": "q/k RMSNorm + RoPE and cb0 processing + top-k sampling as PyTorch ops",
                       "fusion_saves_ms_per_frame": ms_unfused - ms, "clocks": clk,
                       "kernel_breakdown": breakdown}), flush=True)
 

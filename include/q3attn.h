@@ -185,6 +185,43 @@ int q3_cp_step_qkv(const void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
                    int32_t batch, int32_t n_slots, int32_t slot, float softmax_scale,
                    void* out, int64_t out_batch_stride, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * Logit processing + top-k / temperature sampling, one call per sampled token of a frame. Replaces
+ * Talker._cb0_logits (engine/talker.py:90-94: repetition penalty over the seat's `seen` row, + suppress row, EOS masked
+ * while ngen < min_new), sample_topk (engine/ops.py:68-76: topk, softmax(vals / temperature), multinomial) and the
+ * embedding lookup of the sampled id (engine/code_predictor.py:68, 71). top_k = 1 is greedy (the maximum; equal maxima
+ * resolve to the lowest index). The random stream is Philox4x32-10 keyed by `seed`, counter (row, launch index); the
+ * launch index lives in rng_state[0] on the device and advances by one per call (CUDA-graph replays included), so
+ * draws are reproducible from (seed, rng_state) but are not torch.multinomial's stream. Optional parts are switched off
+ * with null pointers. */
+typedef struct q3_sampler {
+  const void* logits;          /* [batch, vocab] rows, row_stride elements apart */
+  int32_t logits_dtype;        /* 0 = bf16, 1 = fp32 */
+  int64_t row_stride;
+  int32_t batch;
+  int32_t vocab;               /* <= 4096 */
+  int32_t top_k;               /* 1..min(64, vocab) */
+  float temperature;           /* > 0 when top_k > 1 */
+  const uint8_t* seen;         /* optional [*, vocab] bool rows: repetition penalty on seen ids (row = seat[b]) */
+  int64_t seen_row_stride;
+  const int64_t* seat;         /* [batch]: row of seen / ngen for each batch row (required with seen or ngen) */
+  float repetition_penalty;
+  const float* bias;           /* optional [vocab] fp32 added after the penalty (the suppress row) */
+  const int64_t* ngen;         /* optional: EOS (eos_id) masked to -inf while ngen[seat[b]] < min_new */
+  int32_t min_new;
+  int32_t eos_id;
+  uint64_t seed;
+  uint64_t* rng_state;         /* device [2] uint64, zero-initialised once by the caller; one stream per state */
+  int64_t* out_ids;            /* [batch] sampled ids, out_stride elements apart */
+  int64_t out_stride;
+  const void* emb;             /* optional [>= vocab rows, emb_dim] bf16 table: row out_ids[b] -> emb_out row b */
+  int64_t emb_row_stride;
+  int32_t emb_dim;
+  void* emb_out;
+  int64_t emb_out_row_stride;
+} q3_sampler;
+int q3_sample_topk(const q3_sampler* sampler, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -398,6 +398,51 @@ int q3_cp_step_qkv(const void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
                    v_head_stride, v_slot_stride, batch, n_slots, slot + 1, softmax_scale, out, out_batch_stride, stream);
 }
 
+int q3_sample_topk(const q3_sampler* p, void* stream) {
+  if (!p) return Q3_ERR_INVALID;
+  if (p->batch < 0) return Q3_ERR_INVALID;
+  if (p->batch == 0) return Q3_OK;
+  if (p->vocab < 1 || p->vocab > 4096 || p->top_k < 1 || p->top_k > q3::kSampleMaxTopK || p->top_k > p->vocab)
+    return p->vocab > 4096 || p->top_k > q3::kSampleMaxTopK ? Q3_ERR_UNSUPPORTED : Q3_ERR_INVALID;
+  if (p->top_k > 1 && !(p->temperature > 0.f)) return Q3_ERR_INVALID;
+  if (!p->logits || !p->rng_state || !p->out_ids || (p->logits_dtype != 0 && p->logits_dtype != 1)) return Q3_ERR_INVALID;
+  if (p->row_stride < p->vocab || p->out_stride < 1) return Q3_ERR_INVALID;
+  if ((p->seen || p->ngen) && !p->seat) return Q3_ERR_INVALID;
+  if (p->seen && p->seen_row_stride < p->vocab) return Q3_ERR_INVALID;
+  if (p->emb && (!p->emb_out || p->emb_dim <= 0 || p->emb_row_stride < p->emb_dim || p->emb_out_row_stride < p->emb_dim))
+    return Q3_ERR_INVALID;
+  if (!aligned(p->rng_state, 8) || (p->emb && (!aligned(p->emb, 8) || !aligned(p->emb_out, 8) || (p->emb_dim % 4) ||
+                                              (p->emb_row_stride % 4) || (p->emb_out_row_stride % 4))))
+    return Q3_ERR_ALIGNMENT;
+  if (p->batch > 2147483647) return Q3_ERR_INVALID;
+  q3::SampleArgs a{};
+  a.logits = p->logits;
+  a.logits_bf16 = p->logits_dtype == 0;
+  a.row_stride = p->row_stride;
+  a.B = p->batch;
+  a.V = p->vocab;
+  a.k = p->top_k;
+  a.inv_temp = p->top_k > 1 ? 1.f / p->temperature : 1.f;
+  a.seen = p->seen;
+  a.seen_stride = p->seen_row_stride;
+  a.seat = p->seat;
+  a.rep = p->repetition_penalty;
+  a.bias = p->bias;
+  a.ngen = p->ngen;
+  a.min_new = p->min_new;
+  a.eos = p->eos_id;
+  a.seed = p->seed;
+  a.rng_state = reinterpret_cast<unsigned long long*>(p->rng_state);
+  a.out_ids = p->out_ids;
+  a.out_stride = p->out_stride;
+  a.emb = static_cast<const __nv_bfloat16*>(p->emb);
+  a.emb_stride = p->emb_row_stride;
+  a.emb_dim = p->emb_dim;
+  a.emb_out = static_cast<__nv_bfloat16*>(p->emb_out);
+  a.emb_out_stride = p->emb_out_row_stride;
+  return record(q3::launch_sample_topk(a, static_cast<cudaStream_t>(stream)));
+}
+
 int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v, int64_t kv_row_stride,
                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t num_seqs, int32_t max_seqlen_q,
                const int32_t* prefix_lens, const int32_t* seat_ids, void* k_pool, void* v_pool, int32_t num_pages,

@@ -92,6 +92,33 @@ struct CpArgs {
 
 cudaError_t launch_cp_attn(const CpArgs& a, cudaStream_t stream);
 
+constexpr int kSampleMaxTopK = 64;
+struct SampleArgs {
+  const void* logits;              // [B, V] rows (bf16 or fp32), row stride row_stride (elements)
+  int logits_bf16;
+  long long row_stride;
+  int B, V, k;                     // V <= 4096, 1 <= k <= min(64, V)
+  float inv_temp;
+  const uint8_t* seen;             // optional [S, V] bool rows (repetition penalty), row = seat[b]
+  long long seen_stride;
+  const int64_t* seat;             // [B] row of seen / ngen for batch row b (needed with seen or ngen)
+  float rep;
+  const float* bias;               // optional [V] additive (the suppress row)
+  const int64_t* ngen;             // optional [S]: EOS is masked while ngen[seat[b]] < min_new
+  int min_new, eos;
+  unsigned long long seed;
+  unsigned long long* rng_state;   // device [2]: launch index, finish ticket
+  int64_t* out_ids;                // [B] at stride out_stride
+  long long out_stride;
+  const __nv_bfloat16* emb;        // optional [*, emb_dim] table: row out_ids[b] copied to emb_out row b
+  long long emb_stride;
+  int emb_dim;
+  __nv_bfloat16* emb_out;
+  long long emb_out_stride;
+};
+
+cudaError_t launch_sample_topk(const SampleArgs& a, cudaStream_t stream);
+
 struct PrefillArgs {
   const __nv_bfloat16* q;          // [Tq, 16, 128] rows, row stride q_stride (elements)
   long long q_stride;

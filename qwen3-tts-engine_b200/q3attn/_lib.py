@@ -22,6 +22,15 @@ class QkNormRope(ctypes.Structure):
 
 _NR = ctypes.POINTER(QkNormRope)
 
+
+class Sampler(ctypes.Structure):
+    """struct q3_sampler (include/q3attn.h): logit processing + top-k sampling of one batch of rows."""
+    _fields_ = [("logits", _P), ("logits_dtype", _I32), ("row_stride", _I64), ("batch", _I32), ("vocab", _I32),
+                ("top_k", _I32), ("temperature", _F32), ("seen", _P), ("seen_row_stride", _I64), ("seat", _P),
+                ("repetition_penalty", _F32), ("bias", _P), ("ngen", _P), ("min_new", _I32), ("eos_id", _I32),
+                ("seed", ctypes.c_uint64), ("rng_state", _P), ("out_ids", _P), ("out_stride", _I64), ("emb", _P),
+                ("emb_row_stride", _I64), ("emb_dim", _I32), ("emb_out", _P), ("emb_out_row_stride", _I64)]
+
 # name -> (restype, argtypes); every symbol include/q3attn.h declares
 SIGNATURES = {
     "q3_version": (ctypes.c_int, []),
@@ -47,6 +56,7 @@ SIGNATURES = {
                                   _P, _I64, _P]),
     "q3_cp_step": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
                                   _I32, _F32, _P, _I64, _P]),
+    "q3_sample_topk": (ctypes.c_int, [ctypes.POINTER(Sampler), _P]),
     "q3_cp_step_qkv": (ctypes.c_int, [_P, _I64, _NR, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
                                       _I32, _F32, _P, _I64, _P]),
 }

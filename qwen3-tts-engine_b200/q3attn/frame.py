@@ -60,9 +60,10 @@ def sample_topk(logits, temperature: float, k: int, gen):
 class CodePredictor:
     """engine/code_predictor.py:14-72 with the attention and slot write of each (step, layer) in one q3attn.cp_step."""
 
-    def __init__(self, W, max_bs, temperature=0.9, top_k=50, fuse_qk_norm_rope=True):
+    def __init__(self, W, max_bs, temperature=0.9, top_k=50, fuse_qk_norm_rope=True, fused_sampler=True):
         self.W, self.L = W, len(W.cp_layers)
         self.fuse = fuse_qk_norm_rope
+        self.fused_sampler = fused_sampler
         self.nh, self.nkv, self.hd = 16, 8, W.head_dim
         self.ffn, self.scale = W.cp_ffn, float(W.head_dim) ** -0.5
         self.temperature, self.top_k = temperature, top_k
@@ -90,18 +91,23 @@ class CodePredictor:
             x = x + F.linear(F.silu(gu[..., :self.ffn]) * gu[..., self.ffn:], w.down)
         return rms(x, W.cp_norm)
 
-    def run(self, h, c0, gen):
-        """code_predictor.py:62-72."""
+    def run(self, h, c0, gen, e0=None):
+        """code_predictor.py:62-72. gen: the talker's SamplerRng (fused sampler) or torch.Generator; e0: codec_emb[c0]
+        when the caller already has it."""
         W = self.W
         B = h.shape[0]
         self._s(self.proj(h), B, 0)
-        e = W.codec_emb[c0]
+        e = W.codec_emb[c0] if e0 is None else e0
         embs, codes = [e], []
         for i in range(15):
             hid = self._s(self.proj(e), B, i + 1)
-            c = sample_topk(F.linear(hid, W.cp_head[i]).float(), self.temperature, self.top_k, gen)
+            if self.fused_sampler:   # top-k draw + cp_emb[i][c] in one launch (code_predictor.py:70-71)
+                c, e = ops.sample_topk(F.linear(hid, W.cp_head[i]), self.temperature, self.top_k, gen,
+                                       emb=W.cp_emb[i])
+            else:
+                c = sample_topk(F.linear(hid, W.cp_head[i]).float(), self.temperature, self.top_k, gen)
+                e = W.cp_emb[i][c]
             codes.append(c)
-            e = W.cp_emb[i][c]
             embs.append(e)
         return torch.stack(codes, 1), torch.stack(embs, 1).sum(1)
 
@@ -124,10 +130,12 @@ class Talker:
 
     block_table: int32 [n_seats + 1, seat_len // page] (the last row is the scratch seat padded rows point at,
     talker.py:29); default = identity pages. fuse_qk_norm_rope=False runs the q/k norms and RoPE as separate
-    PyTorch ops ahead of the attention kernels (same maths; kept to measure what the fusion saves)."""
+    PyTorch ops ahead of the attention kernels, and fused_sampler=False samples with PyTorch ops and torch's generator
+    instead of q3attn.sample_topk (same maths, another random stream; both kept to measure what the fusions save)."""
 
     def __init__(self, W, n_seats, seat_len=768, buckets=None, page=16, block_table=None, max_text=16,
-                 temperature=0.9, top_k=50, rep_penalty=1.05, min_new=2, seed=0, fuse_qk_norm_rope=True):
+                 temperature=0.9, top_k=50, rep_penalty=1.05, min_new=2, seed=0, fuse_qk_norm_rope=True,
+                 fused_sampler=True):
         assert seat_len % page == 0
         self.W = W
         d, dt = W.device, W.dtype
@@ -159,13 +167,15 @@ class Talker:
         self.eos_col[W.eos] = True
         self.gen = torch.Generator(device=d)
         self.gen.manual_seed(seed)
+        self.fused_sampler = fused_sampler
+        self.rng = ops.SamplerRng(seed, d)       # the fused sampler's device random stream
         self.buckets = sorted(set(buckets or [1, 2, 4, 8, 16, 32, 64, 128, 256]))
         self.max_bs = self.buckets[-1]
         self.s_seat = torch.full((self.max_bs,), n_seats, dtype=torch.int64, device=d)
         self.o_codes = torch.zeros(self.max_bs, 16, dtype=torch.int64, device=d)
         self.fuse = fuse_qk_norm_rope
         self.cp = CodePredictor(W, self.max_bs, temperature=temperature, top_k=top_k,
-                                fuse_qk_norm_rope=fuse_qk_norm_rope)
+                                fuse_qk_norm_rope=fuse_qk_norm_rope, fused_sampler=fused_sampler)
         self.graphs = {}
         self.pool = None
 
@@ -196,11 +206,16 @@ class Talker:
 
     def _tail(self, h, seat):
         """talker.py:96-105."""
-        c0 = sample_topk(self._cb0_logits(h, seat), self.temperature, self.top_k, self.gen)
+        if self.fused_sampler:   # _cb0_logits' processing, the top-k draw and codec_emb[c0] in one launch
+            c0, e0 = ops.sample_topk(F.linear(h, self.W.codec_head), self.temperature, self.top_k, self.rng,
+                                     seen=self.seen, seat=seat, rep_penalty=self.rep, bias=self.suppress,
+                                     ngen=self.ngen, min_new=self.min_new, eos=self.W.eos, emb=self.W.codec_emb)
+        else:
+            c0, e0 = sample_topk(self._cb0_logits(h, seat), self.temperature, self.top_k, self.gen), None
         g = self.ngen[seat]
         self.seen.index_put_((seat, c0), self.eos_col.new_ones(()).expand_as(c0))
         self.ngen.index_copy_(0, seat, g + 1)
-        codes, acc = self.cp.run(h, c0, self.gen)
+        codes, acc = self.cp.run(h, c0, self.rng if self.fused_sampler else self.gen, e0)
         t = self.trail[seat, torch.minimum(g, self.trail_len[seat])]
         self.x_in.index_copy_(0, seat, acc + t)
         return torch.cat([c0[:, None], codes], 1)

@@ -318,6 +318,82 @@ def _(qkv, q_norm_w, k_norm_w, cos, sin, K, V, slot, softmax_scale, eps=1e-6):
     return qkv.new_empty(qkv.shape[0], NH * HD)
 
 
+class SamplerRng:
+    """One random stream of q3attn.sample_topk: a seed and a device state [launch index, finish ticket] (int64 x 2)
+    that each sampling launch advances by one, CUDA-graph replays included. Draws are Philox4x32-10 of counter
+    (row, launch index) under key = seed; they are reproducible from (seed, state) but are not torch's stream."""
+
+    def __init__(self, seed: int, device):
+        self.seed = int(seed)
+        self.state = torch.zeros(2, dtype=torch.int64, device=device)
+
+    @property
+    def launch_index(self) -> int:
+        return int(self.state[0])
+
+
+@torch.library.custom_op("q3attn::sample_topk", mutates_args=("rng_state",))
+def _sample_topk_op(logits: torch.Tensor, temperature: float, top_k: int, seed: int, rng_state: torch.Tensor,
+                    seen: Optional[torch.Tensor], seat: Optional[torch.Tensor], rep_penalty: float,
+                    bias: Optional[torch.Tensor], ngen: Optional[torch.Tensor], min_new: int, eos: int,
+                    emb: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor]:
+    lib = _lib.load()
+    _need(logits.is_cuda and logits.dim() == 2 and logits.stride(1) == 1 and
+          logits.dtype in (torch.bfloat16, torch.float32), "logits must be CUDA [B, V] rows, bf16 or fp32")
+    B, V = logits.shape
+    dev = logits.device
+    _need(rng_state.is_cuda and rng_state.dtype == torch.int64 and rng_state.numel() == 2 and
+          rng_state.is_contiguous(), "rng_state must be a CUDA int64 [2] tensor (SamplerRng.state)")
+    if seen is not None:
+        _need(seen.is_cuda and seen.dtype == torch.bool and seen.dim() == 2 and seen.shape[1] == V and
+              seen.stride(1) == 1, "seen must be a CUDA bool [S, V] tensor")
+    if seen is not None or ngen is not None:
+        _need(seat is not None and seat.is_cuda and seat.dtype == torch.int64 and seat.numel() == B and
+              seat.is_contiguous(), "seat must be a contiguous CUDA int64 [B] tensor")
+    if bias is not None:
+        _need(bias.is_cuda and bias.dtype == torch.float32 and bias.numel() == V and bias.is_contiguous(),
+              "bias must be a contiguous CUDA fp32 [V] tensor")
+    if ngen is not None:
+        _need(ngen.is_cuda and ngen.dtype == torch.int64 and ngen.is_contiguous(), "ngen must be CUDA int64")
+    ids = torch.empty(B, dtype=torch.int64, device=dev)
+    if emb is not None:
+        _check_cuda_bf16("emb", emb)
+        _need(emb.dim() == 2 and emb.stride(1) == 1 and emb.shape[0] >= V and emb.shape[1] % 4 == 0,
+              "emb must be a [rows >= V, dim] bf16 table with dim a multiple of 4")
+        emb_out = torch.empty(B, emb.shape[1], dtype=torch.bfloat16, device=dev)
+    else:
+        emb_out = torch.empty(0, dtype=torch.bfloat16, device=dev)
+    p = _lib.Sampler(logits.data_ptr(), 0 if logits.dtype == torch.bfloat16 else 1, logits.stride(0), B, V,
+                     int(top_k), float(temperature), _ptr(seen), seen.stride(0) if seen is not None else 0,
+                     _ptr(seat), float(rep_penalty), _ptr(bias), _ptr(ngen), int(min_new), int(eos),
+                     int(seed) & 0xFFFFFFFFFFFFFFFF, rng_state.data_ptr(), ids.data_ptr(), 1, _ptr(emb),
+                     emb.stride(0) if emb is not None else 0, emb.shape[1] if emb is not None else 0,
+                     emb_out.data_ptr() if emb is not None else None, emb_out.stride(0) if emb is not None else 0)
+    with torch.cuda.device(dev):
+        rc = lib.q3_sample_topk(ctypes.byref(p), _stream(dev))
+    _lib.check(rc, "q3_sample_topk")
+    return ids, emb_out
+
+
+@_sample_topk_op.register_fake
+def _(logits, temperature, top_k, seed, rng_state, seen, seat, rep_penalty, bias, ngen, min_new, eos, emb):
+    B = logits.shape[0]
+    e = logits.new_empty(B, emb.shape[1], dtype=torch.bfloat16) if emb is not None else \
+        logits.new_empty(0, dtype=torch.bfloat16)
+    return logits.new_empty(B, dtype=torch.int64), e
+
+
+def sample_topk(logits, temperature: float, k: int, rng: SamplerRng, *, seen=None, seat=None, rep_penalty=1.0,
+                bias=None, ngen=None, min_new=0, eos=-1, emb=None):
+    """engine/ops.py:68-76 (top-k, softmax(vals / temperature), one draw) on the GPU, with the optional logit
+    processing of engine/talker.py:91-94 applied first (repetition penalty over seen[seat[b]], + bias, EOS masked while
+    ngen[seat[b]] < min_new) and the optional embedding lookup of the sampled ids after. logits [B, V] bf16 or fp32
+    (V <= 4096, k <= 64). Returns ids [B] int64, or (ids, emb[ids]) when emb is given. One launch."""
+    ids, e = _sample_topk_op(logits, float(temperature), int(k), rng.seed, rng.state, seen, seat, float(rep_penalty),
+                             bias, ngen, int(min_new), int(eos), emb)
+    return (ids, e) if emb is not None else ids
+
+
 def _prefill_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale, causal, k_cache=None,
                   v_cache=None, prefix_lens=None, seat_ids=None, block_table=None, write_kv=False):
     lib = _lib.load()

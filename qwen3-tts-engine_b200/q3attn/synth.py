@@ -131,6 +131,21 @@ def prefill_case(seed: int, lens, prefix_lens=None, scale: float = 0.5, dtype=to
     return out
 
 
+def sampler_case(seed: int, B: int = 24, S: int = 30, V: int = 3072, eos: int = 2150, scale: float = 3.0):
+    """Inputs of one codebook-0 sampling call (engine/talker.py:90-97): bf16-representable fp32 logits [B, V], a
+    `seen` table [S, V] (5% set), distinct seats [B], ngen [S] in 0..3, and the reference's suppress row (ids
+    >= V - 1024 at -inf except EOS, talker.py:43)."""
+    g = cpu_gen(seed + 3000)
+    logits = (torch.randn(B, V, generator=g) * scale).to(torch.bfloat16).float()
+    seen = torch.rand(S, V, generator=g) < 0.05
+    seat = torch.randperm(S, generator=g)[:B].to(torch.int64)
+    ngen = torch.randint(0, 4, (S,), generator=g, dtype=torch.int64)
+    sup = torch.zeros(V)
+    sup[V - 1024:] = float("-inf")
+    sup[eos] = 0.0
+    return dict(logits=logits, seen=seen, seat=seat, ngen=ngen, suppress=sup, eos=eos, rep=1.05, min_new=2)
+
+
 def decode_bytes(ctx_after: torch.Tensor, append: bool = True) -> int:
     """Algorithmic HBM bytes of one paged decode layer: K+V read of every attended token (4096 B each), q read and o
     write (4096 B each per seat), the fused append write (4096 B per seat) and the page-table entries read."""

@@ -10,6 +10,7 @@ only need to import) and calls:
                                  the attention expression of code_predictor.py:46-47 exactly     -> cp_attn.npz
   * Talker._frame               (engine/talker.py:107-112) + CodePredictor.run, fp32, greedy (top_k=1), on random-init
                                  weights and a synthetic K/V history                              -> frame_*.npz
+  * Talker._cb0_logits + sample_topk (engine/talker.py:90-94, engine/ops.py:68-76), greedy      -> sampler.npz
 Inputs are regenerated from seeds by q3attn.synth / q3attn.weights (torch CPU generators); each fixture stores a
 checksum of its inputs so a generator mismatch is detected before outputs are compared. The GPU box never runs this.
 """
@@ -213,6 +214,26 @@ def gen_frames(talker, code_predictor):
         print(f"[golden] {name}: codes {tuple(torch.stack(codes).shape)}", flush=True)
 
 
+# --------------------------------------------------------------------------- codebook-0 logit processing + greedy sampling
+def gen_sampler(talker, ops_mod):
+    """Talker._cb0_logits (engine/talker.py:90-94) with an identity codec_head, so its input row IS the logit row, and
+    sample_topk (engine/ops.py:68-76) with top_k = 1 (greedy), on synth.sampler_case inputs."""
+    out = {}
+    for seed in (1, 2):
+        d = synth.sampler_case(seed)
+        V = d["logits"].shape[1]
+        eos_col = torch.zeros(V, dtype=torch.bool)
+        eos_col[d["eos"]] = True
+        ns = types.SimpleNamespace(W=types.SimpleNamespace(codec_head=torch.eye(V)), seen=d["seen"], rep=d["rep"],
+                                   suppress=d["suppress"], ngen=d["ngen"], min_new=d["min_new"], eos_col=eos_col)
+        lg = talker.Talker._cb0_logits(ns, d["logits"], d["seat"])
+        ids = ops_mod.sample_topk(lg, 0.9, 1, torch.Generator().manual_seed(0))
+        out[f"s{seed}_processed"] = lg.numpy()
+        out[f"s{seed}_greedy"] = ids.numpy()
+        out[f"s{seed}_digest"] = np.array(digest(d["logits"], d["seen"], d["seat"], d["ngen"]))
+    np.savez_compressed(os.path.join(HERE, "sampler.npz"), **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     talker, arrivals, code_predictor = ref_modules()
@@ -225,4 +246,7 @@ if __name__ == "__main__":
         gen_cp(code_predictor)
     if not only or "frames" in only:
         gen_frames(talker, code_predictor)
+    if not only or "sampler" in only:
+        from engine import ops as ref_ops
+        gen_sampler(talker, ref_ops)
     print("[golden] done", flush=True)
