@@ -185,6 +185,19 @@ int q3_cp_step_qkv(const void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
                    int32_t batch, int32_t n_slots, int32_t slot, float softmax_scale,
                    void* out, int64_t out_batch_stride, void* stream);
 
+/* Shared-prefix copy at admission (engine/arrivals.py:67-96 keeps, per (voice, language), the K/V of the k prompt
+ * positions every request of that voice shares; arrivals.py:139-145 writes them into each admitted seat). For every
+ * layer l < num_layers, batch row b and prefix row r < prefix_len, the K and V rows at
+ * src + l * src_layer_stride + slot[b] * src_slot_stride + r * (num_kv_heads * head_dim) (elements, 16-byte aligned)
+ * land at position r of seat[b] in layer l's pools, through the block table. k_pools / v_pools are DEVICE arrays of
+ * the num_layers pool base addresses (16-byte aligned, pool_rows rows each). One launch. */
+int q3_kv_copy_prefix(const void* k_src, const void* v_src, int64_t src_layer_stride, int64_t src_slot_stride,
+                      const uint64_t* k_pools, const uint64_t* v_pools, int32_t num_layers, int64_t pool_rows,
+                      int32_t page_size, int32_t num_kv_heads, int32_t head_dim,
+                      const int64_t* seat, const int64_t* slot, int32_t batch, int32_t prefix_len,
+                      const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
+                      void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * Logit processing + top-k / temperature sampling, one call per sampled token of a frame. Replaces
  * Talker._cb0_logits (engine/talker.py:90-94: repetition penalty over the seat's `seen` row, + suppress row, EOS masked

@@ -443,6 +443,47 @@ int q3_sample_topk(const q3_sampler* p, void* stream) {
   return record(q3::launch_sample_topk(a, static_cast<cudaStream_t>(stream)));
 }
 
+int q3_kv_copy_prefix(const void* k_src, const void* v_src, int64_t src_layer_stride, int64_t src_slot_stride,
+                      const uint64_t* k_pools, const uint64_t* v_pools, int32_t num_layers, int64_t pool_rows,
+                      int32_t page_size, int32_t num_kv_heads, int32_t head_dim, const int64_t* seat,
+                      const int64_t* slot, int32_t batch, int32_t prefix_len, const int32_t* block_table,
+                      int64_t block_table_stride, int32_t max_pages_per_seat, void* stream) {
+  if (num_layers < 0 || batch < 0 || prefix_len < 0 || num_kv_heads <= 0 || head_dim <= 0) return Q3_ERR_INVALID;
+  if (num_layers == 0 || batch == 0 || prefix_len == 0) return Q3_OK;
+  const int row_elems = num_kv_heads * head_dim;
+  if (!k_src || !v_src || !k_pools || !v_pools || !seat || !slot || !block_table || pool_rows <= 0 || page_size <= 0 ||
+      max_pages_per_seat <= 0 || block_table_stride < max_pages_per_seat || row_elems % 8)
+    return Q3_ERR_INVALID;
+  if (src_layer_stride < 0 || src_slot_stride < 0) return Q3_ERR_INVALID;
+  if (!aligned(k_src, 16) || !aligned(v_src, 16) || (src_layer_stride % 8) || (src_slot_stride % 8) ||
+      !aligned(k_pools, 8) || !aligned(v_pools, 8))
+    return Q3_ERR_ALIGNMENT;
+  int dev = 0, rc = current_device(&dev);
+  if (rc != Q3_OK) return rc;
+  uint32_t* st = nullptr;
+  if ((rc = status_ptr(dev, &st)) != Q3_OK) return rc;
+  q3::PrefixCopyArgs a{};
+  a.k_src = static_cast<const __nv_bfloat16*>(k_src);
+  a.v_src = static_cast<const __nv_bfloat16*>(v_src);
+  a.src_layer_stride = src_layer_stride;
+  a.src_slot_stride = src_slot_stride;
+  a.k_pools = reinterpret_cast<const unsigned long long*>(k_pools);
+  a.v_pools = reinterpret_cast<const unsigned long long*>(v_pools);
+  a.L = num_layers;
+  a.pool_rows = pool_rows;
+  a.page_size = page_size;
+  a.row_elems = row_elems;
+  a.seat = seat;
+  a.slot = slot;
+  a.B = batch;
+  a.prefix_len = prefix_len;
+  a.block_table = block_table;
+  a.bt_stride = block_table_stride;
+  a.max_pages = max_pages_per_seat;
+  a.status = st;
+  return record(q3::launch_kv_copy_prefix(a, sm_count(dev), static_cast<cudaStream_t>(stream)));
+}
+
 int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v, int64_t kv_row_stride,
                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t num_seqs, int32_t max_seqlen_q,
                const int32_t* prefix_lens, const int32_t* seat_ids, void* k_pool, void* v_pool, int32_t num_pages,

@@ -66,6 +66,26 @@ struct AppendArgs {
 
 cudaError_t launch_kv_append(const AppendArgs& a, int num_sms, cudaStream_t stream);
 
+struct PrefixCopyArgs {
+  const __nv_bfloat16* k_src;      // row (l, slot, r) at l * src_layer_stride + slot * src_slot_stride + r * row_elems
+  const __nv_bfloat16* v_src;
+  long long src_layer_stride, src_slot_stride;
+  const unsigned long long* k_pools;   // [L] device addresses of each layer's [pool_rows, row_elems] pool
+  const unsigned long long* v_pools;
+  int L;
+  long long pool_rows;
+  int page_size, row_elems;
+  const int64_t* seat;             // [B] destination seat
+  const int64_t* slot;             // [B] prefix slot
+  int B, prefix_len;
+  const int32_t* block_table;
+  long long bt_stride;
+  int max_pages;
+  uint32_t* status;
+};
+
+cudaError_t launch_kv_copy_prefix(const PrefixCopyArgs& a, int num_sms, cudaStream_t stream);
+
 struct CpArgs {
   const __nv_bfloat16* q;          // [B, 16, 128] rows, batch stride q_stride
   long long q_stride;

@@ -57,6 +57,8 @@ SIGNATURES = {
     "q3_cp_step": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
                                   _I32, _F32, _P, _I64, _P]),
     "q3_sample_topk": (ctypes.c_int, [ctypes.POINTER(Sampler), _P]),
+    "q3_kv_copy_prefix": (ctypes.c_int, [_P, _P, _I64, _I64, _P, _P, _I32, _I64, _I32, _I32, _I32, _P, _P, _I32, _I32,
+                                         _P, _I64, _I32, _P]),
     "q3_cp_step_qkv": (ctypes.c_int, [_P, _I64, _NR, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
                                       _I32, _F32, _P, _I64, _P]),
 }

@@ -233,6 +233,43 @@ def kv_append_paged(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_c
     _lib.check(rc, "q3_kv_append_paged")
 
 
+def pool_pointers(pools) -> torch.Tensor:
+    """Device int64 array of the base addresses of per-layer pools (for kv_copy_prefix); build it once, outside
+    capture, and keep it with the pools."""
+    for t in pools:
+        _check_cuda_bf16("pool", t)
+        _need(t.is_contiguous() and t.data_ptr() % 16 == 0, "pools must be contiguous and 16-byte aligned")
+    return torch.tensor([t.data_ptr() for t in pools], dtype=torch.int64, device=pools[0].device)
+
+
+def kv_copy_prefix(k_src: torch.Tensor, v_src: torch.Tensor, k_pool_ptrs: torch.Tensor, v_pool_ptrs: torch.Tensor,
+                   pool_shape, seat: torch.Tensor, slot: torch.Tensor, block_table: torch.Tensor) -> None:
+    """Shared-prefix copy at admission (engine/arrivals.py:139-145 for the prefix rows): for every layer l, batch row
+    b and prefix row r, k_src[l, slot[b], r] / v_src[l, slot[b], r] -> position r of seat[b] in layer l's pools
+    (k_pool_ptrs / v_pool_ptrs from pool_pointers; pool_shape = (num_pages, page_size, 8, 128)). One launch."""
+    lib = _lib.load()
+    _check_cuda_bf16("k_src", k_src)
+    _check_cuda_bf16("v_src", v_src)
+    _need(k_src.dim() == 5 and k_src.shape[3:] == (NKV, HD) and k_src.stride(4) == 1 and k_src.stride(3) == HD and
+          k_src.stride(2) == NKV * HD and v_src.shape == k_src.shape and v_src.stride() == k_src.stride(),
+          "k_src/v_src must be [layers, slots, k, 8, 128] with contiguous rows")
+    L = k_src.shape[0]
+    _need(k_pool_ptrs.numel() >= L and v_pool_ptrs.numel() >= L and k_pool_ptrs.dtype == torch.int64,
+          "one pool address per layer")
+    _need(seat.dtype == torch.int64 and slot.dtype == torch.int64 and seat.numel() == slot.numel(),
+          "seat / slot must be int64 [B]")
+    _need(block_table.dtype == torch.int32 and block_table.dim() == 2 and block_table.stride(1) == 1,
+          "block_table must be int32 [seats, max_pages]")
+    num_pages, page = int(pool_shape[0]), int(pool_shape[1])
+    with torch.cuda.device(k_src.device):
+        rc = lib.q3_kv_copy_prefix(k_src.data_ptr(), v_src.data_ptr(), k_src.stride(0), k_src.stride(1),
+                                   k_pool_ptrs.data_ptr(), v_pool_ptrs.data_ptr(), L, num_pages * page, page, NKV, HD,
+                                   seat.data_ptr(), slot.data_ptr(), seat.numel(), k_src.shape[2],
+                                   block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+                                   _stream(k_src.device))
+    _lib.check(rc, "q3_kv_copy_prefix")
+
+
 def _cp_check(q, K, V):
     _check_cuda_bf16("q", q)
     _check_cuda_bf16("K", K)

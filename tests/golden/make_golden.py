@@ -11,6 +11,8 @@ only need to import) and calls:
   * Talker._frame               (engine/talker.py:107-112) + CodePredictor.run, fp32, greedy (top_k=1), on random-init
                                  weights and a synthetic K/V history                              -> frame_*.npz
   * Talker._cb0_logits + sample_topk (engine/talker.py:90-94, engine/ops.py:68-76), greedy      -> sampler.npz
+  * FastAdmit._run with the per-voice prefix from Talker.prefill_hidden (engine/arrivals.py:85-91, 133-152),
+                                 fp32                                                             -> admit.npz
 Inputs are regenerated from seeds by q3attn.synth / q3attn.weights (torch CPU generators); each fixture stores a
 checksum of its inputs so a generator mismatch is detected before outputs are compared. The GPU box never runs this.
 """
@@ -214,6 +216,77 @@ def gen_frames(talker, code_predictor):
         print(f"[golden] {name}: codes {tuple(torch.stack(codes).shape)}", flush=True)
 
 
+# --------------------------------------------------------------------------- admission (shared prefix + graphed prefill)
+ADMIT = dict(size="0.6B", n_layers=3, n_seats=6, seat_len=512, seed=21, k=35, R=42, seats=[1, 4, 2],
+             slots=[0, 1, 0], bucket=4, n_ids=64)
+
+
+def admit_inputs():
+    """Seeded admission inputs: weights/state as frame_state, two voices' prefix embeddings [2, k, H], a text table
+    [n_ids, H], the admitted rows' prompt ids [S, R+1] and trailing-text ids [S, max_text+1] + lengths (bf16 values)."""
+    c = ADMIT
+    W, st = frame_state(c["size"], c["n_layers"], c["n_seats"], 2, c["seat_len"], (50, 100), c["seed"])
+    g = synth.cpu_gen(c["seed"] + 900)
+    prefix = synth.randn((2, c["k"], W.H), g, 0.5, torch.bfloat16).float()
+    tab = synth.randn((c["n_ids"], W.H), g, 0.5, torch.bfloat16).float()
+    S = len(c["seats"])
+    rem = torch.randint(0, c["n_ids"], (S, c["R"] + 1), generator=g)
+    trail_ids = torch.randint(0, c["n_ids"], (S, st["max_text"] + 1), generator=g)
+    tlen = torch.randint(0, st["max_text"] + 1, (S,), generator=g)
+    return W, st, prefix, tab, rem, trail_ids, tlen
+
+
+def gen_admit(talker, arrivals, code_predictor):
+    """FastAdmit._run (engine/arrivals.py:133-152) in fp32 on a reference Talker, with the per-voice prefix K/V computed
+    by Talker.prefill_hidden in the scratch seat (what voice_slot does, arrivals.py:85-91)."""
+    c = ADMIT
+    W, st, prefix, tab, rem, trail_ids, tlen = admit_inputs()
+    T = ref_talker(talker, code_predictor, W, c["n_seats"], c["seat_len"], c["bucket"], st)
+    k, R, nl, sl = c["k"], c["R"], len(W.layers), c["seat_len"]
+    A = object.__new__(arrivals.FastAdmit)
+    A.T, A.W, A.d, A.dt, A.k, A.R, A.L = T, W, torch.device("cpu"), torch.float32, k, R, k + R + 1
+    A.pK = torch.zeros(nl, 2, k, 8, 128)
+    A.pV = torch.zeros_like(A.pK)
+    s = T.n_seats
+    with torch.inference_mode():
+        for slot in (0, 1):
+            T.prefill_hidden([s], [prefix[slot]])
+            for l in range(nl):
+                A.pK[l, slot] = T.kc[l].view(-1, 8, 128)[s * sl:s * sl + k]
+                A.pV[l, slot] = T.vc[l].view(-1, 8, 128)[s * sl:s * sl + k]
+        S, B = c["bucket"], len(c["seats"])
+        A.tab = tab
+        A.crem = torch.zeros(2, R + 1, W.H)
+        A.s_seat = torch.full((S,), c["n_seats"], dtype=torch.int64)
+        A.s_seat[:B] = torch.tensor(c["seats"])
+        A.s_slot = torch.zeros(S, dtype=torch.int64)
+        A.s_slot[:B] = torch.tensor(c["slots"])
+        A.s_rem = torch.zeros(S, R + 1, dtype=torch.int64)
+        A.s_rem[:B] = rem
+        A.s_trail = torch.zeros(S, st["max_text"] + 1, dtype=torch.int64)
+        A.s_trail[:B] = trail_ids
+        A.s_tlen = torch.zeros(S, dtype=torch.int64)
+        A.s_tlen[:B] = tlen
+        A.z_seen = torch.zeros(S, W.vocab, dtype=torch.bool)
+        A.z_i = torch.zeros(S, dtype=torch.int64)
+        A.c_pos = torch.full((S,), k + R, dtype=torch.int64)
+        A.ar = torch.arange(k + R)[None, :]
+        A.cos, A.sin = W.cos[k:k + R][None, :, None, :], W.sin[k:k + R][None, :, None, :]
+        A.layer, A.post = A._layer, A._post
+        T.seen[torch.tensor(c["seats"])] = True                                 # the reset must clear these
+        A._run(S)
+    seats = torch.tensor(c["seats"])
+    out = {}
+    for l in (0, nl - 1):                # the first layer and the deepest (fp16 keeps the fixture small)
+        rows = (seats[:, None] * sl + torch.arange(k + R)[None, :]).reshape(-1)
+        out[f"K{l}"] = T.kc[l].view(-1, 8, 128)[rows].view(B, k + R, 8, 128).numpy().astype(np.float16)
+        out[f"V{l}"] = T.vc[l].view(-1, 8, 128)[rows].view(B, k + R, 8, 128).numpy().astype(np.float16)
+    out.update(x_in=T.x_in[seats].numpy(), pos=T.pos.numpy(), trail=T.trail[seats].numpy(),
+               trail_len=T.trail_len[seats].numpy(), ngen=T.ngen[seats].numpy(), seen=T.seen[seats].numpy(),
+               digest=np.array(digest(prefix, tab, rem.float(), W.layers[0].qkv)))
+    np.savez_compressed(os.path.join(HERE, "admit.npz"), **out)
+
+
 # --------------------------------------------------------------------------- codebook-0 logit processing + greedy sampling
 def gen_sampler(talker, ops_mod):
     """Talker._cb0_logits (engine/talker.py:90-94) with an identity codec_head, so its input row IS the logit row, and
@@ -246,6 +319,8 @@ if __name__ == "__main__":
         gen_cp(code_predictor)
     if not only or "frames" in only:
         gen_frames(talker, code_predictor)
+    if not only or "admit" in only:
+        gen_admit(talker, arrivals, code_predictor)
     if not only or "sampler" in only:
         from engine import ops as ref_ops
         gen_sampler(talker, ref_ops)
