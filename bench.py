@@ -57,7 +57,7 @@ def parse():
     p.add_argument("--cpu-seats", type=int, default=48)
     p.add_argument("--kernel-breakdown", action="store_true",
                    help="c5: add the per-kernel device time of one replayed frame (CUPTI via torch.profiler)")
-    p.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2",
+    p.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "admit"], default="c2",
                    help="c2: the headline decode step (default); c3: 1.7B decode + chunked-prefill mix; c4: CP steps")
     return p.parse_args()
 
@@ -356,6 +356,49 @@ def frame_kernel_breakdown(graph, talker, top=16):
             "top": [[k[:90], round(v[1] / 2, 1), v[0] // 2, round(v[1] / total, 4)] for k, v in rows]}
 
 
+def bench_admit(a):
+    """Admission (engine/arrivals.py FastAdmit) on one GPU: the 0.6B talker (28 layers, random-init weights), a
+    (voice, language) prefix of k = 35 shared positions and R = 42 new prompt positions per sequence, S = 1 and 8
+    sequences per call: device time per replay of the admission graph (prefix copy of all layers + 27 paged-prefill
+    layers + the last layer's K/V write)."""
+    import q3attn
+    from q3attn import weights
+    from q3attn.admit import Admit
+    from q3attn.frame import Talker
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    k, R, n_seats, seat_len = 35, 42, 64, 512
+    W = weights.cast(weights.random_weights(a.seed, "0.6B", max_pos=seat_len + 16), torch.bfloat16, dev)
+    T = Talker(W, n_seats, seat_len=seat_len, buckets=[8], page=16, top_k=1)
+    A = Admit(T, k, R, max_slots=2, buckets=(1, 8))
+    gen = torch.Generator(device=dev).manual_seed(a.seed)
+    A.register_prefix(0, torch.randn(k, W.H, generator=gen, device=dev).mul_(0.5).to(torch.bfloat16))
+    A.capture()
+    x = torch.randn(8, R + 1, W.H, generator=gen, device=dev).mul_(0.5).to(torch.bfloat16)
+    trail = torch.zeros(8, T.max_text + 1, W.H, dtype=torch.bfloat16, device=dev)
+    res = {}
+    for S in (1, 8):
+        A.admit(list(range(S)), [0] * S, x[:S], trail[:S], [0] * S)
+        g = A.graphs[S]
+        for _ in range(a.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = min(a.steps, 50)
+        e0.record()
+        for _ in range(n):
+            g.replay()
+        e1.record()
+        e1.synchronize()
+        if q3attn._lib.read_status():
+            raise RuntimeError("device status raised during admission")
+        res[S] = e0.elapsed_time(e1) / n
+    print(json.dumps({"metric": "admission ms per call (0.6B, k=35 shared + R=42 new positions per sequence)",
+                      "workload": "admit", "value": res[8], "unit": "ms per call of 8 sequences",
+                      "ms_per_call_S1": res[1], "ms_per_call_S8": res[8], "layers": len(W.layers),
+                      "reference_a100": "3-4 ms GPU per admission call (engine README)"}), flush=True)
+
+
 def bench_aux(a):
     """Configs 3 and 4 (reported in DESIGN, not the headline): device time per layer on one GPU, CUDA events over
     graph replays, inputs resident; L2 is not flushed for c4 (its 38 MB per-layer scratch is L2-resident by design)."""
@@ -449,6 +492,8 @@ def main():
     a = parse()
     if a.workload == "c5" and a.impl == "ours":
         return bench_frame(a)
+    if a.workload == "admit" and a.impl == "ours":
+        return bench_admit(a)
     if a.workload != "c2" and a.impl == "ours":
         return bench_aux(a)
     if a.impl == "reference":

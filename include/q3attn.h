@@ -185,6 +185,24 @@ int q3_cp_step_qkv(const void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
                    int32_t batch, int32_t n_slots, int32_t slot, float softmax_scale,
                    void* out, int64_t out_batch_stride, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * Row kernels around the attention layers (one launch each instead of a chain of small ops), bf16 rounding points
+ * of the reference's eager source. */
+/* Residual add + RMSNorm (engine/ops.py:51-55 after the residual adds of talker.py:78-79 / code_predictor.py:48-50):
+ * with residual given, x = bf16(x + residual) is written back to x first; then
+ * out = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))). hidden 1024 or 2048; rows 16-byte aligned. */
+int q3_add_rms_norm(void* x, int64_t x_row_stride, const void* residual, int64_t residual_row_stride,
+                    const void* weight, void* out, int64_t out_row_stride, int64_t rows, int32_t hidden, float eps,
+                    void* stream);
+/* SiLU-gated product of the MLP (engine/ops.py:63-65): out = bf16(bf16(silu(g)) * u) for gate_up = [g | u]
+ * [rows, 2 * ffn]. */
+int q3_silu_mul(const void* gate_up, int64_t gate_up_row_stride, void* out, int64_t out_row_stride, int64_t rows,
+                int32_t ffn, void* stream);
+/* q/k RMSNorm + RoPE (engine/ops.py:51-60 as called at talker.py:69-70, arrivals.py:114-115) in place on QKV rows
+ * [q 16x128 | k 8x128 | v 8x128]; cos/sin row r serves row r (rope_row_stride 0: one row for all). */
+int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rope* norm_rope, int64_t rows,
+                         void* stream);
+
 /* Shared-prefix copy at admission (engine/arrivals.py:67-96 keeps, per (voice, language), the K/V of the k prompt
  * positions every request of that voice shares; arrivals.py:139-145 writes them into each admitted seat). For every
  * layer l < num_layers, batch row b and prefix row r < prefix_len, the K and V rows at

@@ -484,6 +484,70 @@ int q3_kv_copy_prefix(const void* k_src, const void* v_src, int64_t src_layer_st
   return record(q3::launch_kv_copy_prefix(a, sm_count(dev), static_cast<cudaStream_t>(stream)));
 }
 
+int q3_add_rms_norm(void* x, int64_t x_row_stride, const void* residual, int64_t residual_row_stride,
+                    const void* weight, void* out, int64_t out_row_stride, int64_t rows, int32_t hidden, float eps,
+                    void* stream) {
+  if (rows < 0) return Q3_ERR_INVALID;
+  if (hidden != 1024 && hidden != 2048) return Q3_ERR_UNSUPPORTED;
+  if (rows == 0) return Q3_OK;
+  if (!x || !weight || !out || x_row_stride < hidden || out_row_stride < hidden || !(eps >= 0.f) ||
+      (residual && residual_row_stride < hidden) || rows > (1ll << 31) * 4)
+    return Q3_ERR_INVALID;
+  if (!aligned(x, 16) || !aligned(weight, 16) || !aligned(out, 16) || (x_row_stride % 8) || (out_row_stride % 8) ||
+      (residual && (!aligned(residual, 16) || (residual_row_stride % 8))))
+    return Q3_ERR_ALIGNMENT;
+  q3::RowNormArgs a{};
+  a.x = static_cast<__nv_bfloat16*>(x);
+  a.x_stride = x_row_stride;
+  a.r = static_cast<const __nv_bfloat16*>(residual);
+  a.r_stride = residual_row_stride;
+  a.w = static_cast<const __nv_bfloat16*>(weight);
+  a.y = static_cast<__nv_bfloat16*>(out);
+  a.y_stride = out_row_stride;
+  a.rows = rows;
+  a.H = hidden;
+  a.eps = eps;
+  return record(q3::launch_add_rms_norm(a, static_cast<cudaStream_t>(stream)));
+}
+
+int q3_silu_mul(const void* gate_up, int64_t gate_up_row_stride, void* out, int64_t out_row_stride, int64_t rows,
+                int32_t ffn, void* stream) {
+  if (rows < 0 || ffn <= 0 || (ffn % 8)) return Q3_ERR_INVALID;
+  if (rows == 0) return Q3_OK;
+  if (!gate_up || !out || gate_up_row_stride < 2ll * ffn || out_row_stride < ffn) return Q3_ERR_INVALID;
+  if (!aligned(gate_up, 16) || !aligned(out, 16) || (gate_up_row_stride % 8) || (out_row_stride % 8))
+    return Q3_ERR_ALIGNMENT;
+  int dev = 0, rc = current_device(&dev);
+  if (rc != Q3_OK) return rc;
+  q3::SiluMulArgs a{};
+  a.gu = static_cast<const __nv_bfloat16*>(gate_up);
+  a.gu_stride = gate_up_row_stride;
+  a.y = static_cast<__nv_bfloat16*>(out);
+  a.y_stride = out_row_stride;
+  a.rows = rows;
+  a.F = ffn;
+  return record(q3::launch_silu_mul(a, sm_count(dev), static_cast<cudaStream_t>(stream)));
+}
+
+int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rope* norm_rope, int64_t rows,
+                         void* stream) {
+  if (rows < 0 || !norm_rope || !norm_rope_ok(norm_rope)) return Q3_ERR_INVALID;
+  if (rows == 0) return Q3_OK;
+  if (!qkv || qkv_row_stride < (q3::kQHeads + 2 * q3::kKvHeads) * q3::kHeadDim) return Q3_ERR_INVALID;
+  if (!aligned(qkv, 8) || (qkv_row_stride % 4) || !norm_rope_aligned(norm_rope)) return Q3_ERR_ALIGNMENT;
+  q3::QkNormRopeArgs a{};
+  a.qkv = static_cast<__nv_bfloat16*>(qkv);
+  a.qkv_stride = qkv_row_stride;
+  a.rows = rows;
+  a.qn_w = static_cast<const __nv_bfloat16*>(norm_rope->q_norm_weight);
+  a.kn_w = static_cast<const __nv_bfloat16*>(norm_rope->k_norm_weight);
+  a.rope_cos = static_cast<const __nv_bfloat16*>(norm_rope->cos);
+  a.rope_sin = static_cast<const __nv_bfloat16*>(norm_rope->sin);
+  a.rope_stride = norm_rope->rope_row_stride;
+  a.eps = norm_rope->eps;
+  return record(q3::launch_qk_norm_rope(a, static_cast<cudaStream_t>(stream)));
+}
+
 int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v, int64_t kv_row_stride,
                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t num_seqs, int32_t max_seqlen_q,
                const int32_t* prefix_lens, const int32_t* seat_ids, void* k_pool, void* v_pool, int32_t num_pages,

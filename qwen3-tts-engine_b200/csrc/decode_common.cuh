@@ -38,10 +38,6 @@ __device__ __forceinline__ uint32_t word_of(const uint4& w, int e) {
   return e == 0 ? w.x : (e == 1 ? w.y : (e == 2 ? w.z : w.w));
 }
 
-__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t x) {
-  return make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
-}
-
 // CTA index owning global chunk p when N chunks are split over Ge CTAs as [c*N/Ge, (c+1)*N/Ge).
 __device__ __forceinline__ int cta_of_chunk(long long p, long long N, int Ge) {
   return static_cast<int>(((p + 1) * Ge + N - 1) / N - 1);

@@ -41,6 +41,11 @@ __device__ __forceinline__ float4 bf16x4_to_float4(uint2 w) {
   return f;
 }
 
+// Two bf16 packed in a uint32 (low half first) -> two floats.
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t x) {
+  return make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

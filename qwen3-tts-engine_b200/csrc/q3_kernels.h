@@ -139,6 +139,43 @@ struct SampleArgs {
 
 cudaError_t launch_sample_topk(const SampleArgs& a, cudaStream_t stream);
 
+struct RowNormArgs {
+  __nv_bfloat16* x;                // [rows, H] residual stream (updated in place when r is given)
+  long long x_stride;
+  const __nv_bfloat16* r;          // optional [rows, H] added to x first
+  long long r_stride;
+  const __nv_bfloat16* w;          // [H]
+  __nv_bfloat16* y;                // [rows, H] normalised output
+  long long y_stride;
+  long long rows;
+  int H;                           // 1024 or 2048
+  float eps;
+};
+cudaError_t launch_add_rms_norm(const RowNormArgs& a, cudaStream_t stream);
+
+struct SiluMulArgs {
+  const __nv_bfloat16* gu;         // [rows, 2F]: gate | up
+  long long gu_stride;
+  __nv_bfloat16* y;                // [rows, F]
+  long long y_stride;
+  long long rows;
+  int F;
+};
+cudaError_t launch_silu_mul(const SiluMulArgs& a, int num_sms, cudaStream_t stream);
+
+struct QkNormRopeArgs {
+  __nv_bfloat16* qkv;              // [rows, (16 + 8 + 8) * 128]: q and k heads rewritten in place
+  long long qkv_stride;
+  long long rows;
+  const __nv_bfloat16* qn_w;
+  const __nv_bfloat16* kn_w;
+  const __nv_bfloat16* rope_cos;   // row r at r * rope_stride
+  const __nv_bfloat16* rope_sin;
+  long long rope_stride;
+  float eps;
+};
+cudaError_t launch_qk_norm_rope(const QkNormRopeArgs& a, cudaStream_t stream);
+
 struct PrefillArgs {
   const __nv_bfloat16* q;          // [Tq, 16, 128] rows, row stride q_stride (elements)
   long long q_stride;

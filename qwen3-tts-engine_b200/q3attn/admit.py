@@ -6,8 +6,8 @@ voice_slot does with T.prefill_hidden, arrivals.py:85-91) and kept as pK/pV [lay
 seats is one CUDA graph per S bucket (arrivals.py:154-167) whose body (_run, arrivals.py:133-152):
   1. resets each seat's sampling state and trailing text (arrivals.py:136-137);
   2. copies the slot's prefix K/V of every layer into the seats' pages in ONE launch (q3attn.kv_copy_prefix);
-  3. runs the R remaining prompt positions through the layers: per layer the QKV GEMM and q/k norm + RoPE, then ONE
-     paged prefill launch that attends over prefix (in the pages) + new rows with bottom-right causal alignment and
+  3. runs the R remaining prompt positions through the layers: per layer the residual add + RMSNorm (one launch), the
+     QKV GEMM, the q/k norm + RoPE in place (one launch), then ONE paged prefill launch that attends over prefix (in the pages) + new rows with bottom-right causal alignment and
      writes the new K/V rows (arrivals.py:139-148); the last layer only writes its K/V rows (arrivals.py:146);
   4. sets pos = k + R and the pending talker input to the last prompt position (arrivals.py:149-151).
 The prompt embeddings (text table + codec track, arrivals.py:137-139) and trailing-text rows are inputs: building them
@@ -17,7 +17,6 @@ import torch
 import torch.nn.functional as F
 
 from . import ops
-from .frame import mlp, rms, rope
 
 
 class Admit:
@@ -68,22 +67,24 @@ class Admit:
         seat32 = seats.to(torch.int32)
         seat_rows = seat32[meta["row_of"]]
         bt = T.seat_pages
-        c = cos.repeat(S, 1)[:, None, :]
-        s = sin.repeat(S, 1)[:, None, :]
-        xf = x.reshape(S * n, T.H)
+        c = cos.repeat(S, 1)
+        s = sin.repeat(S, 1)
+        xf = x.reshape(S * n, T.H).clone()                      # the residual stream, updated in place
+        r = None
         for l in range(self.nl):
             w = self.W.layers[l]
-            qkv = F.linear(rms(xf, w.ln1), w.qkv)
-            q = rope(rms(qkv[:, :nq].view(-1, T.nh, T.hd), w.qn), c, s)
-            kk = rope(rms(qkv[:, nq:nq + nk].view(-1, T.nkv, T.hd), w.kn), c, s)
-            v = qkv[:, nq + nk:].contiguous().view(-1, T.nkv, T.hd)
+            qkv = F.linear(ops.add_rms_norm(xf, w.ln1, r), w.qkv)
+            ops.qk_norm_rope_(qkv, w.qn, w.kn, c, s)            # arrivals.py:114-115, in place on the q and k heads
+            q = qkv[:, :nq].view(-1, T.nh, T.hd)
+            kk = qkv[:, nq:nq + nk].view(-1, T.nkv, T.hd)
+            v = qkv[:, nq + nk:].view(-1, T.nkv, T.hd)
             if l == self.nl - 1:                 # arrivals.py:146: only the K/V of the last layer are needed
                 ops.kv_append_paged(kk, v, T.kc[l], T.vc[l], meta["pos"], bt, seat_rows)
                 break
             o = ops.prefill_paged(q, kk, v, T.kc[l], T.vc[l], meta["cu"], meta["cu"], n, meta["plen"], seat32, bt,
                                   T.scale, True, True)
-            xf = xf + F.linear(o.reshape(S * n, nq), w.o)
-            xf = xf + mlp(rms(xf, w.ln2), w, T.ffn)
+            h = ops.add_rms_norm(xf, w.ln2, F.linear(o.reshape(S * n, nq), w.o))
+            r = F.linear(ops.silu_mul(F.linear(h, w.gu)), w.down)
 
     @torch.inference_mode()
     def register_prefix(self, slot: int, prefix: torch.Tensor):

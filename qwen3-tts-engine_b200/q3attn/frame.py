@@ -77,15 +77,23 @@ class CodePredictor:
     def _s(self, x, B, p):
         W = self.W
         cos, sin = W.cp_cos[p], W.cp_sin[p]
-        for l in range(self.L):
+        if self.fuse:
+            # code_predictor.py:37-50 with the q3attn row kernels: residual add + RMSNorm and the SiLU gate in one
+            # launch each, q/k norm + RoPE + slot write + attention in one (the residual stream is updated in place)
+            x = x.clone()
+            r = None
+            for l in range(self.L):
+                w = W.cp_layers[l]
+                qkv = F.linear(ops.add_rms_norm(x, w.ln1, r), w.qkv)
+                o = ops.cp_step_qkv(qkv, w.qn, w.kn, cos, sin, self.K[l, :B], self.V[l, :B], p, self.scale)
+                h = ops.add_rms_norm(x, w.ln2, F.linear(o, w.o))
+                r = F.linear(ops.silu_mul(F.linear(h, w.gu)), w.down)
+            return ops.add_rms_norm(x, W.cp_norm, r)
+        for l in range(self.L):   # the same maths as separate PyTorch ops
             w = W.cp_layers[l]
             qkv = F.linear(rms(x, w.ln1), w.qkv)                                        # code_predictor.py:39
-            if self.fuse:
-                o = ops.cp_step_qkv(qkv, w.qn, w.kn, cos, sin, self.K[l, :B], self.V[l, :B], p,  # :40-42, 58, 46-47
-                                    self.scale)
-            else:   # the same maths with the q/k norm and RoPE as separate PyTorch ops
-                q, k, v = _split_qkv(qkv, w, cos, sin, B, self.nh, self.nkv, self.hd)
-                o = ops.cp_step(q, k, v, self.K[l, :B], self.V[l, :B], p, self.scale)
+            q, k, v = _split_qkv(qkv, w, cos, sin, B, self.nh, self.nkv, self.hd)     # :40-42
+            o = ops.cp_step(q, k, v, self.K[l, :B], self.V[l, :B], p, self.scale)    # :58, 46-47
             x = x + F.linear(o, w.o)
             gu = F.linear(rms(x, w.ln2), w.gu)
             x = x + F.linear(F.silu(gu[..., :self.ffn]) * gu[..., self.ffn:], w.down)
@@ -129,9 +137,10 @@ class Talker:
     """engine/talker.py:20-138 over paged K/V pools and the q3attn kernels.
 
     block_table: int32 [n_seats + 1, seat_len // page] (the last row is the scratch seat padded rows point at,
-    talker.py:29); default = identity pages. fuse_qk_norm_rope=False runs the q/k norms and RoPE as separate
-    PyTorch ops ahead of the attention kernels, and fused_sampler=False samples with PyTorch ops and torch's generator
-    instead of q3attn.sample_topk (same maths, another random stream; both kept to measure what the fusions save)."""
+    talker.py:29); default = identity pages. fuse_qk_norm_rope=False runs the layer norms, the q/k norms + RoPE and the
+    MLP gate as separate PyTorch ops around the attention kernels, and fused_sampler=False samples with PyTorch ops and
+    torch's generator instead of q3attn.sample_topk (same maths, another random stream; both kept to measure what the
+    fusions save)."""
 
     def __init__(self, W, n_seats, seat_len=768, buckets=None, page=16, block_table=None, max_text=16,
                  temperature=0.9, top_k=50, rep_penalty=1.05, min_new=2, seed=0, fuse_qk_norm_rope=True,
@@ -185,15 +194,23 @@ class Talker:
         B = x.shape[0]
         nq = self.nh * self.hd
         seqlens = pos.to(torch.int32)
-        for l in range(len(self.W.layers)):
-            w = self.W.layers[l]
-            qkv = F.linear(rms(x, w.ln1), w.qkv)                                           # talker.py:68
-            if self.fuse:
+        if self.fuse:
+            # talker.py:66-80 with the q3attn row kernels (residual add + RMSNorm, SiLU gate) and the fused q/k norm +
+            # RoPE + append + paged attention; x (a gathered copy) is the residual stream, updated in place
+            r = None
+            for l in range(len(self.W.layers)):
+                w = self.W.layers[l]
+                qkv = F.linear(ops.add_rms_norm(x, w.ln1, r), w.qkv)                      # talker.py:68
                 o = ops.paged_decode_qkv(qkv, w.qn, w.kn, cos, sin, self.kc[l], self.vc[l], seqlens, bt,  # :69-77
                                          self.scale)
-            else:
-                q, k, v = _split_qkv(qkv, w, cos, sin, B, self.nh, self.nkv, self.hd)
-                o = ops.paged_decode_append(q, k, v, self.kc[l], self.vc[l], seqlens, bt, self.scale, 0)
+                h = ops.add_rms_norm(x, w.ln2, F.linear(o.reshape(B, nq), w.o))           # :78-79
+                r = F.linear(ops.silu_mul(F.linear(h, w.gu)), w.down)
+            return ops.add_rms_norm(x, self.W.norm, r)
+        for l in range(len(self.W.layers)):   # the same maths as separate PyTorch ops
+            w = self.W.layers[l]
+            qkv = F.linear(rms(x, w.ln1), w.qkv)
+            q, k, v = _split_qkv(qkv, w, cos, sin, B, self.nh, self.nkv, self.hd)
+            o = ops.paged_decode_append(q, k, v, self.kc[l], self.vc[l], seqlens, bt, self.scale, 0)
             x = x + F.linear(o.reshape(B, nq), w.o)
             x = x + mlp(rms(x, w.ln2), w, self.ffn)
         return rms(x, self.W.norm)

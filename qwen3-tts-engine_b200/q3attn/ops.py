@@ -233,6 +233,77 @@ def kv_append_paged(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_c
     _lib.check(rc, "q3_kv_append_paged")
 
 
+def _rows2d(name, t, cols):
+    _check_cuda_bf16(name, t)
+    _need(t.dim() == 2 and t.shape[1] == cols and t.stride(1) == 1, f"{name} must be [rows, {cols}] with unit inner stride")
+
+
+@torch.library.custom_op("q3attn::add_rms_norm", mutates_args=("x",))
+def _add_rms_norm_op(x: torch.Tensor, weight: torch.Tensor, residual: Optional[torch.Tensor], eps: float) -> torch.Tensor:
+    lib = _lib.load()
+    H = x.shape[-1]
+    x2 = x.view(-1, H)
+    _rows2d("x", x2, H)
+    _check_cuda_bf16("weight", weight)
+    _need(weight.numel() == H and weight.is_contiguous(), "weight must be [hidden]")
+    r2 = None
+    if residual is not None:
+        r2 = residual.reshape(-1, H)
+        _rows2d("residual", r2, H)
+        _need(r2.shape[0] == x2.shape[0], "residual must match x")
+    out = torch.empty_like(x2)
+    with torch.cuda.device(x.device):
+        rc = lib.q3_add_rms_norm(x2.data_ptr(), x2.stride(0), _ptr(r2), r2.stride(0) if r2 is not None else 0,
+                                 weight.data_ptr(), out.data_ptr(), out.stride(0), x2.shape[0], H, float(eps),
+                                 _stream(x.device))
+    _lib.check(rc, "q3_add_rms_norm")
+    return out.view(x.shape)
+
+
+@_add_rms_norm_op.register_fake
+def _(x, weight, residual, eps):
+    return torch.empty_like(x)
+
+
+def add_rms_norm(x, weight, residual=None, eps: float = 1e-6):
+    """RMSNorm (engine/ops.py:51-55) of x [..., H] (H = 1024 or 2048), after x += residual in place when residual is
+    given (the residual adds of talker.py:78-79). One launch; returns the normalised rows."""
+    return _add_rms_norm_op(x, weight, residual, float(eps))
+
+
+@torch.library.custom_op("q3attn::silu_mul", mutates_args=())
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """The MLP gate of engine/ops.py:63-65: silu(g) * u for gate_up = [g | u] [..., 2F] -> [..., F]. One launch."""
+    lib = _lib.load()
+    F2 = gate_up.shape[-1]
+    g2 = gate_up.view(-1, F2)
+    _rows2d("gate_up", g2, F2)
+    out = torch.empty(g2.shape[0], F2 // 2, dtype=torch.bfloat16, device=gate_up.device)
+    with torch.cuda.device(gate_up.device):
+        rc = lib.q3_silu_mul(g2.data_ptr(), g2.stride(0), out.data_ptr(), out.stride(0), g2.shape[0], F2 // 2,
+                             _stream(gate_up.device))
+    _lib.check(rc, "q3_silu_mul")
+    return out.view(*gate_up.shape[:-1], F2 // 2)
+
+
+@silu_mul.register_fake
+def _(gate_up):
+    return gate_up.new_empty(*gate_up.shape[:-1], gate_up.shape[-1] // 2)
+
+
+@torch.library.custom_op("q3attn::qk_norm_rope_", mutates_args=("qkv",))
+def qk_norm_rope_(qkv: torch.Tensor, q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, cos: torch.Tensor,
+                  sin: torch.Tensor, eps: float = 1e-6) -> None:
+    """q/k RMSNorm + RoPE (engine/ops.py:51-60) in place on QKV rows [T, 4096] (q | k | v): cos/sin [T, 128] (row r
+    for row r) or one [128] row. One launch."""
+    lib = _lib.load()
+    q = _qkv_rows(qkv)
+    nr = _norm_rope(q_norm_w, k_norm_w, cos, sin, eps, q.shape[0])
+    with torch.cuda.device(qkv.device):
+        rc = lib.q3_qk_norm_rope_rows(q.data_ptr(), q.stride(0), ctypes.byref(nr), q.shape[0], _stream(qkv.device))
+    _lib.check(rc, "q3_qk_norm_rope_rows")
+
+
 def pool_pointers(pools) -> torch.Tensor:
     """Device int64 array of the base addresses of per-layer pools (for kv_copy_prefix); build it once, outside
     capture, and keep it with the pools."""
