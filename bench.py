@@ -57,7 +57,7 @@ def parse():
     p.add_argument("--cpu-seats", type=int, default=48)
     p.add_argument("--kernel-breakdown", action="store_true",
                    help="c5: add the per-kernel device time of one replayed frame (CUPTI via torch.profiler)")
-    p.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "admit"], default="c2",
+    p.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "admit", "prefill"], default="c2",
                    help="c2: the headline decode step (default); c3: 1.7B decode + chunked-prefill mix; c4: CP steps")
     return p.parse_args()
 
@@ -430,6 +430,29 @@ def bench_aux(a):
         return e0.elapsed_time(e1) / n
 
     gen = torch.Generator(device=dev).manual_seed(a.seed)
+    if a.workload == "prefill":
+        # config 3's prefill part alone: 10 seats chunk-prefill 320-token prompts into fresh pages (a pool holding only
+        # those seats: a small case for kernel profiles)
+        np_, plen, pps = 10, 320, 20
+        kp = torch.zeros((np_ * pps, 16, 8, 128), device=dev, dtype=torch.bfloat16)
+        vp = torch.zeros_like(kp)
+        bt = torch.randperm(np_ * pps, generator=torch.Generator().manual_seed(a.seed)).view(np_, pps).to(dev, torch.int32)
+        T_ = np_ * plen
+        qp = torch.randn((T_, 16, 128), generator=gen, device=dev, dtype=torch.bfloat16)
+        kpn = torch.randn((T_, 8, 128), generator=gen, device=dev, dtype=torch.bfloat16)
+        vpn = torch.randn((T_, 8, 128), generator=gen, device=dev, dtype=torch.bfloat16)
+        cu = torch.arange(np_ + 1, dtype=torch.int32, device=dev) * plen
+        zeros = torch.zeros(np_, dtype=torch.int32, device=dev)
+        sid = torch.arange(np_, dtype=torch.int32, device=dev)
+
+        def pre():
+            q3attn.prefill_paged(qp, kpn, vpn, kp, vp, cu, cu, plen, zeros, sid, bt, SCALE, True, True)
+        t_pre = timed(pre, a.steps)
+        flops = 4 * 128 * 16 * np_ * (plen * (plen + 1) // 2)
+        print(json.dumps({"metric": "chunked prefill 10 x 320 tokens into fresh pages (C3 prefill part)",
+                          "workload": "prefill", "value": t_pre * 1e3, "unit": "us", "tflops": flops / t_pre / 1e9,
+                          "flops": flops}), flush=True)
+        return
     if a.workload == "c4":
         B, L = a.seats, 5
         K = torch.randn((L, B, 8, 16, 128), generator=gen, device=dev, dtype=torch.bfloat16)

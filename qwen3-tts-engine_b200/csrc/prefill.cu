@@ -168,16 +168,42 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArg
   const int ntq = s.R > 0 ? (s.R + kPfQRows - 1) / kPfQRows : 1;
   if (qt >= ntq) return;                                     // uniform; nothing allocated yet
 
-  // ---- fused page write: head h of new rows r with r % ntq == qt go to positions P + r of the seat's pages
+  // ---- fused page write: head h of new rows r with r % ntq == qt go to positions P + r of the seat's pages. Every
+  //      (row, K or V, 16-byte chunk) copy is independent: each thread takes kPfWriteBatch of them at a time and
+  //      issues all their table and row loads before any store, so the whole CTA's loads are in flight together.
   if (a.write_kv) {
-    for (int r = qt; r < s.Nn; r += ntq) {
-      const long long prow = pf_pool_row(a, s.seat, s.P + r);
-      const long long src = static_cast<long long>(s.k0 + r) * a.kv_stride + h * kHeadDim;
-      const long long dst = prow * (kKvHeads * kHeadDim) + h * kHeadDim;
-      if (tid < 16)
-        reinterpret_cast<uint4*>(a.k_pool + dst)[tid] = __ldg(reinterpret_cast<const uint4*>(a.k + src) + tid);
-      else if (tid < 32)
-        reinterpret_cast<uint4*>(a.v_pool + dst)[tid - 16] = __ldg(reinterpret_cast<const uint4*>(a.v + src) + tid - 16);
+    constexpr int kPfWriteBatch = 8;
+    const int nrows = s.Nn > qt ? (s.Nn - qt + ntq - 1) / ntq : 0;
+    const int total = nrows * 32;                            // 16 K chunks + 16 V chunks per row
+#pragma unroll 1
+    for (int base = tid; base < total; base += kPfThreads * kPfWriteBatch) {
+      long long dst[kPfWriteBatch];
+      uint4 val[kPfWriteBatch];
+#pragma unroll
+      for (int u = 0; u < kPfWriteBatch; ++u) {
+        const int i = base + u * kPfThreads;
+        dst[u] = -1;
+        if (i < total) {
+          const int r = qt + (i >> 5) * ntq, part = i & 31;
+          const long long prow = pf_pool_row(a, s.seat, s.P + r);
+          dst[u] = prow * (kKvHeads * kHeadDim) + h * kHeadDim + (part & 15) * 8;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kPfWriteBatch; ++u) {
+        const int i = base + u * kPfThreads;
+        val[u] = make_uint4(0, 0, 0, 0);
+        if (i < total) {
+          const int r = qt + (i >> 5) * ntq, part = i & 31;
+          const long long src = static_cast<long long>(s.k0 + r) * a.kv_stride + h * kHeadDim + (part & 15) * 8;
+          val[u] = __ldg(reinterpret_cast<const uint4*>((part < 16 ? a.k : a.v) + src));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kPfWriteBatch; ++u) {
+        const int i = base + u * kPfThreads;
+        if (i < total) *reinterpret_cast<uint4*>(((i & 31) < 16 ? a.k_pool : a.v_pool) + dst[u]) = val[u];
+      }
     }
   }
   if (s.R == 0) return;
@@ -230,20 +256,28 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArg
   constexpr uint32_t kIdescPV = umma_idesc_bf16(128, kHeadDim, 0, 1);
   float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
-  for (int kt = 0; kt < ntk && ok; ++kt) {
-    // ---- K and V tiles: thread t loads half (t/64) of key kt*64 + t%64
-    {
-      const int kk_local = tid & 63, half = tid >> 6, kk = kt * kPfKeys + kk_local;
-      const bool kv_ok = kk < L;
-      const uint4* ks = kv_ok ? reinterpret_cast<const uint4*>(pf_key_ptr(a, s, h, kk, 0)) + half * 8 : nullptr;
-      const uint4* vs = kv_ok ? reinterpret_cast<const uint4*>(pf_key_ptr(a, s, h, kk, 1)) + half * 8 : nullptr;
+  // K and V of a key tile: thread t holds half (t/64) of key kt*64 + t%64 in registers. The next tile's loads are
+  // issued right after the current tile's Q K^T is issued, so they land while the tensor core and the softmax work.
+  const int kk_local = tid & 63, half = tid >> 6;
+  uint4 kreg[8], vreg[8];
+  auto load_tile = [&](int kt) {
+    const int kk = kt * kPfKeys + kk_local;
+    const bool kv_ok = kt < ntk && kk < L;
+    const uint4* ks = kv_ok ? reinterpret_cast<const uint4*>(pf_key_ptr(a, s, h, kk, 0)) + half * 8 : nullptr;
+    const uint4* vs = kv_ok ? reinterpret_cast<const uint4*>(pf_key_ptr(a, s, h, kk, 1)) + half * 8 : nullptr;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 kw = kv_ok ? __ldg(ks + c) : make_uint4(0, 0, 0, 0);
-        const uint4 vw = kv_ok ? __ldg(vs + c) : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(smem + PfSmem::kK + kmajor_off(kk_local, half * 8 + c, 2048)) = kw;
-        *reinterpret_cast<uint4*>(smem + PfSmem::kV + v_off(kk_local, half * 8 + c)) = vw;
-      }
+    for (int c = 0; c < 8; ++c) {
+      kreg[c] = kv_ok ? __ldg(ks + c) : make_uint4(0, 0, 0, 0);
+      vreg[c] = kv_ok ? __ldg(vs + c) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  load_tile(0);
+  for (int kt = 0; kt < ntk && ok; ++kt) {
+    // ---- K and V tiles into shared memory (the previous tile's MMAs have completed)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      *reinterpret_cast<uint4*>(smem + PfSmem::kK + kmajor_off(kk_local, half * 8 + c, 2048)) = kreg[c];
+      *reinterpret_cast<uint4*>(smem + PfSmem::kV + v_off(kk_local, half * 8 + c)) = vreg[c];
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -257,6 +291,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArg
                   ks > 0 ? 1u : 0u);
       umma_commit(bar_s);
     }
+    if (kt + 1 < ntk) load_tile(kt + 1);                     // in flight during this tile's MMAs and softmax
     if (!mbar_wait_bounded(bar_s, kt & 1)) {
       atomicOr(a.status, kStatusWaitTimeout);
       ok = false;
