@@ -57,7 +57,7 @@ def parse():
     p.add_argument("--cpu-seats", type=int, default=48)
     p.add_argument("--kernel-breakdown", action="store_true",
                    help="c5: add the per-kernel device time of one replayed frame (CUPTI via torch.profiler)")
-    p.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "admit", "prefill"], default="c2",
+    p.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "admit", "prefill", "ring"], default="c2",
                    help="c2: the headline decode step (default); c3: 1.7B decode + chunked-prefill mix; c4: CP steps")
     return p.parse_args()
 
@@ -452,6 +452,30 @@ def bench_aux(a):
         print(json.dumps({"metric": "chunked prefill 10 x 320 tokens into fresh pages (C3 prefill part)",
                           "workload": "prefill", "value": t_pre * 1e3, "unit": "us", "tflops": flops / t_pre / 1e9,
                           "flops": flops}), flush=True)
+        return
+    if a.workload == "ring":
+        # the codec decoder's windowed ring attention, one layer per launch: 256 streams, an 88-slot ring, 72-frame
+        # window, fp16; heads x head_dim 16 x 64 assumed (the codec's config is not part of the checkout)
+        Bs, H, hd, L, R = 256, 16, 64, 8, 88
+        K = torch.randn((Bs + 1, R, L, H, hd), generator=gen, device=dev).to(torch.float16)
+        V = torch.randn((Bs + 1, R, L, H, hd), generator=gen, device=dev).to(torch.float16)
+        rows = torch.arange(Bs, device=dev)
+        pos = torch.randint(100, 10000, (Bs,), generator=gen, device=dev)
+        res = {}
+        for n in (1, 4):
+            q = torch.randn((Bs, n, H, hd), generator=gen, device=dev).to(torch.float16)
+
+            def layer_calls():
+                for li in range(L):
+                    q3attn.ring_window_attn(q, q, q, K[:, :, li], V[:, :, li], rows, pos, 71, hd ** -0.5, False)
+            ms = timed(layer_calls, a.steps)
+            byt = Bs * H * (R + 2 * n) * hd * 2 * 2 + Bs * n * H * hd * 2 * 2
+            res[n] = {"us_per_layer": ms * 1e3 / L, "gbs": byt * L / ms / 1e6}
+        print(json.dumps({"metric": "codec decoder ring attention us per layer @256 streams (fp16, 16 x 64 heads)",
+                          "workload": "ring", "value": res[1]["us_per_layer"], "unit": "us per layer (1-frame chunk)",
+                          "chunk1": res[1], "chunk4": res[4], "layers_per_call": L,
+                          "reference_a100": "whole decoder call 14.1 / 44.5 ms at 256 streams x 1 / 4 frames"}),
+              flush=True)
         return
     if a.workload == "c4":
         B, L = a.seats, 5

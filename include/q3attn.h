@@ -203,6 +203,21 @@ int q3_silu_mul(const void* gate_up, int64_t gate_up_row_stride, void* out, int6
 int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rope* norm_rope, int64_t rows,
                          void* stream);
 
+/* Windowed ring attention of the streaming codec decoder, fp16, one transformer layer (engine/decoder_stream.py:147-181,
+ * ring mode). Stream b's rotated keys / values of recent frames live in a ring of `ring` slots (frame f in slot
+ * f % ring) at k_ring + ring_rows[b] * ring_stream_stride + slot * ring_slot_stride + head * head_dim (elements).
+ * The chunk's n frames at positions pos[b] .. pos[b]+n-1 (q / k_new / v_new [B, n, heads, head_dim] rows) attend
+ * over the ring frames within `past` frames before them and over the chunk's keys up to themselves, with the
+ * reference's fp16 rounding points (scores, P and each P.V half rounded to fp16). write_new != 0 also stores the
+ * chunk's K/V into ring slots (pos + j) % ring (the caller's index_copy_, decoder_stream.py:330-333).
+ * head_dim 64 or 128, ring <= 128, n <= min(17, ring - past). out: [B, n, heads * head_dim] fp16. */
+int q3_ring_window_attn(const void* q, const void* k_new, const void* v_new, int64_t qkv_batch_stride,
+                        int64_t qkv_frame_stride, void* k_ring, void* v_ring, int64_t ring_stream_stride,
+                        int64_t ring_slot_stride, const int64_t* ring_rows, const int64_t* pos, int32_t batch,
+                        int32_t n, int32_t heads, int32_t head_dim, int32_t ring, int32_t past, float scale,
+                        int32_t write_new, void* out, int64_t out_batch_stride, int64_t out_frame_stride,
+                        void* stream);
+
 /* Shared-prefix copy at admission (engine/arrivals.py:67-96 keeps, per (voice, language), the K/V of the k prompt
  * positions every request of that voice shares; arrivals.py:139-145 writes them into each admitted seat). For every
  * layer l < num_layers, batch row b and prefix row r < prefix_len, the K and V rows at

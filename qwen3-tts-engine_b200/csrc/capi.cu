@@ -548,6 +548,51 @@ int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
   return record(q3::launch_qk_norm_rope(a, static_cast<cudaStream_t>(stream)));
 }
 
+int q3_ring_window_attn(const void* q, const void* k_new, const void* v_new, int64_t qkv_batch_stride,
+                        int64_t qkv_frame_stride, void* k_ring, void* v_ring, int64_t ring_stream_stride,
+                        int64_t ring_slot_stride, const int64_t* ring_rows, const int64_t* pos, int32_t batch,
+                        int32_t n, int32_t heads, int32_t head_dim, int32_t ring, int32_t past, float scale,
+                        int32_t write_new, void* out, int64_t out_batch_stride, int64_t out_frame_stride,
+                        void* stream) {
+  if (batch < 0 || n < 0 || heads <= 0 || ring <= 0 || past < 0) return Q3_ERR_INVALID;
+  if ((head_dim != 64 && head_dim != 128) || ring > q3::kRingMaxSlots || n > q3::kRingMaxChunk) return Q3_ERR_UNSUPPORTED;
+  if (n > ring - past) return Q3_ERR_INVALID;               // the chunk's ring slots must lie outside every window
+  if (batch == 0 || n == 0) return Q3_OK;
+  if (!q || !k_new || !v_new || !k_ring || !v_ring || !ring_rows || !pos || !out || batch > 2147483647) return Q3_ERR_INVALID;
+  if (qkv_frame_stride < static_cast<int64_t>(heads) * head_dim || ring_slot_stride < static_cast<int64_t>(heads) * head_dim ||
+      out_frame_stride < static_cast<int64_t>(heads) * head_dim || qkv_batch_stride < 0 || ring_stream_stride < 0 ||
+      out_batch_stride < 0)
+    return Q3_ERR_INVALID;
+  if (!aligned(q, 16) || !aligned(k_new, 16) || !aligned(v_new, 16) || !aligned(k_ring, 16) || !aligned(v_ring, 16) ||
+      !aligned(out, 4) || (qkv_batch_stride % 8) || (qkv_frame_stride % 8) || (ring_stream_stride % 8) ||
+      (ring_slot_stride % 8) || (out_batch_stride % 2) || (out_frame_stride % 2))
+    return Q3_ERR_ALIGNMENT;
+  q3::RingArgs a{};
+  a.q = static_cast<const __half*>(q);
+  a.k_new = static_cast<const __half*>(k_new);
+  a.v_new = static_cast<const __half*>(v_new);
+  a.qkv_batch_stride = qkv_batch_stride;
+  a.qkv_frame_stride = qkv_frame_stride;
+  a.k_ring = static_cast<__half*>(k_ring);
+  a.v_ring = static_cast<__half*>(v_ring);
+  a.ring_stream_stride = ring_stream_stride;
+  a.ring_slot_stride = ring_slot_stride;
+  a.ring_rows = ring_rows;
+  a.pos = pos;
+  a.B = batch;
+  a.n = n;
+  a.H = heads;
+  a.hd = head_dim;
+  a.ring = ring;
+  a.past = past;
+  a.scale = scale;
+  a.write_new = write_new;
+  a.out = static_cast<__half*>(out);
+  a.out_batch_stride = out_batch_stride;
+  a.out_frame_stride = out_frame_stride;
+  return record(q3::launch_ring_attn(a, static_cast<cudaStream_t>(stream)));
+}
+
 int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v, int64_t kv_row_stride,
                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t num_seqs, int32_t max_seqlen_q,
                const int32_t* prefix_lens, const int32_t* seat_ids, void* k_pool, void* v_pool, int32_t num_pages,

@@ -3,6 +3,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace q3 {
@@ -175,6 +176,27 @@ struct QkNormRopeArgs {
   float eps;
 };
 cudaError_t launch_qk_norm_rope(const QkNormRopeArgs& a, cudaStream_t stream);
+
+constexpr int kRingMaxChunk = 17;     // frames per call: at most RING - PAST (88 - 71) in the reference
+constexpr int kRingMaxSlots = 128;
+struct RingArgs {
+  const __half* q;                 // [B, n, H, hd] rotated queries (batch / frame strides; heads hd apart)
+  const __half* k_new;             // [B, n, H, hd] the chunk's rotated keys
+  const __half* v_new;
+  long long qkv_batch_stride, qkv_frame_stride;
+  __half* k_ring;                  // stream row r, slot s, head h at r * ring_stream_stride + s * ring_slot_stride + h*hd
+  __half* v_ring;
+  long long ring_stream_stride, ring_slot_stride;
+  const int64_t* ring_rows;        // [B] ring row of each batch entry
+  const int64_t* pos;              // [B] frames decoded before this chunk
+  int B, n, H, hd, ring, past;
+  float scale;
+  int write_new;
+  __half* out;                     // [B, n, H * hd]
+  long long out_batch_stride, out_frame_stride;
+};
+size_t ring_smem_bytes(int ring, int hd);
+cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);
 
 struct PrefillArgs {
   const __nv_bfloat16* q;          // [Tq, 16, 128] rows, row stride q_stride (elements)

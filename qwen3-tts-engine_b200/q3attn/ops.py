@@ -304,6 +304,42 @@ def qk_norm_rope_(qkv: torch.Tensor, q_norm_w: torch.Tensor, k_norm_w: torch.Ten
     _lib.check(rc, "q3_qk_norm_rope_rows")
 
 
+@torch.library.custom_op("q3attn::ring_window_attn", mutates_args=("k_ring", "v_ring"))
+def ring_window_attn(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_ring: torch.Tensor,
+                     v_ring: torch.Tensor, ring_rows: torch.Tensor, pos: torch.Tensor, past: int, scale: float,
+                     write_new: bool = True) -> torch.Tensor:
+    """The streaming codec decoder's windowed ring attention for one layer (engine/decoder_stream.py:147-181), fp16.
+    q / k_new / v_new [B, n, H, hd] (rotated); k_ring / v_ring [S, RING, H, hd] views of the per-stream rings (e.g.
+    K[:, :, layer] of the decoder's [S, RING, L, H, hd] state); ring_rows [B] int64 ring row of each batch entry;
+    pos [B] int64 frames decoded before the chunk. With write_new the chunk's K/V go into ring slots (pos + j) % RING.
+    Returns [B, n, H * hd] fp16. One launch."""
+    lib = _lib.load()
+    for name, t in (("q", q), ("k_new", k_new), ("v_new", v_new), ("k_ring", k_ring), ("v_ring", v_ring)):
+        _need(t.is_cuda and t.dtype == torch.float16, f"{name} must be a CUDA fp16 tensor")
+    _need(q.dim() == 4 and k_new.shape == q.shape and v_new.shape == q.shape and q.stride(3) == 1 and
+          q.stride(2) == q.shape[3] and k_new.stride() == q.stride() and v_new.stride() == q.stride(),
+          "q / k_new / v_new must be [B, n, H, hd] with equal strides and contiguous heads")
+    B, n, H, hd = q.shape
+    _need(k_ring.dim() == 4 and k_ring.shape[2:] == (H, hd) and k_ring.stride(3) == 1 and k_ring.stride(2) == hd and
+          v_ring.shape == k_ring.shape and v_ring.stride() == k_ring.stride(), "rings must be [S, RING, H, hd] views")
+    _need(ring_rows.dtype == torch.int64 and pos.dtype == torch.int64 and ring_rows.numel() == B and
+          pos.numel() == B and ring_rows.is_contiguous() and pos.is_contiguous(), "ring_rows / pos: int64 [B]")
+    out = torch.empty(B, n, H * hd, dtype=torch.float16, device=q.device)
+    with torch.cuda.device(q.device):
+        rc = lib.q3_ring_window_attn(q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), q.stride(0), q.stride(1),
+                                     k_ring.data_ptr(), v_ring.data_ptr(), k_ring.stride(0), k_ring.stride(1),
+                                     ring_rows.data_ptr(), pos.data_ptr(), B, n, H, hd, k_ring.shape[1], int(past),
+                                     float(scale), int(bool(write_new)), out.data_ptr(), out.stride(0),
+                                     out.stride(1), _stream(q.device))
+    _lib.check(rc, "q3_ring_window_attn")
+    return out
+
+
+@ring_window_attn.register_fake
+def _(q, k_new, v_new, k_ring, v_ring, ring_rows, pos, past, scale, write_new=True):
+    return q.new_empty(q.shape[0], q.shape[1], q.shape[2] * q.shape[3])
+
+
 def pool_pointers(pools) -> torch.Tensor:
     """Device int64 array of the base addresses of per-layer pools (for kv_copy_prefix); build it once, outside
     capture, and keep it with the pools."""

@@ -13,6 +13,8 @@ only need to import) and calls:
   * Talker._cb0_logits + sample_topk (engine/talker.py:90-94, engine/ops.py:68-76), greedy      -> sampler.npz
   * FastAdmit._run with the per-voice prefix from Talker.prefill_hidden (engine/arrivals.py:85-91, 133-152),
                                  fp32                                                             -> admit.npz
+  * StreamDecoder._step / StreamCore.forward in ring mode on a small decoder (engine/decoder_stream.py:134-181),
+                                 fp32                                                             -> ring.npz
 Inputs are regenerated from seeds by q3attn.synth / q3attn.weights (torch CPU generators); each fixture stores a
 checksum of its inputs so a generator mismatch is detected before outputs are compared. The GPU box never runs this.
 """
@@ -287,6 +289,96 @@ def gen_admit(talker, arrivals, code_predictor):
     np.savez_compressed(os.path.join(HERE, "admit.npz"), **out)
 
 
+# --------------------------------------------------------------------------- codec decoder: windowed ring attention
+RING_CASE = dict(seed=31, S=3, D=256, H=4, hd=64, L=3, D0=32, C1=16, C2=8,
+                 calls=[([0, 2, 1], 4)] * 23 + [([0, 2, 1], 1), ([2, 0], 2), ([0, 2, 1], 3)])
+
+
+def ring_h(call: int, B: int, n: int, D: int, seed: int):
+    """Seeded transformer input [B, n, D] of call `call` (regenerated identically by the GPU test)."""
+    return synth.randn((B, n, D), synth.cpu_gen(seed * 1000 + call), 1.0)
+
+
+def ring_model(seed, D, H, hd, L):
+    """Decoder transformer layers with the attribute layout of the upstream modules StreamCore uses."""
+    g = synth.cpu_gen(seed)
+    N = types.SimpleNamespace
+
+    def lin(i, o, std):
+        m = torch.nn.Linear(i, o, bias=False)
+        m.weight.data = torch.randn(o, i, generator=g) * std
+        return m
+
+    def norm():
+        return N(weight=1 + 0.1 * torch.randn(D, generator=g), variance_epsilon=1e-5)
+    layers = []
+    for _ in range(L):
+        layers.append(N(input_layernorm=norm(), post_attention_layernorm=norm(),
+                        self_attn=N(q_proj=lin(D, H * hd, 0.06), k_proj=lin(D, H * hd, 0.06),
+                                    v_proj=lin(D, H * hd, 0.06), o_proj=lin(H * hd, D, 0.06)),
+                        self_attn_layer_scale=N(scale=0.5 + 0.1 * torch.randn(D, generator=g)),
+                        mlp=N(gate_proj=lin(D, 2 * D, 0.06), up_proj=lin(D, 2 * D, 0.06), down_proj=lin(2 * D, D, 0.06)),
+                        mlp_layer_scale=N(scale=0.5 + 0.1 * torch.randn(D, generator=g))))
+    inv_freq = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))
+    return layers, inv_freq
+
+
+def gen_ring(decoder_stream):
+    """StreamDecoder._step + StreamCore.forward in ring mode (engine/decoder_stream.py:134-181, 325-339), fp32, on a
+    small decoder: the transformer layers of ring_model, and around them the smallest stack forward() accepts (no
+    upsampling, one conv, one SnakeBeta, the final conv). The transformer input of each call is replaced by seeded
+    values (ring_h) and the transformer output is recorded at the input of output_proj."""
+    c = RING_CASE
+    D, H, hd, L, S = c["D"], c["H"], c["hd"], c["L"], c["S"]
+    layers, inv_freq = ring_model(c["seed"], D, H, hd, L)
+    core = object.__new__(decoder_stream.StreamCore)
+    torch.nn.Module.__init__(core)
+    core.dtype, core.nhwc, core.ring, core.lazy = torch.float32, False, True, False
+    core.H, core.hd, core.L = H, hd, L
+    core.layers = layers
+    core.inv_freq = inv_freq
+    core.rvq = torch.zeros(16, 4, c["D0"])
+    core.rvq_off = (torch.arange(16) * 4)[None, :, None]
+    core.pre_conv = torch.nn.Conv1d(c["D0"], c["D0"], 3)
+    calls = {"i": 0}
+    outs = []
+
+    class SeededH(torch.nn.Module):
+        def forward(self, x):
+            h = ring_h(calls["i"], x.shape[0], x.shape[1], D, c["seed"])
+            calls["i"] += 1
+            return h
+
+    class Record(torch.nn.Module):
+        def forward(self, x):
+            outs.append(x.clone())
+            return torch.zeros(x.shape[0], x.shape[1], c["C1"])
+    core.tr = types.SimpleNamespace(input_proj=SeededH(), norm=types.SimpleNamespace(weight=torch.ones(D),
+                                                                                   variance_epsilon=1e-5),
+                                    output_proj=Record())
+    core.ups, core.blocks, core.rates = [], [], []
+    core.conv0 = torch.nn.Conv1d(c["C1"], c["C2"], 7)
+    core.fin_conv = torch.nn.Conv1d(c["C2"], 1, 7)
+    core.sa0, core.sb0 = torch.ones(c["C2"], 1), torch.zeros(c["C2"], 1)
+    dec = object.__new__(decoder_stream.StreamDecoder)
+    dec.device, dec.dtype, dec.n_slots, dec.dummy = "cpu", torch.float32, S, S
+    dec.core = dec.fn = core
+    dec.pos = torch.zeros(S + 1, dtype=torch.long)
+    R = decoder_stream.RING
+    dec.state = [torch.zeros(S + 1, c["D0"], 2), torch.zeros(S + 1, R, L, H, hd), torch.zeros(S + 1, R, L, H, hd),
+                 torch.zeros(S + 1, c["C1"], 6), torch.zeros(S + 1, c["C2"], 6)]
+    with torch.inference_mode():
+        for seats, n in c["calls"]:
+            dec._step(torch.tensor(seats), torch.zeros(len(seats), 16, n, dtype=torch.long))
+    assert calls["i"] == len(c["calls"])
+    out = {f"h{k}": o.numpy().astype(np.float16) for k, o in enumerate(outs)}
+    out["K_last"] = dec.state[1][:S, :, L - 1].numpy().astype(np.float16)      # the deepest layer's rings
+    out["V_last"] = dec.state[2][:S, :, L - 1].numpy().astype(np.float16)
+    out["pos"] = dec.pos.numpy()
+    out["digest"] = np.array(digest(layers[0].self_attn.q_proj.weight, ring_h(0, 3, 4, D, c["seed"])))
+    np.savez_compressed(os.path.join(HERE, "ring.npz"), **out)
+
+
 # --------------------------------------------------------------------------- codebook-0 logit processing + greedy sampling
 def gen_sampler(talker, ops_mod):
     """Talker._cb0_logits (engine/talker.py:90-94) with an identity codec_head, so its input row IS the logit row, and
@@ -321,6 +413,9 @@ if __name__ == "__main__":
         gen_frames(talker, code_predictor)
     if not only or "admit" in only:
         gen_admit(talker, arrivals, code_predictor)
+    if not only or "ring" in only:
+        from engine import decoder_stream
+        gen_ring(decoder_stream)
     if not only or "sampler" in only:
         from engine import ops as ref_ops
         gen_sampler(talker, ref_ops)

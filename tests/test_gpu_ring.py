@@ -1,0 +1,98 @@
+"""GPU parity: the streaming codec decoder's windowed ring attention (engine/decoder_stream.py:147-181).
+
+* the kernel against the oracle restatement with the reference's fp16 rounding points, on random rings and positions
+  around every window and ring edge, plus the ring write (the chunk's K/V in slots (pos + j) % RING, nothing else
+  touched);
+* the decoder transformer step (q3attn.ring_decoder) against what the reference's own StreamDecoder._step /
+  StreamCore.forward computed in fp32 on a small decoder, over 26 chunks that wrap the 88-slot ring
+  (tests/golden/ring.npz)."""
+import os
+import types
+
+import numpy as np
+import pytest
+import torch
+
+import make_golden as mg
+from helpers import bits_equal
+from oracle import ring as OR
+from q3attn import synth
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+RING, PAST = 88, 71
+
+
+@pytest.fixture(scope="module")
+def q3():
+    import q3attn
+    q3attn._lib.load()
+    return q3attn
+
+
+@pytest.mark.parametrize("hd,H", [(64, 8), (128, 4)])
+@pytest.mark.parametrize("n", [1, 4, 17])
+def test_ring_attention_matches_oracle(q3, hd, H, n):
+    g = synth.cpu_gen(hd + n)
+    pos = torch.tensor([0, 1, 5, 70, 71, 72, 87, 88, 150, 1000], dtype=torch.int64)
+    B, S, L, li = len(pos), 12, 2, 1
+    rows = torch.randperm(S, generator=g)[:B]
+    K = synth.randn((S, RING, L, H, hd), g, 1.0, torch.float16)
+    V = synth.randn((S, RING, L, H, hd), g, 1.0, torch.float16)
+    q = synth.randn((B, n, H, hd), g, 1.0, torch.float16)
+    k = synth.randn((B, n, H, hd), g, 1.0, torch.float16)
+    v = synth.randn((B, n, H, hd), g, 1.0, torch.float16)
+    Kg, Vg = K.to(DEV), V.to(DEV)
+    out = q3.ring_window_attn(q.to(DEV), k.to(DEV), v.to(DEV), Kg[:, :, li], Vg[:, :, li], rows.to(DEV), pos.to(DEV),
+                              PAST, hd ** -0.5, True)
+    torch.cuda.synchronize()
+    ref = OR.ring_attention(q, k, v, K[rows, :, li], V[rows, :, li], pos, PAST, hd ** -0.5, emulate_fp16=True)
+    err = (out.float().cpu() - ref).abs()
+    assert float(err.max()) <= 1e-2 + 2e-2 * float(ref.abs().max()), f"max err {float(err.max()):.3e}"
+    # ring write: slots (pos + j) % RING of layer li get the chunk's rows, everything else is untouched
+    K2, V2 = K.clone(), V.clone()
+    for b in range(B):
+        for j in range(n):
+            K2[rows[b], (pos[b] + j) % RING, li] = k[b, j]
+            V2[rows[b], (pos[b] + j) % RING, li] = v[b, j]
+    assert bits_equal(Kg, K2) and bits_equal(Vg, V2)
+
+
+def test_decoder_transformer_matches_reference_stream(q3, golden_dir):
+    from q3attn.ring_decoder import RingTransformer, _rms
+    c = mg.RING_CASE
+    gold = np.load(os.path.join(golden_dir, "ring.npz"))
+    D, H, hd, L, S = c["D"], c["H"], c["hd"], c["L"], c["S"]
+    layers, inv_freq = mg.ring_model(c["seed"], D, H, hd, L)
+    assert str(gold["digest"]) == mg.digest(layers[0].self_attn.q_proj.weight, mg.ring_h(0, 3, 4, D, c["seed"]))
+
+    def dev(x):
+        if isinstance(x, torch.nn.Module):
+            return x.to(DEV, torch.float16)
+        if torch.is_tensor(x):
+            return x.to(DEV, torch.float16)
+        if isinstance(x, types.SimpleNamespace):
+            return types.SimpleNamespace(**{k: dev(v) for k, v in vars(x).items()})
+        return x
+    T = RingTransformer([dev(l) for l in layers], H, hd, inv_freq)
+    K = torch.zeros(S + 1, RING, L, H, hd, dtype=torch.float16, device=DEV)
+    V = torch.zeros_like(K)
+    pos = torch.zeros(S + 1, dtype=torch.int64, device=DEV)
+    norm = types.SimpleNamespace(weight=torch.ones(D, dtype=torch.float16, device=DEV), variance_epsilon=1e-5)
+    worst = 0.0
+    for call, (seats, n) in enumerate(c["calls"]):
+        rows = torch.tensor(seats, dtype=torch.int64, device=DEV)
+        h = mg.ring_h(call, len(seats), n, D, c["seed"]).to(DEV, torch.float16)
+        out = _rms(norm, T.step(h, pos[rows].contiguous(), rows, K, V)).float().cpu()
+        ref = torch.from_numpy(gold[f"h{call}"].astype(np.float32))
+        rel = float((out - ref).norm() / ref.norm())
+        worst = max(worst, rel)
+        assert rel < 2e-2, f"call {call}: transformer output relative error {rel:.3e}"
+        pos[rows] += n
+    torch.cuda.synchronize()
+    assert np.array_equal(pos.cpu().numpy(), gold["pos"])
+    for name, ring in (("K_last", K), ("V_last", V)):
+        got = ring[:S, :, L - 1].float().cpu()
+        ref = torch.from_numpy(gold[name].astype(np.float32))
+        rel = float((got - ref).norm() / ref.norm())
+        assert rel < 2e-2, f"{name}: relative error {rel:.3e}"
