@@ -148,6 +148,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// 16-byte asynchronous copy global -> shared memory (no register staging; completion by cp_async_wait_all).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // One-dimensional bulk copy global -> this CTA's shared memory, completion signalled on `bar` as transaction bytes.
 // dst/src 16-byte aligned, bytes a multiple of 16 (the callers copy whole 2048-byte token rows).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
