@@ -6,8 +6,9 @@
 // with the arithmetic of the reference's intended kernel cp_attn (engine/cp_attn.py:14-30): fp32 scores and softmax,
 // probabilities rounded to bf16 before P.V, fp32 accumulation, bf16 output. Slots >= n_live are not read.
 //
-// One CTA per seat, one warp per KV head; lane l owns dims 4l..4l+3 of both q heads of the group. All K and V rows are
-// loaded up front (at most 16 x 8 bytes each per lane) so the whole step costs one round of memory latency. With k_new
+// Two CTAs per seat (KV heads 0-3 and 4-7), one warp per KV head; lane l owns dims 4l..4l+3 of both q heads of the
+// group. The live K and V rows are staged in shared memory by asynchronous copies issued up front (one round of memory
+// latency, no registers held), sized by n_live, so the grid of 2 x batch small CTAs runs in about one wave. With k_new
 // given, the new row is stored to slot n_live-1 and used from registers. With the norm weights given (q3_cp_step_qkv,
 // the kernel instantiated with FUSE), q and k_new are raw projections: both q heads and the new k row get RMSNorm +
 // RoPE here (code_predictor.py:40-41).
@@ -16,37 +17,45 @@
 
 namespace q3 {
 
+constexpr int kCpWarps = 4;   // KV heads per CTA: a seat takes two CTAs
+
+// Shared memory of one CTA for n live slots: per warp K and V pieces [n][32 lanes] of 8 bytes, then P [32] floats.
+__host__ __device__ constexpr size_t cp_smem_bytes(int n) {
+  return static_cast<size_t>(kCpWarps) * (2 * n * 256 + 32 * sizeof(float));
+}
+
+__device__ __forceinline__ void cp_async8(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(smem_dst)), "l"(gsrc) : "memory");
+}
+
 template <bool FUSE>
-__global__ void __launch_bounds__(256, FUSE ? 2 : 0) cp_attn_kernel(const CpArgs a) {
-  __shared__ float pbuf[kKvHeads][32];
-  const int b = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(kCpWarps * 32) cp_attn_kernel(const CpArgs a) {
+  extern __shared__ __align__(16) uint8_t cp_smem[];
+  const int b = blockIdx.x, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y * kCpWarps + w;
   const int n = a.n_live, pnew = n - 1;
   const bool append = a.k_new != nullptr;
+  uint2* sK = reinterpret_cast<uint2*>(cp_smem) + w * (2 * n * 32);   // [slot][lane]: dims 4l..4l+3 of head h
+  uint2* sV = sK + n * 32;
+  float* pbuf = reinterpret_cast<float*>(cp_smem + static_cast<size_t>(kCpWarps) * 2 * n * 256) + w * 32;
 
+  // ---- the live K/V slots of head h, staged by asynchronous 8-byte copies (lane-contiguous: one 256-byte row per
+  //      warp instruction), all in flight while q / k_new load and the fused norm + RoPE run
+  const __nv_bfloat16* kb = a.K + static_cast<long long>(b) * a.sk_b + h * a.sk_h + 4 * lane;
+  const __nv_bfloat16* vb = a.V + static_cast<long long>(b) * a.sv_b + h * a.sv_h + 4 * lane;
+  for (int s = 0; s < n; ++s) {
+    if (append && s == pnew) continue;
+    cp_async8(sK + s * 32 + lane, kb + s * a.sk_s);
+    cp_async8(sV + s * 32 + lane, vb + s * a.sv_s);
+  }
   const __nv_bfloat16* qp = a.q + static_cast<long long>(b) * a.q_stride + (2 * h) * kHeadDim + 4 * lane;
   float4 q0 = bf16x4_to_float4(*reinterpret_cast<const uint2*>(qp));
   float4 q1 = bf16x4_to_float4(*reinterpret_cast<const uint2*>(qp + kHeadDim));
-
-  const __nv_bfloat16* kb = a.K + static_cast<long long>(b) * a.sk_b + h * a.sk_h + 4 * lane;
-  const __nv_bfloat16* vb = a.V + static_cast<long long>(b) * a.sv_b + h * a.sv_h + 4 * lane;
-  uint2 kw[16], vw[16];
   uint2 kn = make_uint2(0, 0), vn = make_uint2(0, 0);
   if (append) {
     const long long off = static_cast<long long>(b) * a.kv_new_stride + h * kHeadDim + 4 * lane;
     kn = *reinterpret_cast<const uint2*>(a.k_new + off);
     vn = *reinterpret_cast<const uint2*>(a.v_new + off);
-  }
-#pragma unroll
-  for (int s = 0; s < 16; ++s) {
-    if (s < n) {
-      if (append && s == pnew) {
-        kw[s] = kn;
-        vw[s] = vn;
-      } else {
-        kw[s] = *reinterpret_cast<const uint2*>(kb + s * a.sk_s);
-        vw[s] = *reinterpret_cast<const uint2*>(vb + s * a.sv_s);
-      }
-    }
   }
   if constexpr (FUSE) {   // fused q/k RMSNorm + RoPE
     const long long ro = static_cast<long long>(b) * a.rope_stride;
@@ -55,14 +64,15 @@ __global__ void __launch_bounds__(256, FUSE ? 2 : 0) cp_attn_kernel(const CpArgs
     q0 = rms_rope_head(q0, a.qn_w, cs, sn, a.eps, lane);
     q1 = rms_rope_head(q1, a.qn_w, cs, sn, a.eps, lane);
     kn = float4_to_bf16x4(rms_rope_head(bf16x4_to_float4(kn), a.kn_w, cs, sn, a.eps, lane));
-#pragma unroll
-    for (int s = 0; s < 16; ++s)
-      if (s == pnew) kw[s] = kn;
   }
   if (append) {
+    sK[pnew * 32 + lane] = kn;
+    sV[pnew * 32 + lane] = vn;
     *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(kb) + pnew * a.sk_s) = kn;
     *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(vb) + pnew * a.sv_s) = vn;
   }
+  cp_async_wait_all();
+  __syncwarp();
 
   const float sl = a.scale_log2;
   q0.x *= sl; q0.y *= sl; q0.z *= sl; q0.w *= sl;
@@ -71,7 +81,7 @@ __global__ void __launch_bounds__(256, FUSE ? 2 : 0) cp_attn_kernel(const CpArgs
 #pragma unroll
   for (int s = 0; s < 16; ++s) {
     if (s < n) {
-      const float4 k = bf16x4_to_float4(kw[s]);
+      const float4 k = bf16x4_to_float4(sK[s * 32 + lane]);
       sc[s] = q0.x * k.x + q0.y * k.y + q0.z * k.z + q0.w * k.w;
       sc[16 + s] = q1.x * k.x + q1.y * k.y + q1.z * k.z + q1.w * k.w;
     } else {
@@ -90,15 +100,15 @@ __global__ void __launch_bounds__(256, FUSE ? 2 : 0) cp_attn_kernel(const CpArgs
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   p = round_bf16(p / sum);                            // engine/cp_attn.py:26-27: P rounded to the model dtype
-  pbuf[h][lane] = p;
+  pbuf[lane] = p;
   __syncwarp();
 
   float4 o0 = make_float4(0, 0, 0, 0), o1 = o0;
 #pragma unroll
   for (int s = 0; s < 16; ++s) {
     if (s < n) {
-      const float p0 = pbuf[h][s], p1 = pbuf[h][16 + s];
-      const float4 v = bf16x4_to_float4(vw[s]);
+      const float p0 = pbuf[s], p1 = pbuf[16 + s];
+      const float4 v = bf16x4_to_float4(sV[s * 32 + lane]);
       o0.x += p0 * v.x; o0.y += p0 * v.y; o0.z += p0 * v.z; o0.w += p0 * v.w;
       o1.x += p1 * v.x; o1.y += p1 * v.y; o1.z += p1 * v.z; o1.w += p1 * v.w;
     }
@@ -110,10 +120,12 @@ __global__ void __launch_bounds__(256, FUSE ? 2 : 0) cp_attn_kernel(const CpArgs
 
 cudaError_t launch_cp_attn(const CpArgs& a, cudaStream_t stream) {
   if (a.B == 0) return cudaSuccess;
+  const dim3 grid(a.B, kKvHeads / kCpWarps);
+  const size_t bytes = cp_smem_bytes(a.n_live);
   if (a.qn_w != nullptr)
-    cp_attn_kernel<true><<<a.B, 256, 0, stream>>>(a);
+    cp_attn_kernel<true><<<grid, kCpWarps * 32, bytes, stream>>>(a);
   else
-    cp_attn_kernel<false><<<a.B, 256, 0, stream>>>(a);
+    cp_attn_kernel<false><<<grid, kCpWarps * 32, bytes, stream>>>(a);
   return cudaGetLastError();
 }
 
