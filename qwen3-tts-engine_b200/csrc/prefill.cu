@@ -32,10 +32,11 @@ constexpr int kPfTmemCols = 256;             // S (64 columns) + O (128 columns)
 constexpr uint32_t kPfSCol = 0, kPfOCol = 128;
 
 struct PfSmem {
+  static constexpr int kTile = kPfKeys * 256;                // one K (or V) tile: 64 keys x 128 dims, 16 KB
   static constexpr int kQ = 0;                               // 128 rows x 128 dims, K-major   32 KB
-  static constexpr int kK = kQ + 128 * 256;                  // 64 keys x 128 dims, K-major    16 KB
-  static constexpr int kV = kK + kPfKeys * 256;              // 128 dims x 64 keys, MN-major   16 KB
-  static constexpr int kP = kV + kPfKeys * 256;              // 128 rows x 64 keys, K-major    16 KB
+  static constexpr int kK = kQ + 128 * 256;                  // 2 x [64 keys x 128 dims], K-major (double buffer)
+  static constexpr int kV = kK + 2 * kTile;                  // 2 x [128 dims x 64 keys], MN-major
+  static constexpr int kP = kV + 2 * kTile;                  // 128 rows x 64 keys, K-major    16 KB
   static constexpr int kBar = kP + 128 * kPfKeys * 2;        // bar_s, bar_o
   static constexpr int kTmemSlot = kBar + 16;
   static constexpr int kBytes = kTmemSlot + 16;
@@ -68,6 +69,14 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint6
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
       :
       : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+// 2^x by the PTX approximate base-2 exponential (relative error ~2^-22, flushes denormals): the probabilities are
+// rounded to bf16 right after.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -163,16 +172,18 @@ __device__ __forceinline__ const __nv_bfloat16* pf_key_ptr(const PrefillArgs& a,
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int qt = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
+  const int h = blockIdx.y, seq = blockIdx.z;
   const PfSeq s = pf_seq(a, seq);
   const int ntq = s.R > 0 ? (s.R + kPfQRows - 1) / kPfQRows : 1;
-  if (qt >= ntq) return;                                     // uniform; nothing allocated yet
+  // the last query tiles see the most keys: they take the lowest block indices, so the heavy CTAs start first
+  const int qt = ntq - 1 - static_cast<int>(blockIdx.x);
+  if (qt < 0) return;                                        // uniform; nothing allocated yet
 
   // ---- fused page write: head h of new rows r with r % ntq == qt go to positions P + r of the seat's pages. Every
   //      (row, K or V, 16-byte chunk) copy is independent: each thread takes kPfWriteBatch of them at a time and
   //      issues all their table and row loads before any store, so the whole CTA's loads are in flight together.
   if (a.write_kv) {
-    constexpr int kPfWriteBatch = 8;
+    constexpr int kPfWriteBatch = 16;
     const int nrows = s.Nn > qt ? (s.Nn - qt + ntq - 1) / ntq : 0;
     const int total = nrows * 32;                            // 16 K chunks + 16 V chunks per row
 #pragma unroll 1
@@ -271,23 +282,38 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArg
       vreg[c] = kv_ok ? __ldg(vs + c) : make_uint4(0, 0, 0, 0);
     }
   };
+  // Per key tile kt (K/V in buffer kt & 1): store the tile, one barrier, then a single thread issues O += P(kt-1) V(kt-1)
+  // and S = Q K(kt)^T back to back under one commit. tcgen05.commit tracks every earlier MMA of the thread, so when
+  // S(kt) is ready P(kt-1) V(kt-1) has finished too: P and O may then be rewritten, and the other K/V buffer (tile
+  // kt-1) is free for tile kt+1. The last P V is issued after the loop.
+  auto issue_pv = [&](int kt_pv) {
+    const uint32_t vbuf = sV + (kt_pv & 1) * PfSmem::kTile;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+      umma_bf16(t_o, umma_smem_desc(sP + ks * 256, 128, 1024), umma_smem_desc(vbuf + ks * 256, 128, 1024), kIdescPV,
+                (kt_pv > 0 || ks > 0) ? 1u : 0u);
+  };
   load_tile(0);
   for (int kt = 0; kt < ntk && ok; ++kt) {
-    // ---- K and V tiles into shared memory (the previous tile's MMAs have completed)
+    const int buf = kt & 1;
+    // ---- K and V tiles into buffer `buf` (its previous tile, kt-2, finished both MMAs)
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      *reinterpret_cast<uint4*>(smem + PfSmem::kK + kmajor_off(kk_local, half * 8 + c, 2048)) = kreg[c];
-      *reinterpret_cast<uint4*>(smem + PfSmem::kV + v_off(kk_local, half * 8 + c)) = vreg[c];
+      *reinterpret_cast<uint4*>(smem + PfSmem::kK + buf * PfSmem::kTile + kmajor_off(kk_local, half * 8 + c, 2048)) =
+          kreg[c];
+      *reinterpret_cast<uint4*>(smem + PfSmem::kV + buf * PfSmem::kTile + v_off(kk_local, half * 8 + c)) = vreg[c];
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // ---- S = Q K^T
+    // ---- O += P(kt-1) V(kt-1), then S = Q K(kt)^T
     if (tid == 0) {
+      if (kt > 0) issue_pv(kt - 1);
+      const uint32_t kbuf = sK + buf * PfSmem::kTile;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks)
-        umma_bf16(t_s, umma_smem_desc(sQ + ks * 256, 128, 2048), umma_smem_desc(sK + ks * 256, 128, 2048), kIdescQK,
+        umma_bf16(t_s, umma_smem_desc(sQ + ks * 256, 128, 2048), umma_smem_desc(kbuf + ks * 256, 128, 2048), kIdescQK,
                   ks > 0 ? 1u : 0u);
       umma_commit(bar_s);
     }
@@ -304,38 +330,54 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArg
     tmem_ld32(t_s + lane_base, sv[0]);
     tmem_ld32(t_s + lane_base + 32, sv[1]);
     tc_wait_ld();
-    float cmax = -INFINITY;
+    // masking per element only on tiles that some row of the warp does not fully see (the causal diagonal, the last
+    // keys); the maxima and sums run in 4 independent chains
+    float cm4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    const int tile_last = kt * kPfKeys + kPfKeys - 1;
+    if (__all_sync(0xffffffffu, row_valid && tile_last <= my_limit && tile_last < L)) {
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+      for (int u = 0; u < 2; ++u)
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int kk = kt * kPfKeys + u * 32 + i;
-        const bool vis = row_valid ? (kk <= my_limit && kk < L) : (kk < L);
-        sv[u][i] = vis ? sv[u][i] * a.scale_log2 : -INFINITY;
-        cmax = fmaxf(cmax, sv[u][i]);
-      }
+        for (int i = 0; i < 32; ++i) {
+          sv[u][i] *= a.scale_log2;
+          cm4[i & 3] = fmaxf(cm4[i & 3], sv[u][i]);
+        }
+    } else {
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int kk = kt * kPfKeys + u * 32 + i;
+          const bool vis = row_valid ? (kk <= my_limit && kk < L) : (kk < L);
+          sv[u][i] = vis ? sv[u][i] * a.scale_log2 : -INFINITY;
+          cm4[i & 3] = fmaxf(cm4[i & 3], sv[u][i]);
+        }
+    }
+    const float cmax = fmaxf(fmaxf(cm4[0], cm4[1]), fmaxf(cm4[2], cm4[3]));
     // the running max moves (and O is rescaled) only when it would grow by more than 8 (a factor 256 in P)
     const bool grow = cmax > m_run + 8.f || (m_run == -INFINITY && cmax > -INFINITY);
     const float m_new = grow ? cmax : m_run;
     const float alpha = grow ? exp2f(m_run - m_new) : 1.f;   // 0 on the first visible tile
-    float lsum = 0.f;
+    float ls4[4] = {0.f, 0.f, 0.f, 0.f};
     uint32_t pk[32];
+    const float mm = m_new == -INFINITY ? 0.f : m_new;       // a row with nothing visible yet: every sv is -inf, p = 0
 #pragma unroll
     for (int u = 0; u < 2; ++u)
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
-        const float p0 = m_new == -INFINITY ? 0.f : exp2f(sv[u][i] - m_new);
-        const float p1 = m_new == -INFINITY ? 0.f : exp2f(sv[u][i + 1] - m_new);
-        lsum += p0 + p1;
+        const float p0 = ex2_approx(sv[u][i] - mm);
+        const float p1 = ex2_approx(sv[u][i + 1] - mm);
+        ls4[(i >> 1) & 3] += p0 + p1;
         pk[u * 16 + i / 2] = pack_bf16x2(p0, p1);
       }
+    const float lsum = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
     l_run = l_run * alpha + lsum;
     m_run = m_new;
 #pragma unroll
     for (int c = 0; c < 8; ++c)
       *reinterpret_cast<uint4*>(smem + PfSmem::kP + kmajor_off(tid, c, 1024)) =
           make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-    // ---- rescale O where a max moved (O holds the finished previous tiles; tile 0 starts O from zero instead)
+    // ---- rescale O where a max moved (O holds tiles 0..kt-1, all finished; tile 0 starts O from zero instead)
     if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -348,19 +390,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArg
       }
       tc_wait_st();
     }
+  }
+  // ---- the last O += P V
+  if (ok && ntk > 0) {
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // ---- O += P V
     if (tid == 0) {
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma_bf16(t_o, umma_smem_desc(sP + ks * 256, 128, 1024), umma_smem_desc(sV + ks * 256, 128, 1024), kIdescPV,
-                  (kt > 0 || ks > 0) ? 1u : 0u);
+      issue_pv(ntk - 1);
       umma_commit(bar_o);
     }
-    if (!mbar_wait_bounded(bar_o, kt & 1)) {
+    if (!mbar_wait_bounded(bar_o, 0)) {
       atomicOr(a.status, kStatusWaitTimeout);
       ok = false;
     }
