@@ -335,6 +335,11 @@ static int cp_common(q3::CpArgs& a, const void* q, int64_t q_batch_stride, void*
   if (batch == 0) return Q3_OK;
   if (!q || !K || !V || !out) return Q3_ERR_INVALID;
   if (q_batch_stride < q3::kQHeads * q3::kHeadDim || out_stride < q3::kQHeads * q3::kHeadDim) return Q3_ERR_INVALID;
+  int dev = 0, rc;
+  if ((rc = current_device(&dev)) != Q3_OK) return rc;
+  uint32_t* st = nullptr;
+  if ((rc = status_ptr(dev, &st)) != Q3_OK) return rc;
+  a.status = st;
   if (!aligned(q, 8) || !aligned(K, 8) || !aligned(V, 8) || !aligned(out, 8) || (q_batch_stride % 4) || (out_stride % 4) ||
       (kb % 4) || (kh % 4) || (ks % 4) || (vb % 4) || (vh % 4) || (vs % 4))
     return Q3_ERR_ALIGNMENT;
@@ -346,6 +351,9 @@ static int cp_common(q3::CpArgs& a, const void* q, int64_t q_batch_stride, void*
   a.sv_b = vb; a.sv_h = vh; a.sv_s = vs;
   a.B = batch;
   a.n_live = n_live;
+  // one bulk copy per (seat, head) when its live slots are one contiguous 16-byte aligned range
+  a.bulk = (ks == q3::kHeadDim && vs == q3::kHeadDim && aligned(K, 16) && aligned(V, 16) && (kb % 8) == 0 &&
+            (kh % 8) == 0 && (vb % 8) == 0 && (vh % 8) == 0) ? 1 : 0;
   a.scale_log2 = scale * q3::kLog2e;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.out_stride = out_stride;

@@ -7,8 +7,10 @@
 // probabilities rounded to bf16 before P.V, fp32 accumulation, bf16 output. Slots >= n_live are not read.
 //
 // Two CTAs per seat (KV heads 0-3 and 4-7), one warp per KV head; lane l owns dims 4l..4l+3 of both q heads of the
-// group. The live K and V rows are staged in shared memory by asynchronous copies issued up front (one round of memory
-// latency, no registers held), sized by n_live, so the grid of 2 x batch small CTAs runs in about one wave. With k_new
+// group. The live K and V rows are staged in shared memory by copies issued up front (one round of memory latency, no
+// registers held), sized by n_live, so the grid of 2 x batch small CTAs runs in about one wave: one TMA bulk copy per
+// (head, K/V) when the slot rows of a head are one contiguous, 16-byte aligned range (the engine's [B, 8, 16, 128]
+// caches), else 8-byte asynchronous copies per lane. With k_new
 // given, the new row is stored to slot n_live-1 and used from registers. With the norm weights given (q3_cp_step_qkv,
 // the kernel instantiated with FUSE), q and k_new are raw projections: both q heads and the new k row get RMSNorm +
 // RoPE here (code_predictor.py:40-41).
@@ -19,9 +21,10 @@ namespace q3 {
 
 constexpr int kCpWarps = 4;   // KV heads per CTA: a seat takes two CTAs
 
-// Shared memory of one CTA for n live slots: per warp K and V pieces [n][32 lanes] of 8 bytes, then P [32] floats.
+// Shared memory of one CTA for n live slots: per warp K and V pieces [n][32 lanes] of 8 bytes (row-major [n][128]
+// bf16), then P [32] floats per warp, then one mbarrier per warp.
 __host__ __device__ constexpr size_t cp_smem_bytes(int n) {
-  return static_cast<size_t>(kCpWarps) * (2 * n * 256 + 32 * sizeof(float));
+  return static_cast<size_t>(kCpWarps) * (2 * n * 256 + 32 * sizeof(float) + sizeof(uint64_t));
 }
 
 __device__ __forceinline__ void cp_async8(void* smem_dst, const void* gsrc) {
@@ -38,15 +41,27 @@ __global__ void __launch_bounds__(kCpWarps * 32) cp_attn_kernel(const CpArgs a) 
   uint2* sK = reinterpret_cast<uint2*>(cp_smem) + w * (2 * n * 32);   // [slot][lane]: dims 4l..4l+3 of head h
   uint2* sV = sK + n * 32;
   float* pbuf = reinterpret_cast<float*>(cp_smem + static_cast<size_t>(kCpWarps) * 2 * n * 256) + w * 32;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(cp_smem + static_cast<size_t>(kCpWarps) * (2 * n * 256 + 128)) + w;
 
-  // ---- the live K/V slots of head h, staged by asynchronous 8-byte copies (lane-contiguous: one 256-byte row per
-  //      warp instruction), all in flight while q / k_new load and the fused norm + RoPE run
+  // ---- the live K/V slots of head h (all but the appended one), in flight while q / k_new load and the fused norm +
+  //      RoPE run: one bulk copy each for K and V, or asynchronous 8-byte copies (one 256-byte row per warp
+  //      instruction)
   const __nv_bfloat16* kb = a.K + static_cast<long long>(b) * a.sk_b + h * a.sk_h + 4 * lane;
   const __nv_bfloat16* vb = a.V + static_cast<long long>(b) * a.sv_b + h * a.sv_h + 4 * lane;
-  for (int s = 0; s < n; ++s) {
-    if (append && s == pnew) continue;
-    cp_async8(sK + s * 32 + lane, kb + s * a.sk_s);
-    cp_async8(sV + s * 32 + lane, vb + s * a.sv_s);
+  const int n_copy = append ? n - 1 : n;
+  if (a.bulk) {
+    if (lane == 0 && n_copy > 0) {
+      mbar_init(bar, 1);
+      fence_mbar_init();
+      mbar_arrive_expect_tx(bar, static_cast<uint32_t>(2 * n_copy * kHeadBytes));
+      bulk_g2s(sK, kb, n_copy * kHeadBytes, bar);
+      bulk_g2s(sV, vb, n_copy * kHeadBytes, bar);
+    }
+  } else {
+    for (int s = 0; s < n_copy; ++s) {
+      cp_async8(sK + s * 32 + lane, kb + s * a.sk_s);
+      cp_async8(sV + s * 32 + lane, vb + s * a.sv_s);
+    }
   }
   const __nv_bfloat16* qp = a.q + static_cast<long long>(b) * a.q_stride + (2 * h) * kHeadDim + 4 * lane;
   float4 q0 = bf16x4_to_float4(*reinterpret_cast<const uint2*>(qp));
@@ -71,7 +86,20 @@ __global__ void __launch_bounds__(kCpWarps * 32) cp_attn_kernel(const CpArgs a) 
     *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(kb) + pnew * a.sk_s) = kn;
     *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(vb) + pnew * a.sv_s) = vn;
   }
-  cp_async_wait_all();
+  if (a.bulk) {
+    __syncwarp();   // the barrier's initialisation (lane 0) before any lane waits on it
+    if (n_copy > 0 && !mbar_wait_bounded(bar, 0)) {
+      // the copies did not land within the limit: flag it, leave the outputs untouched, and keep the shared memory
+      // alive (bounded) until the copies in flight are done
+      if (lane == 0) {
+        atomicOr(a.status, kStatusWaitTimeout);
+        mbar_wait_bounded(bar, 0, 100000000ull);
+      }
+      return;
+    }
+  } else {
+    cp_async_wait_all();
+  }
   __syncwarp();
 
   const float sl = a.scale_log2;

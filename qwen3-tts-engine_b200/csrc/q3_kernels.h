@@ -99,6 +99,8 @@ struct CpArgs {
   long long sv_b, sv_h, sv_s;
   int B;
   int n_live;                      // slots attended: 1..16; with k_new the new row lands in slot n_live - 1
+  int bulk;                        // 1: slot rows contiguous (stride 128) and every (seat, head) base 16-byte aligned
+  uint32_t* status;                // error bits (a bulk-copy wait that gave up)
   float scale_log2;
   __nv_bfloat16* out;              // [B, 16*128] rows, batch stride out_stride
   long long out_stride;

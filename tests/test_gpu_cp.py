@@ -56,6 +56,29 @@ def test_cp_step_fused_append(q3, p):
     assert bits_equal(gK[l, B:], Kall[l, B:]) and bits_equal(gK[:l], Kall[:l]), "rows outside the live batch touched"
 
 
+@pytest.mark.parametrize("layout", ["slot_stride_256", "base_8_byte_aligned"])
+def test_cp_attn_strided_fallback(q3, layout):
+    """K/V views that a single bulk copy per (seat, head) cannot stage (slot rows not contiguous, or a base that is
+    only 8-byte aligned) take the per-lane copy path and give the same results."""
+    n_live, B = 11, 48
+    d = synth.cp_case(n_live, B)
+    if layout == "slot_stride_256":
+        Kb = torch.zeros((B, 8, 16, 256), dtype=torch.bfloat16, device=DEV)
+        Vb = torch.zeros_like(Kb)
+        K, V = Kb[..., :128], Vb[..., :128]
+    else:
+        Kb = torch.zeros(B * 8 * 16 * 128 + 4, dtype=torch.bfloat16, device=DEV)
+        Vb = torch.zeros_like(Kb)
+        K, V = Kb[4:].view(B, 8, 16, 128), Vb[4:].view(B, 8, 16, 128)
+    K.copy_(d["K"].to(DEV))
+    V.copy_(d["V"].to(DEV))
+    poison_allocator((B, 2048))
+    out = q3.cp_attn(d["q"].to(DEV), K, V, n_live, SCALE)
+    torch.cuda.synchronize()
+    ref = OA.cp_attention(d["q"], d["K"], d["V"], n_live, SCALE)
+    assert_close_attn(out, ref, what=f"cp fallback {layout}")
+
+
 def test_cp_attn_against_reference_golden(q3, golden_dir):
     """Against CodePredictor._post's attention computed by the reference itself (fp32 inputs rounded to bf16 here)."""
     g = np.load(os.path.join(golden_dir, "cp_attn.npz"))
