@@ -5,17 +5,21 @@
 //     (where(lg < 0, lg * rep, lg / rep)); + the suppress row; EOS masked to -inf while ngen[seat] < min_new
 //   sample_topk (engine/ops.py:68-76): topk(k) -> softmax(vals / temperature) -> multinomial(1) -> gather
 //   the embedding lookup of the sampled id that feeds the next step (engine/code_predictor.py:68, 71)
-// k = 1 is greedy (the row's maximum; equal maxima resolve to the lowest index).
+// k = 1 is greedy (the row's maximum; equal maxima resolve to the lowest index): one block-wide max over
+// (key, -index), no selection.
 //
-// Selection: the processed row is held as order-preserving 32-bit keys, 16 per thread at most (vocab <= 4096). The
-// k-th largest key is found by a 4-pass most-significant-digit radix select over 8-bit digits (a shared 256-bin
-// histogram per pass); the k winners (keys above it, then the lowest-index keys equal to it) are gathered in index
-// order by a block scan and ranked by (value desc, index asc).
+// Selection (k > 1): the processed row is held as order-preserving 32-bit keys, 16 per thread at most (vocab <= 4096).
+// The k-th largest key T is found by a 4-pass most-significant-digit radix select over 8-bit digits (a shared 256-bin
+// histogram per pass); the k winners are the keys above T and the lowest-index keys equal to T. They are placed by
+// shared-memory atomics (order is irrelevant: they are ranked next) -- the keys equal to T into a side list whose
+// lowest indices are kept -- unless more than kSampleMaxTopK keys equal T (massive ties), in which case an ordered
+// block scan gathers them. The winners are then ranked by (value desc, index asc).
 // Sampling: p_j = exp((v_j - v_0) / T) over the sorted winners; one uniform u in [0, 1) from Philox4x32-10 (Salmon,
 // Moraes, Dror, Shaw, "Parallel random numbers: as easy as 1, 2, 3", SC 2011) keyed by the caller's seed with counter
 // (row, launch index); the pick is the first j whose inclusive prefix sum exceeds u * sum. The launch index lives in
-// device memory: every CTA reads it, and the last CTA to finish (atomic ticket) advances it, so CUDA-graph replays
-// draw fresh numbers and a run is reproducible from (seed, starting index).
+// device memory: every CTA reads it and then takes an atomic ticket, and the CTA holding the last ticket (every CTA
+// has read the index by then) advances it, so CUDA-graph replays draw fresh numbers and a run is reproducible from
+// (seed, starting index). The ticket is taken at the start, off the end of the kernel's critical path.
 #include "q3_common.cuh"
 #include "q3_kernels.h"
 
@@ -74,14 +78,26 @@ __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const Sampl
   __shared__ int cand_idx[kSampleMaxTopK];
   __shared__ uint32_t sort_key[kSampleMaxTopK];
   __shared__ int sort_idx[kSampleMaxTopK];
+  __shared__ int eq_idx[kSampleMaxTopK];
+  __shared__ unsigned long long warp_best[kSampleThreads / 32];
   __shared__ uint32_t s_prefix;
   __shared__ int s_krem;
+  __shared__ unsigned s_eq;
+  __shared__ int s_ngt, s_neq;
   __shared__ int s_pick;
   __shared__ unsigned long long s_launch;
 
   const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
   const int V = a.V, K = a.k;
-  if (tid == 0) s_launch = *reinterpret_cast<volatile unsigned long long*>(a.rng_state);
+  if (tid == 0) {
+    s_launch = *reinterpret_cast<volatile unsigned long long*>(a.rng_state);
+    __threadfence();   // the read of the launch index is performed before this CTA's ticket
+    const unsigned long long t = atomicAdd(a.rng_state + 1, 1ull);
+    if (t == static_cast<unsigned long long>(gridDim.x) - 1) {   // the last ticket: reset it, advance the index
+      a.rng_state[1] = 0ull;
+      atomicAdd(a.rng_state, 1ull);
+    }
+  }
   if (tid < kSampleMaxTopK) {   // defined contents whatever the selection leaves: every index read below is < V
     cand_key[tid] = 0u;
     cand_idx[tid] = 0;
@@ -112,10 +128,41 @@ __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const Sampl
     }
   }
 
+  if (K == 1) {
+    // ---- greedy: the largest (key, -index); padding slots never compete
+    unsigned long long best = 0ull;
+#pragma unroll
+    for (int j = 0; j < kSamplePerThread; ++j) {
+      const int v = j * kSampleThreads + tid;
+      if (v < V) {
+        const unsigned long long c = (static_cast<unsigned long long>(key[j]) << 32) | (0xffffffffu - static_cast<uint32_t>(v));
+        best = c > best ? c : best;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long y = __shfl_xor_sync(0xffffffffu, best, o);
+      best = y > best ? y : best;
+    }
+    if (lane == 0) warp_best[tid >> 5] = best;
+    __syncthreads();
+    if (tid == 0) {
+      unsigned long long m = warp_best[0];
+#pragma unroll
+      for (int w = 1; w < kSampleThreads / 32; ++w) m = warp_best[w] > m ? warp_best[w] : m;
+      const int id = static_cast<int>(0xffffffffu - static_cast<uint32_t>(m));
+      s_pick = id;
+      a.out_ids[b * a.out_stride] = id;
+    }
+    __syncthreads();
+  } else {
   // ---- radix select of the K-th largest key
   if (tid == 0) {
     s_prefix = 0u;
     s_krem = K;
+    s_eq = 0u;
+    s_ngt = 0;
+    s_neq = 0;
   }
   uint32_t mask = 0u;
 #pragma unroll 1
@@ -149,17 +196,21 @@ __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const Sampl
       const unsigned hit = __ballot_sync(0xffffffffu, incl >= static_cast<unsigned>(krem));
       const int first = __ffs(hit) - 1;   // krem <= elements matching the prefix, so some lane is hit
       if (lane == first) {
-        unsigned above = excl;
+        unsigned above = excl, at = 0u;
         int d = 255 - 8 * lane;
-        for (int i = 0; i < 8; ++i) {
-          if (above + c[i] >= static_cast<unsigned>(krem)) {
+        bool found = false;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {   // static indexing: c stays in registers
+          if (!found && above + c[i] >= static_cast<unsigned>(krem)) {
             d = 255 - 8 * lane - i;
-            break;
+            at = c[i];
+            found = true;
           }
-          above += c[i];
+          if (!found) above += c[i];
         }
         s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
         s_krem = krem - static_cast<int>(above);
+        s_eq = at;   // keys matching the new prefix (after the last pass: the keys equal to T)
       }
     }
     mask |= 255u << shift;
@@ -167,7 +218,34 @@ __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const Sampl
   }
   const uint32_t T = s_prefix;   // the K-th largest key; s_krem of the keys equal to it are taken
   const int take_eq = s_krem;
+  const int eq_total = static_cast<int>(s_eq);
 
+  if (eq_total <= kSampleMaxTopK) {
+    // ---- winners by atomics: keys > T (fewer than K of them) straight into cand, keys == T into eq_idx
+#pragma unroll
+    for (int j = 0; j < kSamplePerThread; ++j) {
+      const int v = j * kSampleThreads + tid;
+      if (v < V) {
+        if (key[j] > T) {
+          const int slot = atomicAdd(&s_ngt, 1);
+          cand_key[slot] = key[j];
+          cand_idx[slot] = v;
+        } else if (key[j] == T) {
+          eq_idx[atomicAdd(&s_neq, 1)] = v;
+        }
+      }
+    }
+    __syncthreads();
+    if (tid < eq_total) {   // the take_eq lowest indices among the keys equal to T follow the keys above it
+      const int mi = eq_idx[tid];
+      int r = 0;
+      for (int j = 0; j < eq_total; ++j) r += eq_idx[j] < mi ? 1 : 0;
+      if (r < take_eq) {
+        cand_key[s_ngt + r] = T;
+        cand_idx[s_ngt + r] = mi;
+      }
+    }
+  } else {
   // ---- gather the K winners in index order (keys > T, then the lowest-index keys == T)
   int gt_run = 0, eq_run = 0;
 #pragma unroll
@@ -189,6 +267,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const Sampl
     }
     gt_run += gt_tot;
     eq_run += eq_tot;
+  }
   }
   __syncthreads();
 
@@ -253,6 +332,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const Sampl
     }
   }
   __syncthreads();
+  }
 
   // ---- the embedding row of the sampled id
   if (a.emb) {
@@ -260,16 +340,6 @@ __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const Sampl
     const uint2* src = reinterpret_cast<const uint2*>(a.emb + id * a.emb_stride);
     uint2* dst = reinterpret_cast<uint2*>(a.emb_out + b * a.emb_out_stride);
     for (int i = tid; i < a.emb_dim / 4; i += kSampleThreads) dst[i] = src[i];
-  }
-
-  // ---- the last CTA out advances the launch index (every CTA has read it by now) and resets the ticket
-  if (tid == 0) {
-    __threadfence();
-    const unsigned long long t = atomicAdd(a.rng_state + 1, 1ull);
-    if (t == static_cast<unsigned long long>(gridDim.x) - 1) {
-      a.rng_state[1] = 0ull;
-      atomicAdd(a.rng_state, 1ull);
-    }
   }
 }
 

@@ -99,6 +99,26 @@ def test_edges_ties_small_vocab_and_masked_rows(q3):
     assert rng.launch_index == 4
 
 
+def test_ties_at_the_kth_value(q3):
+    """Ties at the k-th largest value, few enough for the atomic winner placement (<= 64 equal keys): the lowest
+    indices among them are the winners, whatever order the atomics placed them in."""
+    gen = synth.cpu_gen(21)
+    B, V, k = 40, 3000, 15
+    lg = synth.randn((B, V), gen, 1.0) - 10.0                   # below every planted value
+    for b in range(B):
+        perm = torch.randperm(V, generator=gen)
+        lg[b, perm[:10]] = 5.0                                  # 10 keys above the threshold
+        lg[b, perm[10:10 + 20 + b % 30]] = 3.0                  # 20..49 keys equal to it: 5 of them are taken
+    rng = q3.SamplerRng(8, DEV)
+    ids = q3.sample_topk(lg.to(DEV), 1.0, k, rng)
+    torch.cuda.synchronize()
+    ref, margin = OS.sample(lg, k, 1.0, 8, 0)
+    _check_sampled(ids, ref, margin, "ties at the k-th value")
+    # greedy over rows whose maximum repeats: the lowest index of the maximum
+    g1 = q3.sample_topk(lg.to(DEV), 1.0, 1, rng)
+    assert g1.cpu().tolist() == [int(torch.nonzero(lg[b] == 5.0)[0]) for b in range(B)]
+
+
 def test_graph_replays_advance_the_stream(q3):
     gen = synth.cpu_gen(12)
     B, V = 64, 2048
