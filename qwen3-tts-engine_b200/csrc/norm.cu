@@ -19,6 +19,9 @@ __global__ void __launch_bounds__(128) add_rms_norm_kernel(const RowNormArgs a) 
   const long long row = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
   if (row >= a.rows) return;
   __nv_bfloat16* xr = a.x + row * a.x_stride;
+  uint4 wv[J];   // the norm weight, loaded up front: its latency overlaps the row's loads and the reduction
+#pragma unroll
+  for (int j = 0; j < J; ++j) wv[j] = *reinterpret_cast<const uint4*>(a.w + 256 * j + 8 * lane);
   float v[J][8];
   float ss = 0.f;
 #pragma unroll
@@ -55,8 +58,7 @@ __global__ void __launch_bounds__(128) add_rms_norm_kernel(const RowNormArgs a) 
 #pragma unroll
   for (int j = 0; j < J; ++j) {
     const int c = 256 * j + 8 * lane;
-    const uint4 wv = *reinterpret_cast<const uint4*>(a.w + c);
-    const uint32_t* wwv = reinterpret_cast<const uint32_t*>(&wv);
+    const uint32_t* wwv = reinterpret_cast<const uint32_t*>(&wv[j]);
     uint4 o;
     uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
