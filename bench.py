@@ -469,7 +469,10 @@ def bench_aux(a):
                 for li in range(L):
                     q3attn.ring_window_attn(q, q, q, K[:, :, li], V[:, :, li], rows, pos, 71, hd ** -0.5, False)
             ms = timed(layer_calls, a.steps)
-            byt = Bs * H * (R + 2 * n) * hd * 2 * 2 + Bs * n * H * hd * 2 * 2
+            # bytes a layer must move: the ring rows some query of the chunk sees (min(pos, past) slots), K and V,
+            # plus the chunk's q, k, v rows read and its output rows written
+            vis = int(torch.clamp(pos, max=71).sum())
+            byt = (2 * vis + Bs * 4 * n) * H * hd * 2
             res[n] = {"us_per_layer": ms * 1e3 / L, "gbs": byt * L / ms / 1e6}
         print(json.dumps({"metric": "codec decoder ring attention us per layer @256 streams (fp16, 16 x 64 heads)",
                           "workload": "ring", "value": res[1]["us_per_layer"], "unit": "us per layer (1-frame chunk)",

@@ -197,7 +197,7 @@ struct RingArgs {
   __half* out;                     // [B, n, H * hd]
   long long out_batch_stride, out_frame_stride;
 };
-size_t ring_smem_bytes(int ring, int hd, int n);
+size_t ring_smem_bytes(int ring, int past, int hd, int n);
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);
 
 struct PrefillArgs {

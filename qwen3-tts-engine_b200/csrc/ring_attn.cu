@@ -12,7 +12,15 @@
 // StreamDecoder._step, decoder_stream.py:330-333); those slots hold frames older than the window (n <= RING - PAST),
 // so no query of this launch can see them, and each CTA writes only its own head after reading it.
 //
-// One CTA per (stream, head): ring and chunk rows staged in shared memory (16-byte loads), scores and softmax in fp32.
+// One CTA per (stream, head), 4 warps. The ring rows that some query of the chunk sees form one contiguous range of
+// distances d = 0 .. nvis-1 back from the newest frame (the union over the chunk is query 0's window); they are staged
+// in shared memory in that order (row d), followed by the chunk's rows, by 16-byte asynchronous copies. Ring rows no
+// query sees are never read. The two ring contractions run on the tensor cores (mma.sync m16n8k16, fp16 in, fp32
+// accumulation): S = Q.K^T over 8-key column tiles (the chunk's keys included) and O_ring = P_ring.V_ring over 16-key
+// steps with V fragments by ldmatrix.trans (V rows past nvis zeroed, so a zero probability never meets stale data);
+// the chunk part O_new = P_new.V_new (n <= 17 keys) is a few scalar FMAs per output. Rows of K, V and Q are 16-byte
+// chunks XOR-swizzled by (row & 7), which keeps every fragment load free of bank conflicts. Shared memory is about
+// 23 KB at 88 slots, head_dim 64, one frame: nine CTAs per SM.
 #include "q3_common.cuh"
 #include "q3_kernels.h"
 
@@ -24,8 +32,243 @@ constexpr int kRingThreads = 128;
 
 __device__ __forceinline__ float round_fp16(float x) { return __half2float(__float2half_rn(x)); }
 
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x2_trans(const void* p, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_addr(p)));
+}
+
+// Shared-memory geometry of one launch (every CTA uses the same layout): K, V: [KA][HD] halves (ring rows by distance
+// 0 .. RP-1, then the chunk's rows RP .. RP+n-1, padded to 8), Q: [n][HD]; S: [n][KA] floats; P_ring: [n][RP + 8]
+// halves; P_new: [n][n] floats.
+struct RingGeom {
+  int RP, KA, LPR;
+  __host__ __device__ RingGeom(int ring, int past, int n) {
+    const int nv = past < ring ? past : ring;   // ring rows any query can see
+    RP = ((nv > 0 ? nv : 1) + 15) & ~15;
+    KA = RP + ((n + 7) & ~7);
+    LPR = RP + 8;
+  }
+  __host__ __device__ size_t bytes(int hd, int n) const {
+    return (2ull * KA + n) * hd * sizeof(__half) + static_cast<size_t>(n) * KA * sizeof(float) +
+           static_cast<size_t>(n) * LPR * sizeof(__half) + static_cast<size_t>(n) * n * sizeof(float);
+  }
+};
+
 template <int HD>
-__global__ void __launch_bounds__(kRingThreads) ring_attn_kernel(const RingArgs a) {
+__device__ __forceinline__ __half* swz(__half* base, int row, int chunk) {
+  return base + (row * (HD / 8) + (chunk ^ (row & 7))) * 8;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kRingThreads, HD == 64 ? 9 : 4) ring_attn_mma_kernel(const RingArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int CH = HD / 8;                                 // 16-byte chunks per row
+  const int b = blockIdx.x, hh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;                     // mma fragment coordinates
+  const int n = a.n, RING = a.ring;
+  const RingGeom G(RING, a.past, n);
+  __half* sK = reinterpret_cast<__half*>(smem);
+  __half* sV = sK + G.KA * HD;
+  __half* sQ = sV + G.KA * HD;
+  float* sS = reinterpret_cast<float*>(sQ + n * HD);
+  __half* sPr = reinterpret_cast<__half*>(sS + n * G.KA);
+  float* sPn = reinterpret_cast<float*>(sPr + n * G.LPR);
+
+  const long long row = a.ring_rows[b];
+  const long long pos = a.pos[b];
+  // Distance d back from the newest frame (pos-1) lives in slot (pos-1-d) mod RING; query i sees it when
+  // d <= min(pos-1, PAST-1-i) (decoder_stream.py:152-155), so rows d < nvis = min(pos, PAST, RING) cover every query.
+  const long long pm1 = pos - 1;
+  const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+  int nvis = a.past < RING ? a.past : RING;
+  if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
+
+  const __half* kr = a.k_ring + row * a.ring_stream_stride + hh * HD;
+  const __half* vr = a.v_ring + row * a.ring_stream_stride + hh * HD;
+  for (int i = tid; i < G.RP * CH; i += kRingThreads) {
+    const int d = i / CH, c = i - d * CH;
+    if (d < nvis) {
+      int j = pm1_mod - d;
+      if (j < 0) j += RING;
+      cp_async16(swz<HD>(sK, d, c), kr + j * a.ring_slot_stride + c * 8);
+      cp_async16(swz<HD>(sV, d, c), vr + j * a.ring_slot_stride + c * 8);
+    } else {
+      *reinterpret_cast<uint4*>(swz<HD>(sV, d, c)) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  for (int i = tid; i < n * CH; i += kRingThreads) {
+    const int f = i / CH, c = i - f * CH;
+    const long long off = b * a.qkv_batch_stride + f * a.qkv_frame_stride + hh * HD + c * 8;
+    cp_async16(swz<HD>(sK, G.RP + f, c), a.k_new + off);
+    cp_async16(swz<HD>(sV, G.RP + f, c), a.v_new + off);
+    cp_async16(swz<HD>(sQ, f, c), a.q + off);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  // ---- S = Q.K^T: warp w takes key tiles w, w+4, ..., two at a time (independent accumulator chains); each score is
+  //      an fp16-rounded dot product (the reference's fp16 matmul), scaled and masked in fp32. Query rows >= n enter
+  //      the MMA as zeros; with n <= 16 (one query tile) the Q fragments are loaded once for all key tiles.
+  const int MT = (n + 15) / 16;
+  auto q_frag = [&](int q0, int ks, uint32_t (&f)[4]) {
+    f[0] = q0 < n ? *reinterpret_cast<const uint32_t*>(swz<HD>(sQ, q0, 2 * ks) + 2 * t) : 0u;
+    f[1] = q0 + 8 < n ? *reinterpret_cast<const uint32_t*>(swz<HD>(sQ, q0 + 8, 2 * ks) + 2 * t) : 0u;
+    f[2] = q0 < n ? *reinterpret_cast<const uint32_t*>(swz<HD>(sQ, q0, 2 * ks + 1) + 2 * t) : 0u;
+    f[3] = q0 + 8 < n ? *reinterpret_cast<const uint32_t*>(swz<HD>(sQ, q0 + 8, 2 * ks + 1) + 2 * t) : 0u;
+  };
+  auto store_scores = [&](const float (&acc)[4], int q0, int nt) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = q0 + (e >> 1) * 8;                       // query row of accumulator element e
+      const int c = nt * 8 + 2 * t + (e & 1);                // key column
+      if (i < n) {
+        const bool ok = c < G.RP ? (c < nvis && c <= a.past - 1 - i)   // ring row at distance c
+                                 : (c - G.RP <= i);                    // the chunk's own keys, causally
+        sS[i * G.KA + c] = ok ? round_fp16(acc[e]) * a.scale : -INFINITY;
+      }
+    }
+  };
+  const int NT = G.KA / 8;
+  constexpr int NW = kRingThreads / 32;
+  if (MT == 1) {
+    uint32_t qf[HD / 16][4];
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) q_frag(g, ks, qf[ks]);
+    for (int nt = warp; nt < NT; nt += 2 * NW) {
+      const int nt2 = nt + NW;                               // second tile of the pair (may be past the end)
+      const bool two = nt2 < NT;
+      const int k1 = nt * 8 + g, k2 = (two ? nt2 : nt) * 8 + g;
+      float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < HD / 16; ++ks) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, k1, 2 * ks) + 2 * t);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, k1, 2 * ks + 1) + 2 * t);
+        const uint32_t c0 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, k2, 2 * ks) + 2 * t);
+        const uint32_t c1 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, k2, 2 * ks + 1) + 2 * t);
+        mma_f16(acc1, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b0, b1);
+        mma_f16(acc2, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], c0, c1);
+      }
+      store_scores(acc1, g, nt);
+      if (two) store_scores(acc2, g, nt2);
+    }
+  } else {
+    for (int nt = warp; nt < NT; nt += NW) {
+      const int key = nt * 8 + g;
+      for (int mt = 0; mt < MT; ++mt) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          uint32_t qf[4];
+          q_frag(mt * 16 + g, ks, qf);
+          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, key, 2 * ks) + 2 * t);
+          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, key, 2 * ks + 1) + 2 * t);
+          mma_f16(acc, qf[0], qf[1], qf[2], qf[3], b0, b1);
+        }
+        store_scores(acc, mt * 16 + g, nt);
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- softmax per query row (one warp per row), P rounded to fp16: the ring part as halves (MMA operand), the
+  //      chunk part as floats
+  for (int i = warp; i < n; i += NW) {
+    float* srow = sS + i * G.KA;
+    float m = -INFINITY;
+    for (int c = lane; c < G.KA; c += 32) m = fmaxf(m, srow[c]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.f;
+    for (int c = lane; c < G.KA; c += 32) {
+      const float e = srow[c] == -INFINITY ? 0.f : expf(srow[c] - m);
+      srow[c] = e;
+      sum += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = 1.f / sum;                             // the query always sees itself: sum > 0
+    for (int c = lane; c < G.KA; c += 32) {
+      const float p = round_fp16(srow[c] * inv);
+      if (c < G.RP)
+        sPr[i * G.LPR + c] = __float2half_rn(p);
+      else if (c - G.RP < n)
+        sPn[i * n + (c - G.RP)] = p;
+    }
+  }
+  __syncthreads();
+
+  // ---- O = fp16(fp16(P_ring.V_ring) + fp16(P_new.V_new)): warp w takes dim tiles w, w+4, ... (HD / 32 of them), all
+  //      in one pass over the 16-key steps so the P fragment of a step is loaded once
+  constexpr int DT = HD / 8 / NW;                            // dim tiles per warp
+  const int vrow = lane & 15;                                // the ldmatrix row this lane supplies (lanes 0-15)
+  for (int mt = 0; mt < MT; ++mt) {
+    const int q0 = mt * 16 + g;
+    float acc[DT][4];
+#pragma unroll
+    for (int u = 0; u < DT; ++u) acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
+    for (int ks = 0; ks < G.RP / 16; ++ks) {
+      const __half* pr = sPr + ks * 16 + 2 * t;
+      const uint32_t a0 = q0 < n ? *reinterpret_cast<const uint32_t*>(pr + q0 * G.LPR) : 0u;
+      const uint32_t a1 = q0 + 8 < n ? *reinterpret_cast<const uint32_t*>(pr + (q0 + 8) * G.LPR) : 0u;
+      const uint32_t a2 = q0 < n ? *reinterpret_cast<const uint32_t*>(pr + q0 * G.LPR + 8) : 0u;
+      const uint32_t a3 = q0 + 8 < n ? *reinterpret_cast<const uint32_t*>(pr + (q0 + 8) * G.LPR + 8) : 0u;
+#pragma unroll
+      for (int u = 0; u < DT; ++u) {
+        uint32_t b0, b1;
+        ldsm_x2_trans(swz<HD>(sV, ks * 16 + vrow, warp + u * NW), b0, b1);
+        mma_f16(acc[u], a0, a1, a2, a3, b0, b1);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < DT; ++u) {
+      const int dt = warp + u * NW;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {                        // rows g and g + 8 of the tile
+        const int i = q0 + 8 * h2;
+        if (i < n) {
+          float n0 = 0.f, n1 = 0.f;                           // the chunk's keys jj <= i
+          for (int jj = 0; jj <= i; ++jj) {
+            const float p = sPn[i * n + jj];
+            const float2 v = __half22float2(*reinterpret_cast<const __half2*>(swz<HD>(sV, G.RP + jj, dt) + 2 * t));
+            n0 = fmaf(p, v.x, n0);
+            n1 = fmaf(p, v.y, n1);
+          }
+          const __half2 o = __floats2half2_rn(round_fp16(acc[u][2 * h2]) + round_fp16(n0),
+                                              round_fp16(acc[u][2 * h2 + 1]) + round_fp16(n1));
+          *reinterpret_cast<__half2*>(a.out + b * a.out_batch_stride + i * a.out_frame_stride + hh * HD + dt * 8 +
+                                      2 * t) = o;
+        }
+      }
+    }
+  }
+
+  // ---- the chunk's columns into the ring (slots of frames outside every window of this launch, never staged)
+  if (a.write_new) {
+    __half* kw = a.k_ring + row * a.ring_stream_stride + hh * HD;
+    __half* vw = a.v_ring + row * a.ring_stream_stride + hh * HD;
+    for (int i = tid; i < n * CH; i += kRingThreads) {
+      const int f = i / CH, c = i - f * CH;
+      const long long slot = (pos + f) % RING;
+      reinterpret_cast<uint4*>(kw + slot * a.ring_slot_stride)[c] =
+          *reinterpret_cast<const uint4*>(swz<HD>(sK, G.RP + f, c));
+      reinterpret_cast<uint4*>(vw + slot * a.ring_slot_stride)[c] =
+          *reinterpret_cast<const uint4*>(swz<HD>(sV, G.RP + f, c));
+    }
+  }
+}
+
+// One query frame (the streaming case, n = 1): scalar dot products and P.V, which for a single query row finish
+// sooner than 16-row tensor-core tiles that are 15/16 padding.
+template <int HD>
+__global__ void __launch_bounds__(kRingThreads) ring_attn_single_kernel(const RingArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int b = blockIdx.x, hh = blockIdx.y, tid = threadIdx.x;
   const int n = a.n, RING = a.ring, NK = RING + n;
@@ -40,9 +283,16 @@ __global__ void __launch_bounds__(kRingThreads) ring_attn_kernel(const RingArgs 
   const long long pos = a.pos[b];
   const __half* kr = a.k_ring + row * a.ring_stream_stride + hh * HD;
   const __half* vr = a.v_ring + row * a.ring_stream_stride + hh * HD;
-  // every row is staged with asynchronous 16-byte copies, all in flight together
+  // the ring slots query 0 sees (the union over the chunk) and the chunk's rows are staged with asynchronous 16-byte
+  // copies, all in flight together; the other slots are never read (masked scores, zero probabilities skipped)
+  const long long pm1s = pos - 1;
+  const int pm1s_mod = static_cast<int>(((pm1s % RING) + RING) % RING);
+  const int d_vis = min(pm1s < 0 ? -1 : static_cast<int>(pm1s < 0x7fffffff ? pm1s : 0x7fffffff), a.past - 1);
   for (int i = tid; i < RING * CH; i += kRingThreads) {
     const int j = i / CH, c = i - j * CH;
+    int d = pm1s_mod - j;
+    if (d < 0) d += RING;
+    if (d > d_vis) continue;
     cp_async16(sK + j * HD + c * 8, kr + j * a.ring_slot_stride + c * 8);
     cp_async16(sV + j * HD + c * 8, vr + j * a.ring_slot_stride + c * 8);
   }
@@ -178,33 +428,49 @@ __global__ void __launch_bounds__(kRingThreads) ring_attn_kernel(const RingArgs 
   }
 }
 
-size_t ring_smem_bytes(int ring, int hd, int n) {
+static size_t single_smem_bytes(int ring, int hd, int n) {
   return (2ull * (ring + n) + n) * hd * sizeof(__half) + static_cast<size_t>(n) * (ring + n) * sizeof(float) +
          2ull * kRingThreads * sizeof(float);
 }
 
+size_t ring_smem_bytes(int ring, int past, int hd, int n) { return RingGeom(ring, past, n).bytes(hd, n); }
+
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
-  // the shared-memory limit is raised once per device, for the largest ring supported (kRingMaxSlots), so a call
-  // made during stream capture sets no attribute
+  // the shared-memory limits are raised once per device, for the largest ring and chunk supported, so a call made
+  // during stream capture sets no attribute
   static thread_local int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(ring_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(ring_smem_bytes(kRingMaxSlots, 64, kRingMaxChunk)));
+    const int m64 = static_cast<int>(ring_smem_bytes(kRingMaxSlots, kRingMaxSlots, 64, kRingMaxChunk));
+    const int m128 = static_cast<int>(ring_smem_bytes(kRingMaxSlots, kRingMaxSlots, 128, kRingMaxChunk));
+    const int s64 = static_cast<int>(single_smem_bytes(kRingMaxSlots, 64, 1));
+    const int s128 = static_cast<int>(single_smem_bytes(kRingMaxSlots, 128, 1));
+    cudaError_t e = cudaFuncSetAttribute(ring_attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, m64);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(ring_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(ring_smem_bytes(kRingMaxSlots, 128, kRingMaxChunk)));
+      e = cudaFuncSetAttribute(ring_attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, m128);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ring_attn_single_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, s64);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ring_attn_single_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, s128);
     if (e != cudaSuccess) return e;
     configured_device = dev;
   }
   if (a.B == 0 || a.n == 0) return cudaSuccess;
-  const size_t bytes = ring_smem_bytes(a.ring, a.hd, a.n);
   dim3 grid(a.B, a.H);
-  if (a.hd == 64)
-    ring_attn_kernel<64><<<grid, kRingThreads, bytes, stream>>>(a);
-  else
-    ring_attn_kernel<128><<<grid, kRingThreads, bytes, stream>>>(a);
+  if (a.n == 1) {
+    const size_t bytes = single_smem_bytes(a.ring, a.hd, 1);
+    if (a.hd == 64)
+      ring_attn_single_kernel<64><<<grid, kRingThreads, bytes, stream>>>(a);
+    else
+      ring_attn_single_kernel<128><<<grid, kRingThreads, bytes, stream>>>(a);
+  } else {
+    const size_t bytes = ring_smem_bytes(a.ring, a.past, a.hd, a.n);
+    if (a.hd == 64)
+      ring_attn_mma_kernel<64><<<grid, kRingThreads, bytes, stream>>>(a);
+    else
+      ring_attn_mma_kernel<128><<<grid, kRingThreads, bytes, stream>>>(a);
+  }
   return cudaGetLastError();
 }
 

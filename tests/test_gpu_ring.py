@@ -96,3 +96,34 @@ def test_decoder_transformer_matches_reference_stream(q3, golden_dir):
         ref = torch.from_numpy(gold[name].astype(np.float32))
         rel = float((got - ref).norm() / ref.norm())
         assert rel < 2e-2, f"{name}: relative error {rel:.3e}"
+
+
+@pytest.mark.parametrize("hd,H", [(64, 8), (128, 4)])
+@pytest.mark.parametrize("n", [1, 4])
+def test_ring_slots_no_query_sees_are_never_used(q3, hd, H, n):
+    """Ring slots outside every query's window (never written yet, or older than the window) may hold anything, NaN
+    included: the outputs equal those computed with the same slots zeroed."""
+    g = synth.cpu_gen(500 + hd + n)
+    pos = torch.tensor([0, 1, 3, 40, 71, 72, 90, 500], dtype=torch.int64)
+    B, S = len(pos), 9
+    rows = torch.arange(B)
+    K = synth.randn((S, RING, H, hd), g, 1.0, torch.float16)
+    V = synth.randn((S, RING, H, hd), g, 1.0, torch.float16)
+    for b in range(B):
+        p = int(pos[b])
+        for j in range(RING):
+            d = ((p - 1) - j) % RING
+            if d > min(p - 1, PAST - 1):
+                K[b, j] = float("nan")
+                V[b, j] = float("inf") if j % 2 else float("nan")
+    Kz, Vz = torch.nan_to_num(K, nan=0.0, posinf=0.0), torch.nan_to_num(V, nan=0.0, posinf=0.0)
+    q = synth.randn((B, n, H, hd), g, 1.0, torch.float16)
+    k = synth.randn((B, n, H, hd), g, 1.0, torch.float16)
+    v = synth.randn((B, n, H, hd), g, 1.0, torch.float16)
+    outs = []
+    for KK, VV in ((K, V), (Kz, Vz)):
+        outs.append(q3.ring_window_attn(q.to(DEV), k.to(DEV), v.to(DEV), KK.to(DEV), VV.to(DEV), rows.to(DEV),
+                                        pos.to(DEV), PAST, hd ** -0.5, False))
+    torch.cuda.synchronize()
+    assert torch.isfinite(outs[0]).all()
+    assert bits_equal(outs[0], outs[1])
