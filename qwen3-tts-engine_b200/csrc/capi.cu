@@ -598,6 +598,9 @@ int q3_ring_window_attn(const void* q, const void* k_new, const void* v_new, int
   a.out = static_cast<__half*>(out);
   a.out_batch_stride = out_batch_stride;
   a.out_frame_stride = out_frame_stride;
+  int dev = 0, rc;
+  if ((rc = current_device(&dev)) != Q3_OK) return rc;
+  if ((rc = status_ptr(dev, &a.status)) != Q3_OK) return rc;
   return record(q3::launch_ring_attn(a, static_cast<cudaStream_t>(stream)));
 }
 

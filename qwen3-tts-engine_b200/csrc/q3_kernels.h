@@ -196,6 +196,7 @@ struct RingArgs {
   int write_new;
   __half* out;                     // [B, n, H * hd]
   long long out_batch_stride, out_frame_stride;
+  uint32_t* status;                // error bits (a staging wait that gave up)
 };
 size_t ring_smem_bytes(int ring, int past, int hd, int n);
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);

@@ -14,13 +14,15 @@
 //
 // One CTA per (stream, head), 4 warps. The ring rows that some query of the chunk sees form one contiguous range of
 // distances d = 0 .. nvis-1 back from the newest frame (the union over the chunk is query 0's window); they are staged
-// in shared memory in that order (row d), followed by the chunk's rows, by 16-byte asynchronous copies. Ring rows no
-// query sees are never read. The two ring contractions run on the tensor cores (mma.sync m16n8k16, fp16 in, fp32
-// accumulation): S = Q.K^T over 8-key column tiles (the chunk's keys included) and O_ring = P_ring.V_ring over 16-key
-// steps with V fragments by ldmatrix.trans (V rows past nvis zeroed, so a zero probability never meets stale data);
-// the chunk part O_new = P_new.V_new (n <= 17 keys) is a few scalar FMAs per output. Rows of K, V and Q are 16-byte
-// chunks XOR-swizzled by (row & 7), which keeps every fragment load free of bank conflicts. Shared memory is about
-// 23 KB at 88 slots, head_dim 64, one frame: nine CTAs per SM.
+// in shared memory in that order (row d), followed by the chunk's rows. Ring rows no query sees are never read. Two
+// kernels, by chunk size:
+//   * ring_attn_mma_kernel (2..17 frames): rows staged by 16-byte asynchronous copies; the two ring contractions run
+//     on the tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulation): S = Q.K^T over 8-key column tiles (the
+//     chunk's keys included) and O_ring = P_ring.V_ring over 16-key steps with V fragments by ldmatrix.trans (V rows
+//     past nvis zeroed, so a zero probability never meets stale data); O_new = P_new.V_new (n <= 17 keys) is a few
+//     scalar FMAs per output. Rows of K, V and Q are 16-byte chunks XOR-swizzled by (row & 7), which keeps every
+//     fragment load free of bank conflicts. About 23 KB of shared memory at 88 slots, head_dim 64: nine CTAs per SM.
+//   * ring_attn_frame_kernel (one frame, the streaming case): rows staged by one bulk copy each, scalar math.
 #include "q3_common.cuh"
 #include "q3_kernels.h"
 
@@ -256,7 +258,7 @@ __global__ void __launch_bounds__(kRingThreads, HD == 64 ? 9 : 4) ring_attn_mma_
     __half* vw = a.v_ring + row * a.ring_stream_stride + hh * HD;
     for (int i = tid; i < n * CH; i += kRingThreads) {
       const int f = i / CH, c = i - f * CH;
-      const long long slot = (pos + f) % RING;
+      const long long slot = (((pos + f) % RING) + RING) % RING;
       reinterpret_cast<uint4*>(kw + slot * a.ring_slot_stride)[c] =
           *reinterpret_cast<const uint4*>(swz<HD>(sK, G.RP + f, c));
       reinterpret_cast<uint4*>(vw + slot * a.ring_slot_stride)[c] =
@@ -265,172 +267,169 @@ __global__ void __launch_bounds__(kRingThreads, HD == 64 ? 9 : 4) ring_attn_mma_
   }
 }
 
-// One query frame (the streaming case, n = 1): scalar dot products and P.V, which for a single query row finish
-// sooner than 16-row tensor-core tiles that are 15/16 padding.
+// One query frame (the streaming case, n = 1). The frame sees every staged ring row (distances d < nvis) and itself,
+// so nothing is masked. Each row (K, V: one per distance, then the frame's own; q) arrives by its own 1-D bulk copy,
+// all completing on one mbarrier: a few instructions per thread instead of an address computation per 16 bytes. For a
+// single query row this scalar form finishes sooner than 16-row tensor-core tiles that are 15/16 padding. Thread r
+// scores key r over 16-byte pieces in the rotated order (pc + r) % CH (the 8 lanes of a quarter-warp read 8 distinct
+// bank groups), one warp runs the softmax, and P.V is split as (key group, 8-dim piece) per thread with the key groups
+// summed by shuffles and a per-warp shared row.
 template <int HD>
-__global__ void __launch_bounds__(kRingThreads) ring_attn_single_kernel(const RingArgs a) {
+__global__ void __launch_bounds__(kRingThreads) ring_attn_frame_kernel(const RingArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  const int b = blockIdx.x, hh = blockIdx.y, tid = threadIdx.x;
-  const int n = a.n, RING = a.ring, NK = RING + n;
-  constexpr int CH = HD / 8;                                 // 16-byte chunks per row
-  __half* sK = reinterpret_cast<__half*>(smem);              // [RING + n][HD]: ring rows, then the chunk's rows
-  __half* sV = sK + static_cast<size_t>(NK) * HD;
-  __half* sQ = sV + static_cast<size_t>(NK) * HD;            // [n][HD]
-  float* sS = reinterpret_cast<float*>(sQ + n * HD);         // [n][RING + n] scores, then P
-  float* sR = sS + n * NK;                                   // [kRingThreads][2] partial P.V sums of the ring keys
+  constexpr int CH = HD / 8;                                 // 16-byte pieces per row
+  constexpr int NW = kRingThreads / 32;
+  constexpr uint32_t kRow = HD * sizeof(__half);
+  const int b = blockIdx.x, hh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int RING = a.ring;
+  const int NV = a.past < RING ? a.past : RING;              // ring rows any frame can see (launch-wide)
+  __half* sK = reinterpret_cast<__half*>(smem);              // [NV + 1][HD]: ring rows by distance, then the frame's
+  __half* sV = sK + (NV + 1) * HD;
+  __half* sQ = sV + (NV + 1) * HD;                           // [HD]
+  float* sP = reinterpret_cast<float*>(sQ + HD);             // [NV + 1] scores, then probabilities
+  float* sR = sP + ((NV + 1 + 3) & ~3);                      // [NW][HD] per-warp partial P_ring.V_ring
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sR + NW * HD);
 
   const long long row = a.ring_rows[b];
   const long long pos = a.pos[b];
-  const __half* kr = a.k_ring + row * a.ring_stream_stride + hh * HD;
-  const __half* vr = a.v_ring + row * a.ring_stream_stride + hh * HD;
-  // the ring slots query 0 sees (the union over the chunk) and the chunk's rows are staged with asynchronous 16-byte
-  // copies, all in flight together; the other slots are never read (masked scores, zero probabilities skipped)
-  const long long pm1s = pos - 1;
-  const int pm1s_mod = static_cast<int>(((pm1s % RING) + RING) % RING);
-  const int d_vis = min(pm1s < 0 ? -1 : static_cast<int>(pm1s < 0x7fffffff ? pm1s : 0x7fffffff), a.past - 1);
-  for (int i = tid; i < RING * CH; i += kRingThreads) {
-    const int j = i / CH, c = i - j * CH;
-    int d = pm1s_mod - j;
-    if (d < 0) d += RING;
-    if (d > d_vis) continue;
-    cp_async16(sK + j * HD + c * 8, kr + j * a.ring_slot_stride + c * 8);
-    cp_async16(sV + j * HD + c * 8, vr + j * a.ring_slot_stride + c * 8);
-  }
-  for (int i = tid; i < n * CH; i += kRingThreads) {
-    const int f = i / CH, c = i - f * CH;
-    const long long off = b * a.qkv_batch_stride + f * a.qkv_frame_stride + hh * HD + c * 8;
-    cp_async16(sK + (RING + f) * HD + c * 8, a.k_new + off);
-    cp_async16(sV + (RING + f) * HD + c * 8, a.v_new + off);
-    cp_async16(sQ + f * HD + c * 8, a.q + off);
-  }
-  cp_async_wait_all();
-  __syncthreads();
-
-  // ---- scores: fp16-rounded dot products, scaled and masked in fp32. Slot j holds frame qj = (pos-1) - d with
-  //      d = ((pos-1) - j) mod RING; "qj >= 0 and qj >= pos + i - PAST" is "d <= min(pos-1, PAST-1-i)".
   const long long pm1 = pos - 1;
   const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
-  const int d_cap = pm1 < 0 ? -1 : static_cast<int>(pm1 < 0x7fffffff ? pm1 : 0x7fffffff);
-  for (int p = tid; p < n * NK; p += kRingThreads) {
-    const int i = p / NK, j = p - i * NK;
-    bool ok;
-    if (j < RING) {
-      int d = pm1_mod - j;
-      if (d < 0) d += RING;
-      ok = d <= d_cap && d <= a.past - 1 - i;
+  int nvis = NV;                                             // distance d lives in slot (pos-1-d) mod RING
+  if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
+  const int nk = nvis + 1;                                   // keys: nvis ring rows, then the frame itself
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(2 * nk + 1) * kRow);
+  }
+  __syncthreads();
+  const long long fo = b * a.qkv_batch_stride + hh * HD;     // the frame's q / k / v rows
+  const __half* kr = a.k_ring + row * a.ring_stream_stride + hh * HD;
+  const __half* vr = a.v_ring + row * a.ring_stream_stride + hh * HD;
+  for (int i = tid; i < 2 * nk + 1; i += kRingThreads) {
+    const __half* src;
+    __half* dst;
+    if (i == 2 * nk) {
+      src = a.q + fo;
+      dst = sQ;
     } else {
-      ok = (j - RING) <= i;
-    }
-    float s = -INFINITY;
-    if (ok) {
-      // lanes score consecutive keys whose rows sit a multiple of 32 banks apart: each starts at word j, so the 32
-      // lanes of a warp read 32 distinct banks
-      const __half2* qh = reinterpret_cast<const __half2*>(sQ + i * HD);
-      const __half2* kh = reinterpret_cast<const __half2*>(sK + j * HD);
-      float acc = 0.f;
-#pragma unroll 8
-      for (int e = 0; e < HD / 2; ++e) {
-        const int w = (e + j) & (HD / 2 - 1);
-        const float2 q2 = __half22float2(qh[w]), k2 = __half22float2(kh[w]);
-        acc = fmaf(q2.x, k2.x, acc);
-        acc = fmaf(q2.y, k2.y, acc);
+      const int r = i >> 1;
+      const bool v = (i & 1) != 0;
+      if (r < nvis) {
+        int j = pm1_mod - r;
+        if (j < 0) j += RING;
+        src = (v ? vr : kr) + j * a.ring_slot_stride;
+      } else {
+        src = (v ? a.v_new : a.k_new) + fo;
       }
-      s = round_fp16(acc) * a.scale;
+      dst = (v ? sV : sK) + r * HD;
     }
-    sS[i * NK + j] = s;
+    bulk_g2s(dst, src, kRow, bar);
+  }
+  if (!__syncthreads_and(mbar_wait_bounded(bar, 0))) {       // uniform: every thread leaves together
+    if (tid == 0) {
+      atomicOr(a.status, kStatusWaitTimeout);
+      mbar_wait_bounded(bar, 0, 100000000ull);                // the copies in flight land before the CTA exits
+    }
+    return;
+  }
+
+  // ---- scores: fp16-rounded dot products (the reference's fp16 matmul), scaled in fp32
+  for (int r = tid; r < nk; r += kRingThreads) {
+    const __half* krow = sK + r * HD;
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+    for (int pc = 0; pc < CH; ++pc) {
+      const int pp = (pc + r) & (CH - 1);
+      const uint4 kw = *reinterpret_cast<const uint4*>(krow + pp * 8);
+      const uint4 qw = *reinterpret_cast<const uint4*>(sQ + pp * 8);
+      const __half2* kh = reinterpret_cast<const __half2*>(&kw);
+      const __half2* qh = reinterpret_cast<const __half2*>(&qw);
+      acc0 = __ffma2_rn(__half22float2(kh[0]), __half22float2(qh[0]), acc0);
+      acc1 = __ffma2_rn(__half22float2(kh[1]), __half22float2(qh[1]), acc1);
+      acc0 = __ffma2_rn(__half22float2(kh[2]), __half22float2(qh[2]), acc0);
+      acc1 = __ffma2_rn(__half22float2(kh[3]), __half22float2(qh[3]), acc1);
+    }
+    sP[r] = round_fp16((acc0.x + acc0.y) + (acc1.x + acc1.y)) * a.scale;
   }
   __syncthreads();
 
-  // ---- softmax per query row (one warp per row), P rounded to fp16
-  const int warp = tid >> 5, lane = tid & 31;
-  for (int i = warp; i < n; i += kRingThreads / 32) {
-    float* srow = sS + i * NK;
+  // ---- softmax (one warp), P rounded to fp16
+  if (warp == 0) {
     float m = -INFINITY;
-    for (int j = lane; j < NK; j += 32) m = fmaxf(m, srow[j]);
+    for (int r = lane; r < nk; r += 32) m = fmaxf(m, sP[r]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float sum = 0.f;
-    for (int j = lane; j < NK; j += 32) {
-      const float e = srow[j] == -INFINITY ? 0.f : expf(srow[j] - m);
-      srow[j] = e;
+    for (int r = lane; r < nk; r += 32) {
+      const float e = expf(sP[r] - m);
+      sP[r] = e;
       sum += e;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float inv = 1.f / sum;                             // the query always sees itself: sum > 0
-    for (int j = lane; j < NK; j += 32) srow[j] = round_fp16(srow[j] * inv);
+    const float inv = 1.f / sum;
+    for (int r = lane; r < nk; r += 32) sP[r] = round_fp16(sP[r] * inv);
   }
   __syncthreads();
 
-  // ---- o = fp16(fp16(P_ring V_ring) + fp16(P_new V_new)), two dims per task; when the chunk has fewer tasks than
-  //      threads, the ring keys are split into G groups whose partial sums are added in group order
-  const int tasks = n * (HD / 2);
-  const int G = tasks >= kRingThreads ? 1 : kRingThreads / tasks;
-  for (int p = tid; p < tasks * G; p += kRingThreads) {
-    const int g = p / tasks, t = p - g * tasks;
-    const int i = t / (HD / 2), d2 = t - i * (HD / 2);
-    const float* prow = sS + i * NK;
-    float r0 = 0.f, r1 = 0.f;
-    const int j0 = g * RING / G, j1 = (g + 1) * RING / G;
-    for (int j = j0; j < j1; ++j) {
-      const float pj = prow[j];
-      if (pj == 0.f) continue;                               // masked slot: never read its (possibly stale) V
-      const float2 v = __half22float2(reinterpret_cast<const __half2*>(sV + j * HD)[d2]);
-      r0 = fmaf(pj, v.x, r0);
-      r1 = fmaf(pj, v.y, r1);
+  // ---- P_ring.V_ring: thread = (key group kg, 8-dim piece p); groups summed within the warp, then across warps
+  constexpr int G = kRingThreads / CH;                       // key groups
+  const int p = tid % CH, kg = tid / CH;
+  float2 o[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  for (int r = kg; r < nvis; r += G) {
+    const float pr = sP[r];
+    const float2 pp2 = make_float2(pr, pr);
+    const uint4 vw = *reinterpret_cast<const uint4*>(sV + r * HD + p * 8);
+    const __half2* vh = reinterpret_cast<const __half2*>(&vw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = __ffma2_rn(__half22float2(vh[e]), pp2, o[e]);
+  }
+#pragma unroll
+  for (int off = CH; off < 32; off <<= 1)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      o[e].x += __shfl_xor_sync(0xffffffffu, o[e].x, off);
+      o[e].y += __shfl_xor_sync(0xffffffffu, o[e].y, off);
     }
-    if (G > 1) {
-      sR[2 * p] = r0;
-      sR[2 * p + 1] = r1;
-    } else {
-      float n0 = 0.f, n1 = 0.f;
-      for (int j = RING; j < NK; ++j) {
-        const float pj = prow[j];
-        const float2 v = __half22float2(reinterpret_cast<const __half2*>(sV + j * HD)[d2]);
-        n0 = fmaf(pj, v.x, n0);
-        n1 = fmaf(pj, v.y, n1);
-      }
-      const __half2 o = __floats2half2_rn(round_fp16(r0) + round_fp16(n0), round_fp16(r1) + round_fp16(n1));
-      reinterpret_cast<__half2*>(a.out + b * a.out_batch_stride + i * a.out_frame_stride + hh * HD)[d2] = o;
+  if (lane < CH) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      sR[warp * HD + p * 8 + 2 * e] = o[e].x;
+      sR[warp * HD + p * 8 + 2 * e + 1] = o[e].y;
     }
   }
-  if (G > 1) {                                               // uniform across the CTA
-    __syncthreads();
-    for (int t = tid; t < tasks; t += kRingThreads) {
-      const int i = t / (HD / 2), d2 = t - i * (HD / 2);
-      const float* prow = sS + i * NK;
-      float r0 = 0.f, r1 = 0.f, n0 = 0.f, n1 = 0.f;
-      for (int g = 0; g < G; ++g) {
-        r0 += sR[2 * (g * tasks + t)];
-        r1 += sR[2 * (g * tasks + t) + 1];
-      }
-      for (int j = RING; j < NK; ++j) {
-        const float pj = prow[j];
-        const float2 v = __half22float2(reinterpret_cast<const __half2*>(sV + j * HD)[d2]);
-        n0 = fmaf(pj, v.x, n0);
-        n1 = fmaf(pj, v.y, n1);
-      }
-      const __half2 o = __floats2half2_rn(round_fp16(r0) + round_fp16(n0), round_fp16(r1) + round_fp16(n1));
-      reinterpret_cast<__half2*>(a.out + b * a.out_batch_stride + i * a.out_frame_stride + hh * HD)[d2] = o;
-    }
+  __syncthreads();
+  // ---- o = fp16(fp16(P_ring.V_ring) + fp16(P_self.V_self))
+  const float pself = sP[nvis];
+  for (int d = tid; d < HD; d += kRingThreads) {
+    float ring = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) ring += sR[w * HD + d];
+    const float self = pself * __half2float(sV[nvis * HD + d]);
+    a.out[b * a.out_batch_stride + hh * HD + d] = __float2half_rn(round_fp16(ring) + round_fp16(self));
   }
 
-  // ---- the chunk's columns into the ring (slots of frames outside every window of this launch; read above)
+  // ---- the frame's columns into the ring (a slot outside every window of this launch, never staged)
   if (a.write_new) {
-    __half* kw = a.k_ring + row * a.ring_stream_stride + hh * HD;
-    __half* vw = a.v_ring + row * a.ring_stream_stride + hh * HD;
-    for (int i = tid; i < n * CH; i += kRingThreads) {
-      const int f = i / CH, c = i - f * CH;
-      const long long slot = (pos + f) % RING;
-      reinterpret_cast<uint4*>(kw + slot * a.ring_slot_stride)[c] = reinterpret_cast<const uint4*>(sK + (RING + f) * HD)[c];
-      reinterpret_cast<uint4*>(vw + slot * a.ring_slot_stride)[c] = reinterpret_cast<const uint4*>(sV + (RING + f) * HD)[c];
+    const long long slot = ((pos % RING) + RING) % RING;
+    __half* kw = a.k_ring + row * a.ring_stream_stride + hh * HD + slot * a.ring_slot_stride;
+    __half* vw = a.v_ring + row * a.ring_stream_stride + hh * HD + slot * a.ring_slot_stride;
+    for (int i = tid; i < 2 * CH; i += kRingThreads) {
+      const int c = i % CH;
+      if (i < CH)
+        reinterpret_cast<uint4*>(kw)[c] = *reinterpret_cast<const uint4*>(sK + nvis * HD + c * 8);
+      else
+        reinterpret_cast<uint4*>(vw)[c] = *reinterpret_cast<const uint4*>(sV + nvis * HD + c * 8);
     }
   }
 }
 
-static size_t single_smem_bytes(int ring, int hd, int n) {
-  return (2ull * (ring + n) + n) * hd * sizeof(__half) + static_cast<size_t>(n) * (ring + n) * sizeof(float) +
-         2ull * kRingThreads * sizeof(float);
+static size_t frame_smem_bytes(int ring, int past, int hd) {
+  const int nv = past < ring ? past : ring;
+  return static_cast<size_t>(2 * (nv + 1) + 1) * hd * sizeof(__half) + static_cast<size_t>((nv + 1 + 3) & ~3) * 4 +
+         static_cast<size_t>(kRingThreads / 32) * hd * 4 + sizeof(uint64_t);
 }
 
 size_t ring_smem_bytes(int ring, int past, int hd, int n) { return RingGeom(ring, past, n).bytes(hd, n); }
@@ -444,26 +443,26 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
   if (configured_device != dev) {
     const int m64 = static_cast<int>(ring_smem_bytes(kRingMaxSlots, kRingMaxSlots, 64, kRingMaxChunk));
     const int m128 = static_cast<int>(ring_smem_bytes(kRingMaxSlots, kRingMaxSlots, 128, kRingMaxChunk));
-    const int s64 = static_cast<int>(single_smem_bytes(kRingMaxSlots, 64, 1));
-    const int s128 = static_cast<int>(single_smem_bytes(kRingMaxSlots, 128, 1));
+    const int s64 = static_cast<int>(frame_smem_bytes(kRingMaxSlots, kRingMaxSlots, 64));
+    const int s128 = static_cast<int>(frame_smem_bytes(kRingMaxSlots, kRingMaxSlots, 128));
     cudaError_t e = cudaFuncSetAttribute(ring_attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, m64);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(ring_attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, m128);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(ring_attn_single_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, s64);
+      e = cudaFuncSetAttribute(ring_attn_frame_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, s64);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(ring_attn_single_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, s128);
+      e = cudaFuncSetAttribute(ring_attn_frame_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, s128);
     if (e != cudaSuccess) return e;
     configured_device = dev;
   }
   if (a.B == 0 || a.n == 0) return cudaSuccess;
   dim3 grid(a.B, a.H);
   if (a.n == 1) {
-    const size_t bytes = single_smem_bytes(a.ring, a.hd, 1);
+    const size_t bytes = frame_smem_bytes(a.ring, a.past, a.hd);
     if (a.hd == 64)
-      ring_attn_single_kernel<64><<<grid, kRingThreads, bytes, stream>>>(a);
+      ring_attn_frame_kernel<64><<<grid, kRingThreads, bytes, stream>>>(a);
     else
-      ring_attn_single_kernel<128><<<grid, kRingThreads, bytes, stream>>>(a);
+      ring_attn_frame_kernel<128><<<grid, kRingThreads, bytes, stream>>>(a);
   } else {
     const size_t bytes = ring_smem_bytes(a.ring, a.past, a.hd, a.n);
     if (a.hd == 64)
