@@ -229,6 +229,9 @@ int decode_common(const void* q, int64_t q_batch_stride, const void* k_new, cons
   a.ws_ml = reinterpret_cast<float*>(ws + w.ml);
   a.ws_o = reinterpret_cast<float*>(ws + w.o);
   a.status = st;
+  // the full two-CTAs-per-SM grid gets the pair-weighted split (the kernel falls back to the uniform one when there
+  // are too few chunks)
+  a.pair_split = (num_splits <= 0 && q3::decode_ctas_per_sm(variant) == 2 && G == 2ll * sm_count(dev)) ? sm_count(dev) : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (nr) {
     a.qn_w = static_cast<const __nv_bfloat16*>(nr->q_norm_weight);

@@ -38,9 +38,30 @@ __device__ __forceinline__ uint32_t word_of(const uint4& w, int e) {
   return e == 0 ? w.x : (e == 1 ? w.y : (e == 2 ? w.z : w.w));
 }
 
-// CTA index owning global chunk p when N chunks are split over Ge CTAs as [c*N/Ge, (c+1)*N/Ge).
-__device__ __forceinline__ int cta_of_chunk(long long p, long long N, int Ge) {
-  return static_cast<int>(((p + 1) * Ge + N - 1) / N - 1);
+// The chunk split. Uniform: CTA c of Ge takes [c*N/Ge, (c+1)*N/Ge). Pair-weighted (H > 0, Ge = 2H CTAs, two per SM):
+// the CTAs a block index below H (the first to become resident on each SM) take kPairW1 shares and the others
+// kPairW2: the younger CTA of an SM gets fewer issue slots, so equal shares leave it finishing last. With
+// S(c) = W1*c (c <= H) or W1*H + W2*(c - H), CTA c takes [N*S(c)/T, N*S(c+1)/T), T = S(Ge).
+constexpr int kPairW1 = 47, kPairW2 = 45;
+
+__device__ __forceinline__ long long pair_share(int c, int H) {
+  return c <= H ? static_cast<long long>(kPairW1) * c
+                : static_cast<long long>(kPairW1) * H + static_cast<long long>(kPairW2) * (c - H);
+}
+
+// First chunk of CTA c.
+__device__ __forceinline__ long long chunk_start(int c, long long N, int Ge, int H) {
+  if (H == 0) return (N * c) / Ge;
+  return (N * pair_share(c, H)) / pair_share(Ge, H);
+}
+
+// CTA index owning global chunk p: the largest c whose first chunk is <= p.
+__device__ __forceinline__ int cta_of_chunk(long long p, long long N, int Ge, int H) {
+  if (H == 0) return static_cast<int>(((p + 1) * Ge + N - 1) / N - 1);
+  const long long X = ((p + 1) * pair_share(Ge, H) - 1) / N;   // chunk_start(c) <= p  <=>  S(c) <= X
+  const long long c = X < static_cast<long long>(kPairW1) * H ? X / kPairW1
+                                                                 : H + (X - static_cast<long long>(kPairW1) * H) / kPairW2;
+  return static_cast<int>(c < Ge - 1 ? c : Ge - 1);
 }
 
 // Pool row of token `tok` of `seat` (bounds-checked page id) and how many rows remain in its page.
@@ -117,6 +138,7 @@ struct DecodePlan {
   long long N;       // chunks of all seats
   long long c0, c1;  // this CTA's chunk range
   int Ge;            // effective CTA count
+  int H;             // > 0: pair-weighted split (see chunk_start), else uniform
   SeatCursor cur;    // positioned on the seat holding chunk c0
 };
 
@@ -156,7 +178,9 @@ __device__ __forceinline__ bool decode_plan(const DecodeArgs& a, DecodePlan& P) 
   // between a seat's first and last owner all contribute a partial (the merge counts them).
   const int Ge = static_cast<int>(N < G ? N : G);
   if (c >= Ge) return false;   // uniform across the CTA
-  const long long c0 = (N * c) / Ge, c1 = (N * (c + 1)) / Ge;
+  // pair weighting only for the full two-per-SM grid and enough chunks that every CTA keeps several
+  const int H = (a.pair_split > 0 && Ge == G && G == 2 * a.pair_split && N >= 4ll * Ge) ? a.pair_split : 0;
+  const long long c0 = chunk_start(c, N, Ge, H), c1 = chunk_start(c + 1, N, Ge, H);
 
   long long base = 0;
   for (int t0 = 0; t0 < a.B; t0 += kThreads) {
@@ -192,6 +216,7 @@ __device__ __forceinline__ bool decode_plan(const DecodeArgs& a, DecodePlan& P) 
   P.c0 = c0;
   P.c1 = c1;
   P.Ge = Ge;
+  P.H = H;
   P.cur.seat = plan_seat;
   P.cur.first = plan_first;
   P.cur.len = seat_tokens(a, plan_seat);
@@ -238,8 +263,8 @@ __device__ __forceinline__ void decode_finish_seat(const DecodeArgs& a, const De
                                                    int h, int lane, float4 o0, float4 o1, float m0, float m1,
                                                    float l0, float l1) {
   const int c = blockIdx.x;
-  const int c_first = cta_of_chunk(cur.first, P.N, P.Ge);
-  const int c_last = cta_of_chunk(cur.first + cur.nch - 1, P.N, P.Ge);
+  const int c_first = cta_of_chunk(cur.first, P.N, P.Ge, P.H);
+  const int c_last = cta_of_chunk(cur.first + cur.nch - 1, P.N, P.Ge, P.H);
   __nv_bfloat16* op = a.out + static_cast<long long>(cur.seat) * a.out_stride + (2 * h) * kHeadDim + 4 * lane;
   if (c_first == c_last) {
     const float r0 = 1.f / l0, r1 = 1.f / l1;

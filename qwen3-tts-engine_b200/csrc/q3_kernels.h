@@ -30,6 +30,7 @@ struct DecodeArgs {
   float* ws_ml;                    // [(G + B), 8, 2, 2] fp32 (running max, running sum)
   uint32_t* counters;              // [B, 8] zero between launches
   uint32_t* status;
+  int pair_split = 0;              // SM count when the grid is two CTAs per SM on every SM (pair-weighted split)
   // Fused q/k RMSNorm + RoPE (the kernel instantiated with FUSE): q rows and k_new rows are raw projections.
   const __nv_bfloat16* qn_w = nullptr;     // [128]
   const __nv_bfloat16* kn_w = nullptr;     // [128]
