@@ -4,7 +4,8 @@
 //   flash_attn_varlen_func(q, k, v, cu, cu, max, max, softmax_scale, causal=True)   engine/talker.py:169
 //   flash_attn_func(q [S,R,16,128], K [S,k+R,8,128], V, softmax_scale, causal=True)  engine/arrivals.py:148
 // and a chunked prefill whose cached prefix lives in the paged K/V pool, with the new rows written into the pages
-// (the index_copy_ page writes of engine/talker.py:161-162 and engine/arrivals.py:144-145 fused into the launch).
+// (the index_copy_ page writes of engine/talker.py:161-162 and engine/arrivals.py:144-145) by a second kernel of the
+// same call (prefill_page_write_kernel).
 //
 // Sequence i has R_i query rows, N_i new key rows (N_i >= R_i) and P_i cached prefix keys in its pages; its L_i =
 // P_i + N_i keys are indexed prefix first. Query j (0-based) sees keys 0 .. L_i - R_i + j (causal aligned to the bottom
@@ -171,7 +172,7 @@ __device__ __forceinline__ const __nv_bfloat16* pf_key_ptr(const PrefillArgs& a,
 
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int h = blockIdx.y, seq = blockIdx.z;
   const PfSeq s = pf_seq(a, seq);
   const int ntq = s.R > 0 ? (s.R + kPfQRows - 1) / kPfQRows : 1;
@@ -179,44 +180,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArg
   const int qt = ntq - 1 - static_cast<int>(blockIdx.x);
   if (qt < 0) return;                                        // uniform; nothing allocated yet
 
-  // ---- fused page write: head h of new rows r with r % ntq == qt go to positions P + r of the seat's pages. Every
-  //      (row, K or V, 16-byte chunk) copy is independent: each thread takes kPfWriteBatch of them at a time and
-  //      issues all their table and row loads before any store, so the whole CTA's loads are in flight together.
-  if (a.write_kv) {
-    constexpr int kPfWriteBatch = 16;
-    const int nrows = s.Nn > qt ? (s.Nn - qt + ntq - 1) / ntq : 0;
-    const int total = nrows * 32;                            // 16 K chunks + 16 V chunks per row
-#pragma unroll 1
-    for (int base = tid; base < total; base += kPfThreads * kPfWriteBatch) {
-      long long dst[kPfWriteBatch];
-      uint4 val[kPfWriteBatch];
-#pragma unroll
-      for (int u = 0; u < kPfWriteBatch; ++u) {
-        const int i = base + u * kPfThreads;
-        dst[u] = -1;
-        if (i < total) {
-          const int r = qt + (i >> 5) * ntq, part = i & 31;
-          const long long prow = pf_pool_row(a, s.seat, s.P + r);
-          dst[u] = prow * (kKvHeads * kHeadDim) + h * kHeadDim + (part & 15) * 8;
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kPfWriteBatch; ++u) {
-        const int i = base + u * kPfThreads;
-        val[u] = make_uint4(0, 0, 0, 0);
-        if (i < total) {
-          const int r = qt + (i >> 5) * ntq, part = i & 31;
-          const long long src = static_cast<long long>(s.k0 + r) * a.kv_stride + h * kHeadDim + (part & 15) * 8;
-          val[u] = __ldg(reinterpret_cast<const uint4*>((part < 16 ? a.k : a.v) + src));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kPfWriteBatch; ++u) {
-        const int i = base + u * kPfThreads;
-        if (i < total) *reinterpret_cast<uint4*>(((i & 31) < 16 ? a.k_pool : a.v_pool) + dst[u]) = val[u];
-      }
-    }
-  }
   if (s.R == 0) return;
 
   uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + PfSmem::kBar);
@@ -446,6 +409,25 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArg
   }
 }
 
+// The page writes of a chunked prefill (write_kv): new row r of sequence i goes to position P_i + r of its seat's pages,
+// K and V, all 8 heads (2 KB per row each). A separate launch after the attention: the attention reads new keys from
+// the input rows and only the prefix from the pages, so the order does not matter, and the writes then cost the
+// attention CTAs nothing. CTA (x, i) walks sequence i's 16-byte vectors with a grid stride; loads are coalesced.
+__global__ void __launch_bounds__(256) prefill_page_write_kernel(const PrefillArgs a) {
+  const PfSeq s = pf_seq(a, blockIdx.y);
+  constexpr int kVec = kKvHeads * kHeadDim / 8;              // 16-byte vectors per row and pool
+  const long long total = 2ll * s.Nn * kVec;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(idx / (2 * kVec));
+    const int rem = static_cast<int>(idx - static_cast<long long>(r) * 2 * kVec);
+    const int which = rem / kVec, vec = rem - which * kVec;
+    const long long prow = pf_pool_row(a, s.seat, s.P + r);
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>((which ? a.v : a.k) + static_cast<long long>(s.k0 + r) * a.kv_stride) + vec);
+    reinterpret_cast<uint4*>((which ? a.v_pool : a.k_pool) + prow * (kKvHeads * kHeadDim))[vec] = v;
+  }
+}
+
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   static thread_local int configured_device = -1;
   int dev = 0;
@@ -459,6 +441,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   const int qtiles = a.max_seqlen_q > 0 ? (a.max_seqlen_q + kPfQRows - 1) / kPfQRows : 1;
   dim3 grid(qtiles, kKvHeads, a.num_seqs);
   prefill_kernel<<<grid, kPfThreads, PfSmem::kBytes, stream>>>(a);
+  if (a.write_kv) prefill_page_write_kernel<<<dim3(16, a.num_seqs), 256, 0, stream>>>(a);
   return cudaGetLastError();
 }
 
