@@ -1,7 +1,7 @@
 """Generate the golden fixtures by running the REFERENCE engine's own fp32 code on seeded inputs.
 
-Run in a container where the reference checkout is readable (default path from $Q3_REFERENCE, else /root/reference):
-    python tests/golden/make_golden.py
+Run where the reference checkout is readable, with Q3_REFERENCE set to its directory:
+    Q3_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 It imports engine.talker / engine.arrivals / engine.code_predictor from the reference (read-only; flash-attn and triton
 only need to import) and calls:
   * Talker._attn_ref            (engine/talker.py:82-88)      paged decode on page-gathered caches  -> decode_c1.npz
@@ -31,7 +31,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "qwen3-tts-engine_b200"))
 from q3attn import synth, weights  # noqa: E402
 
-REF = os.environ.get("Q3_REFERENCE", "/root/reference")
+REF = os.environ.get("Q3_REFERENCE")   # the reference checkout (only the generators below need it)
 
 
 def digest(*ts) -> str:
@@ -42,6 +42,8 @@ def digest(*ts) -> str:
 
 
 def ref_modules():
+    if not REF:
+        raise RuntimeError("set Q3_REFERENCE to the reference checkout to regenerate the fixtures")
     sys.path.insert(0, REF)
     from engine import talker, arrivals, code_predictor   # noqa: F401
     return talker, arrivals, code_predictor
