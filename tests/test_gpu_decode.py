@@ -110,6 +110,22 @@ def test_decode_split_counts(q3, num_splits):
     assert_close_attn(out, ref, what=f"splits {num_splits}")
 
 
+@pytest.mark.parametrize("variant", [0, 2, 3, 4])
+def test_decode_pair_weighted_split(q3, variant):
+    """The default grid of the two-CTAs-per-SM variants (pair-weighted chunk split: the first CTA resident on each SM
+    takes a larger share) with enough chunks to engage it; every seat checked, seats straddling CTAs of both weights."""
+    prev = q3.set_decode_variant(variant)
+    try:
+        lay = synth.paged_layout(21, B=128, ctx_lo=100, ctx_hi=700, page=16, pages_per_seat=44)
+        d = synth.decode_case(21, lay, scale=0.5)
+        out, dd = _run_decode(q3, lay, d, append=True)
+        ref, kp, vp = _oracle(lay, d, append=True)
+        assert_close_attn(out, ref, what=f"pair split variant {variant}")
+        assert bits_equal(dd["k_pool"], kp) and bits_equal(dd["v_pool"], vp)
+    finally:
+        q3.set_decode_variant(prev)
+
+
 def test_decode_empty_seats_give_zero(q3):
     lay = _layout(4, [0, 5, 0, 40], 16, 4, seed=3)
     d = synth.decode_case(3, lay)
