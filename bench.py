@@ -66,12 +66,33 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
 
 
-def hbm_peak():
-    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+def read_hbm_peak(path):
+    """The measured HBM copy bandwidth (GB/s) from a peaks file: the top-level `hbm_gbs`, else the first numeric entry
+    whose key names HBM (top level or one level down, e.g. {"hbm": {"gbs": ...}}); None when absent or unreadable."""
     try:
-        return float(json.load(open(path))["hbm_gbs"]), "measured"
-    except Exception:
-        return FALLBACK_HBM_GBS, "fallback"
+        data = json.load(open(path))
+    except (OSError, ValueError):
+        return None
+    if not isinstance(data, dict):
+        return None
+    v = data.get("hbm_gbs")
+    if isinstance(v, (int, float)) and v > 0:
+        return float(v)
+    for k, v in data.items():
+        if "hbm" not in str(k).lower():
+            continue
+        if isinstance(v, (int, float)) and v > 0:
+            return float(v)
+        if isinstance(v, dict):
+            for kk, vv in v.items():
+                if isinstance(vv, (int, float)) and vv > 0 and "gb" in str(kk).lower():
+                    return float(vv)
+    return None
+
+
+def hbm_peak():
+    v = read_hbm_peak(os.path.join(REPO, "MEASURED_PEAKS.json"))
+    return (v, "measured") if v is not None else (FALLBACK_HBM_GBS, "fallback")
 
 
 def reduce_max(x, pg, device):

@@ -53,3 +53,20 @@ def test_reference_arm_under_torchrun_prints_once():
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
     assert d["cpu_baseline"]["kind"] == "port" and d["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_peaks_file_parsing(tmp_path):
+    """The roofline denominator: the driver-written peaks file's HBM figure (top-level `hbm_gbs`, or an HBM entry one
+    level down); absent, unreadable or without an HBM number means the fallback figure."""
+    sys.path.insert(0, REPO)
+    import bench
+    p = tmp_path / "peaks.json"
+    p.write_text(json.dumps({"hbm_gbs": 6541.2, "bf16_tflops": 1590.0}))
+    assert bench.read_hbm_peak(str(p)) == 6541.2
+    p.write_text(json.dumps({"hbm": {"gbs": 6400.0}, "bf16": {"tflops": 1500}}))
+    assert bench.read_hbm_peak(str(p)) == 6400.0
+    p.write_text(json.dumps({"bf16_tflops": 1590.0}))
+    assert bench.read_hbm_peak(str(p)) is None
+    p.write_text("not json")
+    assert bench.read_hbm_peak(str(p)) is None
+    assert bench.read_hbm_peak(str(tmp_path / "missing.json")) is None
