@@ -59,3 +59,21 @@ def test_oracle_draws_follow_the_softmax():
         sd = np.sqrt(n * p[j] * (1 - p[j]))
         assert abs(counts[i] - n * p[j]) < 4 * sd + 1, (i, counts[i], n * p[j])
     assert counts[[4, 5, 6]].sum() == 0                     # outside the top k
+
+
+def test_oracle_ties_at_the_kth_value_take_the_lowest_indices():
+    """Winners are ranked by (value desc, index asc): among keys equal to the k-th largest value only the lowest
+    indices enter the draw (the rule the GPU sampler follows)."""
+    lg = torch.full((1, 40), -5.0)
+    lg[0, 7] = 5.0
+    lg[0, [2, 9, 20, 33]] = 3.0                  # k = 3: index 7, then 2 and 9 of the tied threes
+    seen = set()
+    for launch in range(200):
+        ids, _ = OS.sample(lg, 3, 1e6, 11, launch)   # a huge temperature: every winner is about equally likely
+        seen.add(int(ids[0]))
+    assert seen == {7, 2, 9}
+    ids, _ = OS.sample(lg, 1, 1.0, 11, 0)
+    assert int(ids[0]) == 7
+    flat = torch.zeros((1, 16))
+    ids, _ = OS.sample(flat, 1, 1.0, 11, 0)
+    assert int(ids[0]) == 0                       # equal maxima: the lowest index
