@@ -143,3 +143,79 @@ def test_flash_api_refuses_unimplemented_options():
         q3attn.flash_attn_with_kvcache(q, q, q, cache_seqlens=1, window_size=(4, 0))
     with pytest.raises(NotImplementedError):
         q3attn.flash_attn_with_kvcache(q, q, q, cache_seqlens=1, return_softmax_lse=True)
+
+
+def _ring(q=16, batch=2, n=1, heads=4, hd=64, ring=88, past=71, qkv_bs=1024, qkv_fs=256, slot_s=256, out=16,
+          ring_rows=64, pos=64):
+    lib = _lib.load()
+    return lib.q3_ring_window_attn(q, q, q, qkv_bs, qkv_fs, 32, 48, 88 * 256, slot_s, ring_rows, pos, batch, n,
+                                   heads, hd, ring, past, 0.125, 0, out, qkv_bs, qkv_fs, None)
+
+
+def test_ring_rejects_bad_arguments_before_cuda():
+    assert _ring(batch=-1) == _lib.Q3_ERR_INVALID
+    assert _ring(hd=96) == _lib.Q3_ERR_UNSUPPORTED                       # head_dim 64 or 128 only
+    assert _ring(ring=129) == _lib.Q3_ERR_UNSUPPORTED                    # ring <= 128 slots
+    assert _ring(n=18, ring=120, past=71) == _lib.Q3_ERR_UNSUPPORTED     # chunk <= 17 frames
+    assert _ring(n=18, ring=88, past=71) == _lib.Q3_ERR_UNSUPPORTED
+    assert _ring(n=17, ring=88, past=72) == _lib.Q3_ERR_INVALID          # chunk slots must lie outside every window
+    assert _ring(ring_rows=None) == _lib.Q3_ERR_INVALID
+    assert _ring(qkv_fs=128) == _lib.Q3_ERR_INVALID                      # frame stride shorter than heads x head_dim
+    assert _ring(q=24) == _lib.Q3_ERR_ALIGNMENT                          # q not 16-byte aligned
+    assert _ring(batch=0) == _lib.Q3_OK and _ring(n=0) == _lib.Q3_OK     # empty calls are no-ops
+
+
+def _sampler(**kw):
+    f = dict(logits=64, logits_dtype=0, row_stride=3072, batch=4, vocab=3072, top_k=50, temperature=0.9, seen=None,
+             seen_row_stride=0, seat=None, repetition_penalty=1.0, bias=None, ngen=None, min_new=0, eos_id=0, seed=1,
+             rng_state=128, out_ids=256, out_stride=1, emb=None, emb_row_stride=0, emb_dim=0, emb_out=None,
+             emb_out_row_stride=0)
+    f.update(kw)
+    s = _lib.Sampler(**f)
+    return _lib.load().q3_sample_topk(ctypes.byref(s), None)
+
+
+def test_sampler_rejects_bad_arguments_before_cuda():
+    assert _lib.load().q3_sample_topk(None, None) == _lib.Q3_ERR_INVALID
+    assert _sampler(vocab=5000, row_stride=5000) == _lib.Q3_ERR_UNSUPPORTED        # vocab <= 4096
+    assert _sampler(top_k=65) == _lib.Q3_ERR_UNSUPPORTED                          # k <= 64
+    assert _sampler(vocab=32, row_stride=32, top_k=40) == _lib.Q3_ERR_INVALID     # k > vocab
+    assert _sampler(temperature=0.0) == _lib.Q3_ERR_INVALID                       # sampling needs T > 0
+    assert _sampler(logits_dtype=2) == _lib.Q3_ERR_INVALID
+    assert _sampler(seen=512, seen_row_stride=3072) == _lib.Q3_ERR_INVALID        # seen rows need seat ids
+    assert _sampler(emb=1024, emb_dim=1024, emb_row_stride=1024) == _lib.Q3_ERR_INVALID   # embedding without output
+    assert _sampler(rng_state=132) == _lib.Q3_ERR_ALIGNMENT
+    assert _sampler(batch=0) == _lib.Q3_OK
+
+
+def test_row_kernels_reject_bad_arguments_before_cuda():
+    lib = _lib.load()
+    assert lib.q3_add_rms_norm(16, 1024, None, 0, 16, 16, 1024, 4, 1536, 1e-6, None) == _lib.Q3_ERR_UNSUPPORTED
+    assert lib.q3_add_rms_norm(16, 512, None, 0, 16, 16, 1024, 4, 1024, 1e-6, None) == _lib.Q3_ERR_INVALID
+    assert lib.q3_add_rms_norm(16, 1024, 24, 1024, 16, 16, 1024, 4, 1024, 1e-6, None) == _lib.Q3_ERR_ALIGNMENT
+    assert lib.q3_add_rms_norm(None, 0, None, 0, None, None, 0, 0, 1024, 1e-6, None) == _lib.Q3_OK
+    assert lib.q3_silu_mul(16, 6144, 16, 3072, 4, 3070, None) == _lib.Q3_ERR_INVALID     # ffn not a multiple of 8
+    assert lib.q3_silu_mul(16, 4096, 16, 3072, 4, 3072, None) == _lib.Q3_ERR_INVALID     # row shorter than [g | u]
+    assert lib.q3_silu_mul(24, 6144, 16, 3072, 4, 3072, None) == _lib.Q3_ERR_ALIGNMENT
+    nr = _norm_rope()
+    assert lib.q3_qk_norm_rope_rows(4096, 2048, ctypes.byref(nr), 4, None) == _lib.Q3_ERR_INVALID
+    assert lib.q3_qk_norm_rope_rows(4096, 4096, None, 4, None) == _lib.Q3_ERR_INVALID
+    assert lib.q3_qk_norm_rope_rows(4100, 4096, ctypes.byref(nr), 4, None) == _lib.Q3_ERR_ALIGNMENT
+
+
+def test_prefix_copy_rejects_bad_arguments_before_cuda():
+    lib = _lib.load()
+    args = dict(k_src=16, v_src=16, ls=4096, ss=1024, kp=64, vp=64, L=28, rows=1024, page=16, nkv=8, hd=128,
+                seat=128, slot=128, batch=2, plen=35, bt=256, bts=4, maxp=4)
+
+    def call(**kw):
+        a = dict(args)
+        a.update(kw)
+        return lib.q3_kv_copy_prefix(a["k_src"], a["v_src"], a["ls"], a["ss"], a["kp"], a["vp"], a["L"], a["rows"],
+                                     a["page"], a["nkv"], a["hd"], a["seat"], a["slot"], a["batch"], a["plen"],
+                                     a["bt"], a["bts"], a["maxp"], None)
+    assert call(batch=-1) == _lib.Q3_ERR_INVALID
+    assert call(seat=None) == _lib.Q3_ERR_INVALID
+    assert call(bts=2) == _lib.Q3_ERR_INVALID                                     # table stride < pages per seat
+    assert call(k_src=24) == _lib.Q3_ERR_ALIGNMENT
+    assert call(L=0) == _lib.Q3_OK and call(plen=0) == _lib.Q3_OK
