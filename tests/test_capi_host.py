@@ -241,3 +241,18 @@ def test_prefill_rejects_bad_arguments_before_cuda():
     assert call(q=24) == _lib.Q3_ERR_ALIGNMENT
     assert call(ns=70000) == _lib.Q3_ERR_INVALID                                # beyond the grid's z extent
     assert call(ns=0) == _lib.Q3_OK
+
+
+def test_cp_step_and_noalloc_reject_bad_arguments_before_cuda():
+    lib = _lib.load()
+    strides = (16384, 2048, 128, 16384, 2048, 128)
+    assert lib.q3_cp_step(16, 2048, None, None, 1024, 16, 16, *strides, 4, 16, 2, 0.1, 16, 2048, None) == \
+        _lib.Q3_ERR_INVALID                                                     # the new slot's k / v are required
+    assert lib.q3_cp_step(16, 2048, 16, 16, 512, 16, 16, *strides, 4, 16, 2, 0.1, 16, 2048, None) == \
+        _lib.Q3_ERR_INVALID                                                     # k / v rows shorter than 8 x 128
+    assert lib.q3_cp_step(16, 2048, 20, 16, 1024, 16, 16, *strides, 4, 16, 2, 0.1, 16, 2048, None) == \
+        _lib.Q3_ERR_ALIGNMENT
+    assert lib.q3_paged_decode_noalloc(16, 2048, None, None, 0, 32, 32, 10, 16, 64, 64, 4, 4, -1, 16, 8, 128, 0.1,
+                                       16, 2048, 0, None) == _lib.Q3_ERR_INVALID
+    assert lib.q3_paged_decode_noalloc(16, 2048, None, None, 0, 32, 32, 10, 16, 64, 64, 4, 4, 2, 16, 8, 128, 0.1,
+                                       16, 2048, -3, None) == _lib.Q3_ERR_INVALID
