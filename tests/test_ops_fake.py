@@ -76,3 +76,23 @@ def test_ring_and_sampler_ops(fake):
     ids, emb = res
     assert ids.shape == (B,) and ids.dtype == torch.int64
     assert emb.shape == (B, 1024) and emb.dtype == BF
+
+
+def test_ops_trace_as_single_opaque_nodes():
+    """Traced with fake tensors (as torch.compile's front end does), each op is one node of the graph, mutating ones
+    included: nothing of the attention is decomposed into aten ops."""
+    from torch.fx.experimental.proxy_tensor import make_fx
+
+    def layer(q, k, v, kc, vc, seq, bt, cq, K):
+        o = OPS.paged_decode_append(q, k, v, kc, vc, seq, bt, 0.1, 0)
+        c = OPS.cp_step(cq, k, v, K, K, 2, 0.1)
+        return o.float().sum() + c.float().sum()
+
+    with FakeTensorMode():
+        args = (e(3, 16, 128), e(3, 8, 128), e(3, 8, 128), e(20, 16, 8, 128), e(20, 16, 8, 128), i32(3), i32(3, 4),
+                e(3, 16, 128), e(3, 8, 16, 128))
+        g = make_fx(layer, tracing_mode="fake")(*args)
+    targets = [str(n.target) for n in g.graph.nodes if n.op == "call_function"]
+    assert targets.count("q3attn.paged_decode_append.default") == 1
+    assert targets.count("q3attn.cp_step.default") == 1
+    assert not any("softmax" in t or "bmm" in t or "matmul" in t for t in targets)
