@@ -81,8 +81,9 @@ int q3_paged_decode_resident_ctas(int variant);
  * allocate. The split-K scratch lives in a 16 MiB array compiled into the library, held by every GPU that loads it
  * until exit; calls whose workspace would exceed it (roughly batch + CTAs > 2000) return Q3_ERR_SCRATCH_LIMIT before
  * launching anything. The first call on a device looks up the array's device address (do it before any stream
- * capture). Every call clears the counters it uses on its stream; calls that overlap on the GPU share the array and
- * race. */
+ * capture); the address is cached per device, so after a cudaDeviceReset the library must be reloaded. Arguments are
+ * checked before anything is queued: a refused call leaves the array alone. Every accepted call clears the counters it
+ * uses on its stream; calls that overlap on the GPU share the array and race. */
 int q3_paged_decode_noalloc(const void* q, int64_t q_batch_stride,
                             const void* k_new, const void* v_new, int64_t kv_new_batch_stride,
                             void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,

@@ -170,14 +170,13 @@ bool norm_rope_aligned(const q3_qk_norm_rope* nr) {
          aligned(nr->sin, 8) && (nr->rope_row_stride % 4) == 0;
 }
 
-// q3_paged_decode and q3_paged_decode_qkv: validation, workspace carving and launch. With nr set, q and k_new are raw
-// projections and the kernel applies RMSNorm + RoPE (default configuration only).
-int decode_common(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
-                  int64_t kv_new_batch_stride, const q3_qk_norm_rope* nr, void* k_pool, void* v_pool,
-                  int32_t num_pages, int32_t page_size, const int32_t* cache_seqlens, const int32_t* block_table,
-                  int64_t block_table_stride, int32_t max_pages_per_seat, int32_t batch, int32_t num_heads,
-                  int32_t num_kv_heads, int32_t head_dim, float softmax_scale, void* out, int64_t out_batch_stride,
-                  void* workspace, size_t workspace_bytes, int32_t num_splits, void* stream) {
+// Argument checks of the decode entries that need no CUDA call (shapes, null pointers, strides, alignment).
+int decode_check_args(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
+                      int64_t kv_new_batch_stride, const q3_qk_norm_rope* nr, const void* k_pool, const void* v_pool,
+                      int32_t num_pages, int32_t page_size, const int32_t* cache_seqlens, const int32_t* block_table,
+                      int64_t block_table_stride, int32_t max_pages_per_seat, int32_t batch, int32_t num_heads,
+                      int32_t num_kv_heads, int32_t head_dim, const void* out, int64_t out_batch_stride,
+                      int32_t num_splits) {
   int rc = check_family(num_heads, num_kv_heads, head_dim);
   if (rc != Q3_OK) return rc;
   if (batch < 0 || num_pages <= 0 || page_size <= 0 || max_pages_per_seat <= 0 || num_splits < 0) return Q3_ERR_INVALID;
@@ -196,6 +195,24 @@ int decode_common(const void* q, int64_t q_batch_stride, const void* k_new, cons
                 kv_new_batch_stride < q3::kKvHeads * q3::kHeadDim))
     return Q3_ERR_ALIGNMENT;
   if (nr && !norm_rope_aligned(nr)) return Q3_ERR_ALIGNMENT;
+  return Q3_OK;
+}
+
+// q3_paged_decode and q3_paged_decode_qkv: validation, workspace carving and launch. With nr set, q and k_new are raw
+// projections and the kernel applies RMSNorm + RoPE (default configuration only). With clear_counters set, the ticket
+// counters of the call's seats are zeroed on the stream right before the launch, after every check has passed (the
+// workspace of the allocation-free entry may hold whatever an earlier call left).
+int decode_common(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
+                  int64_t kv_new_batch_stride, const q3_qk_norm_rope* nr, void* k_pool, void* v_pool,
+                  int32_t num_pages, int32_t page_size, const int32_t* cache_seqlens, const int32_t* block_table,
+                  int64_t block_table_stride, int32_t max_pages_per_seat, int32_t batch, int32_t num_heads,
+                  int32_t num_kv_heads, int32_t head_dim, float softmax_scale, void* out, int64_t out_batch_stride,
+                  void* workspace, size_t workspace_bytes, int32_t num_splits, void* stream,
+                  bool clear_counters = false) {
+  int rc = decode_check_args(q, q_batch_stride, k_new, v_new, kv_new_batch_stride, nr, k_pool, v_pool, num_pages,
+                             page_size, cache_seqlens, block_table, block_table_stride, max_pages_per_seat, batch,
+                             num_heads, num_kv_heads, head_dim, out, out_batch_stride, num_splits);
+  if (rc != Q3_OK || batch == 0) return rc;
   int dev = 0;
   if ((rc = current_device(&dev)) != Q3_OK) return rc;
   const int variant = nr ? 0 : g_decode_variant;
@@ -233,6 +250,10 @@ int decode_common(const void* q, int64_t q_batch_stride, const void* k_new, cons
   // are too few chunks)
   a.pair_split = (num_splits <= 0 && q3::decode_ctas_per_sm(variant) == 2 && G == 2ll * sm_count(dev)) ? sm_count(dev) : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (clear_counters) {
+    cudaError_t e = cudaMemsetAsync(a.counters, 0, static_cast<size_t>(batch) * kSeatTicketBytes, s);
+    if (e != cudaSuccess) return record(e);
+  }
   if (nr) {
     a.qn_w = static_cast<const __nv_bfloat16*>(nr->q_norm_weight);
     a.kn_w = static_cast<const __nv_bfloat16*>(nr->k_norm_weight);
@@ -246,6 +267,40 @@ int decode_common(const void* q, int64_t q_batch_stride, const void* k_new, cons
 }
 
 }  // namespace
+
+}  // extern "C"
+
+namespace q3 {
+
+int record_cuda_error(cudaError_t e) { return record(e); }
+
+int paged_decode_check_args(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
+                            int64_t kv_new_batch_stride, const void* k_pool, const void* v_pool, int32_t num_pages,
+                            int32_t page_size, const int32_t* cache_seqlens, const int32_t* block_table,
+                            int64_t block_table_stride, int32_t max_pages_per_seat, int32_t batch, int32_t num_heads,
+                            int32_t num_kv_heads, int32_t head_dim, const void* out, int64_t out_batch_stride,
+                            int32_t num_splits) {
+  return decode_check_args(q, q_batch_stride, k_new, v_new, kv_new_batch_stride, nullptr, k_pool, v_pool, num_pages,
+                           page_size, cache_seqlens, block_table, block_table_stride, max_pages_per_seat, batch,
+                           num_heads, num_kv_heads, head_dim, out, out_batch_stride, num_splits);
+}
+
+int paged_decode_clearing_counters(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
+                                   int64_t kv_new_batch_stride, void* k_pool, void* v_pool, int32_t num_pages,
+                                   int32_t page_size, const int32_t* cache_seqlens, const int32_t* block_table,
+                                   int64_t block_table_stride, int32_t max_pages_per_seat, int32_t batch,
+                                   int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float softmax_scale,
+                                   void* out, int64_t out_batch_stride, void* workspace, size_t workspace_bytes,
+                                   int32_t num_splits, void* stream) {
+  return decode_common(q, q_batch_stride, k_new, v_new, kv_new_batch_stride, nullptr, k_pool, v_pool, num_pages,
+                       page_size, cache_seqlens, block_table, block_table_stride, max_pages_per_seat, batch, num_heads,
+                       num_kv_heads, head_dim, softmax_scale, out, out_batch_stride, workspace, workspace_bytes,
+                       num_splits, stream, /*clear_counters=*/true);
+}
+
+}  // namespace q3
+
+extern "C" {
 
 int q3_paged_decode(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
                     int64_t kv_new_batch_stride, void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,

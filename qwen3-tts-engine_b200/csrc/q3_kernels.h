@@ -231,4 +231,22 @@ struct PrefillArgs {
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
 
+// Host-side helpers of capi.cu shared with the allocation-free decode entry (decode_noalloc.cu).
+int record_cuda_error(cudaError_t e);   // keeps the error text for q3_last_cuda_error(); returns Q3_ERR_CUDA
+// The argument checks of q3_paged_decode that need no CUDA call.
+int paged_decode_check_args(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
+                            int64_t kv_new_batch_stride, const void* k_pool, const void* v_pool, int32_t num_pages,
+                            int32_t page_size, const int32_t* cache_seqlens, const int32_t* block_table,
+                            int64_t block_table_stride, int32_t max_pages_per_seat, int32_t batch, int32_t num_heads,
+                            int32_t num_kv_heads, int32_t head_dim, const void* out, int64_t out_batch_stride,
+                            int32_t num_splits);
+// q3_paged_decode that also zeroes the call's ticket counters on the stream, after every check passed, before launch.
+int paged_decode_clearing_counters(const void* q, int64_t q_batch_stride, const void* k_new, const void* v_new,
+                                   int64_t kv_new_batch_stride, void* k_pool, void* v_pool, int32_t num_pages,
+                                   int32_t page_size, const int32_t* cache_seqlens, const int32_t* block_table,
+                                   int64_t block_table_stride, int32_t max_pages_per_seat, int32_t batch,
+                                   int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float softmax_scale,
+                                   void* out, int64_t out_batch_stride, void* workspace, size_t workspace_bytes,
+                                   int32_t num_splits, void* stream);
+
 }  // namespace q3

@@ -4,10 +4,13 @@
 
 Every .cu under qwen3-tts-engine_b200/csrc is compiled separately (in parallel) and linked into
 qwen3-tts-engine_b200/q3attn/libq3attn.so next to this file, where q3attn._lib loads it. Objects go to
-qwen3-tts-engine_b200/_build/. A rebuild happens only when a source or header is newer than the library.
+qwen3-tts-engine_b200/_build/. The library is rebuilt unless the SHA-256 of every source, header and this script (and
+the nvcc flags) equals the digest stamped beside it when it was last built, so a copied tree never runs a library that
+was built from other sources, whatever the files' modification times say.
 """
 import concurrent.futures as cf
 import glob
+import hashlib
 import os
 import shutil
 import subprocess
@@ -20,6 +23,7 @@ CSRC = os.path.join(ROOT, "csrc")
 INCLUDE = os.path.join(REPO, "include")
 BUILD_DIR = os.path.join(ROOT, "_build")
 LIB = os.path.join(PKG_DIR, "libq3attn.so")
+STAMP = LIB + ".sha256"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
               "-I", CSRC, "-I", INCLUDE] + ARCH
@@ -41,11 +45,21 @@ def _deps():
         glob.glob(os.path.join(INCLUDE, "*.h")) + [os.path.abspath(__file__)]
 
 
+def source_digest() -> str:
+    """SHA-256 over the build inputs: each dependency's name and bytes, in name order, plus the nvcc flags."""
+    h = hashlib.sha256(" ".join(NVCC_FLAGS).encode())
+    for d in sorted(set(_deps())):
+        h.update(os.path.basename(d).encode() + b"\0")
+        with open(d, "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
 def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+    if not (os.path.exists(LIB) and os.path.exists(STAMP)):
         return False
-    t = os.path.getmtime(LIB)
-    return all(os.path.getmtime(d) <= t for d in _deps())
+    with open(STAMP) as f:
+        return f.read().strip() == source_digest()
 
 
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> str:
@@ -75,6 +89,8 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr}")
     os.replace(tmp, LIB)
+    with open(STAMP, "w") as f:
+        f.write(source_digest() + "\n")
     return LIB
 
 

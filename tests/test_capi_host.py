@@ -256,3 +256,26 @@ def test_cp_step_and_noalloc_reject_bad_arguments_before_cuda():
                                        16, 2048, 0, None) == _lib.Q3_ERR_INVALID
     assert lib.q3_paged_decode_noalloc(16, 2048, None, None, 0, 32, 32, 10, 16, 64, 64, 4, 4, 2, 16, 8, 128, 0.1,
                                        16, 2048, -3, None) == _lib.Q3_ERR_INVALID
+
+
+def test_noalloc_checks_every_argument_before_touching_cuda_or_its_scratch():
+    """The allocation-free decode entry shares one scratch array between all calls on a device, so a call it refuses
+    must queue nothing on it (no counter clearing that could hit a call in flight on another stream). Every argument
+    check therefore runs before its first CUDA call: on a host without a GPU each bad call below returns its argument
+    error, never Q3_ERR_CUDA, which is what any CUDA call would produce here."""
+    lib = _lib.load()
+
+    def call(q=16, kn=None, vn=None, kvs=0, kp=32, vp=32, pages=10, page=16, seq=64, bt=64, bts=4, mp=4, B=2,
+             nh=16, nkv=8, hd=128, out=16, outs=2048, ns=0):
+        return lib.q3_paged_decode_noalloc(q, 2048, kn, vn, kvs, kp, vp, pages, page, seq, bt, bts, mp, B, nh, nkv, hd,
+                                           0.1, out, outs, ns, None)
+
+    assert call(q=24) == _lib.Q3_ERR_ALIGNMENT                                  # q rows need 16-byte alignment
+    assert call(kp=40) == _lib.Q3_ERR_ALIGNMENT
+    assert call(nh=12) == _lib.Q3_ERR_UNSUPPORTED
+    assert call(bt=None) == _lib.Q3_ERR_INVALID
+    assert call(out=None) == _lib.Q3_ERR_INVALID
+    assert call(outs=100) == _lib.Q3_ERR_INVALID                                # out rows shorter than 16 x 128
+    assert call(kn=16) == _lib.Q3_ERR_INVALID                                   # k without v
+    assert call(kn=16, vn=16, kvs=512) == _lib.Q3_ERR_ALIGNMENT                 # new rows shorter than 8 x 128
+    assert call(B=0) == _lib.Q3_OK                                              # an empty batch does nothing at all
