@@ -27,7 +27,7 @@ import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(REPO, "qwen3-tts-engine_b200")
-for _p in (REPO, PKG):
+for _p in (REPO, PKG, os.path.join(REPO, "tests")):     # tests/: the frame harness the c5 and admit workloads drive
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
@@ -54,7 +54,7 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
-    p.add_argument("--cpu-seats", type=int, default=48)
+    p.add_argument("--cpu-seats", type=int, default=64)
     p.add_argument("--kernel-breakdown", action="store_true",
                    help="c5: add the per-kernel device time of one replayed frame (CUPTI via torch.profiler)")
     p.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "admit", "prefill", "ring"], default="c2",
@@ -189,17 +189,23 @@ def cpu_layer(s):
     return OA.decode_step(s["q"], s["kn"], s["vn"], s["kp"], s["vp"], s["ctx"], s["bt"], SCALE)
 
 
-def cpu_rate(s, layers, seconds):
-    cpu_layer(s)
+def cpu_step(s, layers):
+    """One step of the CPU path for the sampled seats: all `layers` layers (each one pass of the append + page gather
+    + Talker._attn_ref restatement over the sample's K/V, which is larger than the host caches); returns seconds."""
     t0 = time.perf_counter()
-    n = 0
-    while True:
+    for _ in range(layers):
         cpu_layer(s)
+    return time.perf_counter() - t0
+
+
+def cpu_rate(s, layers, seconds):
+    """CPU seat-steps/s over whole steps (cpu_step) repeated for at least `seconds`, after one untimed step."""
+    cpu_step(s, layers)
+    n, el = 0, 0.0
+    while el < seconds:
+        el += cpu_step(s, layers)
         n += 1
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
-    return s["n"] * n / el / layers, n, el
+    return s["n"] * n / el, n, el
 
 
 def host_cores():
@@ -211,6 +217,10 @@ def host_cores():
 
 # ----------------------------------------------------------------------------------------------------- reference arm
 def run_reference(a):
+    """The reference's CPU path on the host cores: each step is one whole 28-layer decode step for a bounded sample of
+    the seats (cpu_step), the same unit the GPU arm's cpu_baseline times; W untimed steps, then exactly K timed ones.
+    ms_per_step is the time actually measured per step (for the sampled seats); the time a step of all the config's
+    seats would take on the CPU is reported separately as an extrapolation."""
     rank, _, world = dist_env()
     if rank != 0:
         return
@@ -218,20 +228,19 @@ def run_reference(a):
     lay = layout_for_rank(a.seed, 0, a.seats)
     s = cpu_sample(lay, a.seed, a.cpu_seats)
     for _ in range(max(a.warmup, 1)):
-        cpu_layer(s)
-    times = []
-    for _ in range(a.steps):
-        t0 = time.perf_counter()
-        cpu_layer(s)
-        times.append(time.perf_counter() - t0)
-    per_layer = sum(times) / len(times)
-    value = s["n"] / per_layer / a.layers
-    sample = (f"each step: 1 of {a.layers} layers for {s['n']} of {a.seats} seats (append + page gather + "
-              f"Talker._attn_ref restated, fp32 torch CPU); seat-steps/s = seats / layer time / {a.layers}")
+        cpu_step(s, a.layers)
+    times = [cpu_step(s, a.layers) for _ in range(a.steps)]
+    per_step = sum(times) / len(times)
+    value = s["n"] / per_step
+    sample = (f"each step: all {a.layers} layers for {s['n']} of {a.seats} seats (append + page gather + "
+              f"Talker._attn_ref restated, fp32 torch CPU, {torch.get_num_threads()} threads); "
+              f"seat-steps/s = sampled seats / step time")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": per_layer * a.layers * 1e3 * a.seats / s["n"], "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE config 2 shapes)",
-            "config": config_dict(a, world),
+            "warmup": a.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE config 2 shapes)",
+            "config": config_dict(a, world), "seats_timed_per_step": s["n"],
+            "timed_s": sum(times), "step_ms_min": min(times) * 1e3, "step_ms_max": max(times) * 1e3,
+            "extrapolated_ms_per_step_all_seats": per_step * 1e3 * a.seats / s["n"],
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -255,7 +264,7 @@ def bench_frame(a):
     logit processing + sampling as PyTorch ops, for comparison."""
     import q3attn
     from q3attn import synth, weights
-    from q3attn.frame import Talker
+    from frame_harness import Talker
     rank, local, world = dist_env()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -385,7 +394,7 @@ def bench_admit(a):
     import q3attn
     from q3attn import weights
     from q3attn.admit import Admit
-    from q3attn.frame import Talker
+    from frame_harness import Talker
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     k, R, n_seats, seat_len = 35, 42, 64, 512
@@ -733,8 +742,8 @@ def main():
         s = cpu_sample(lay, a.seed, a.cpu_seats)
         rate, n, el = cpu_rate(s, L, a.cpu_seconds)
         cpu = {"value": rate, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"{n} layer passes over {s['n']} of {B} seats in {el:.1f} s (append + page gather + "
-                         f"Talker._attn_ref restated, fp32 torch CPU), scaled by 1/{L} layers"}
+               "sample": f"{n} steps of all {L} layers for {s['n']} of {B} seats in {el:.1f} s (append + page gather "
+                         f"+ Talker._attn_ref restated, fp32 torch CPU); seat-steps/s = sampled seats / step time"}
 
     for g in graphs:
         del g

@@ -132,7 +132,7 @@ int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v
 /* ---------------------------------------------------------------- code-predictor attention
  * Replaces cp_attn(q, K, V, n_live, scale) (engine/cp_attn.py:33-39), i.e. the attention expression of
  * CodePredictor._post (engine/code_predictor.py:46-47): q [B,16,128] over slots 0..n_live-1 of K/V [B,8,S,128];
- * fp32 scores and softmax, probabilities rounded to bf16, fp32 P.V, bf16 out [B, 2048]. 1 <= n_live <= min(S,16). */
+ * fp32 scores, softmax, probabilities and P.V, bf16 out [B, 2048]. 1 <= n_live <= min(S,16). */
 int q3_cp_attn(const void* q, int64_t q_batch_stride,
                const void* K, const void* V,
                int64_t k_batch_stride, int64_t k_head_stride, int64_t k_slot_stride,

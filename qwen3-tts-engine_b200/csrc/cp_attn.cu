@@ -3,8 +3,8 @@
 // Replaces, per (step, layer) of CodePredictor._s (engine/code_predictor.py:52-60):
 //   K.index_copy_(2, [p], k); V.index_copy_(2, [p], v)                  engine/code_predictor.py:58
 //   att = q.view(B,8,2,128) @ K^T * scale + mask[p]; softmax; @ V       engine/code_predictor.py:46-47
-// with the arithmetic of the reference's intended kernel cp_attn (engine/cp_attn.py:14-30): fp32 scores and softmax,
-// probabilities rounded to bf16 before P.V, fp32 accumulation, bf16 output. Slots >= n_live are not read.
+// with fp32 scores and softmax as in the reference's intended kernel cp_attn (engine/cp_attn.py:14-30), but fp32
+// probabilities into P.V (cp_attn.py rounds them to bf16), fp32 accumulation, bf16 output. Slots >= n_live are not read.
 //
 // Two CTAs per seat (KV heads 0-3 and 4-7), one warp per KV head; lane l owns dims 4l..4l+3 of both q heads of the
 // group. The live K and V rows are staged in shared memory by copies issued up front (one round of memory latency, no
@@ -127,7 +127,10 @@ __global__ void __launch_bounds__(kCpWarps * 32) cp_attn_kernel(const CpArgs a) 
   float sum = p;
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  p = round_bf16(p / sum);                            // engine/cp_attn.py:26-27: P rounded to the model dtype
+  // P stays fp32 for P.V. engine/cp_attn.py:26-27 (and the bf16 matmul of code_predictor.py:47) round it to the model
+  // dtype first; keeping it costs nothing here (it lives in registers / shared memory either way) and removes that
+  // rounding from the error against the reference's fp32 result (the scores are fp32 dot products for the same reason).
+  p = p / sum;
   pbuf[lane] = p;
   __syncwarp();
 

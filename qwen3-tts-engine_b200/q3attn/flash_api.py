@@ -1,10 +1,11 @@
-"""flash-attn-compatible entry points backed by the q3attn kernels (drop-in for the engine's imports).
+"""Drop-in entry points with the reference engine's call signatures, backed by the q3attn kernels.
 
 The engine imports ``flash_attn_with_kvcache, flash_attn_varlen_func`` (engine/talker.py:13) and ``flash_attn_func``
-(engine/arrivals.py:30). These functions accept the same arguments for the shapes the engine uses (GQA 16/8,
-head_dim 128, bf16) and raise NotImplementedError for flash-attn features the engine never passes (sliding windows,
-softcap, ALiBi, rotary inside the kernel, cache_batch_idx/leftpad, returning the LSE), rather than computing something
-else.
+(engine/arrivals.py:30) from flash-attn. These functions accept the same arguments for the shapes the engine uses
+(GQA 16/8, head_dim 128, bf16) and raise NotImplementedError for flash-attn features the engine never passes (sliding
+windows, softcap, ALiBi, rotary inside the kernel, cache_batch_idx/leftpad, returning the LSE), rather than computing
+something else. ``cp_attn`` keeps the signature of engine/cp_attn.py:33, and ``cp_step`` is the code predictor's slot
+write + attention (engine/code_predictor.py:58, 46-47) as one call.
 """
 import torch
 
@@ -80,3 +81,16 @@ def flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None, causal=False, wi
     o = ops.prefill(q.reshape(S * R, NH, HD), k.reshape(S * n, NKV, HD), v.reshape(S * n, NKV, HD), cu_q, cu_k, R,
                     scale, bool(causal))
     return o.view(S, R, NH, HD)
+
+
+def cp_attn(q, K, V, n_live, scale):
+    """``cp_attn(q, K, V, n_live, scale) -> o [B, 2048]`` (engine/cp_attn.py:33-39): q [B,16,128] or [B,2048]; K/V
+    [B,8,16,128] whose batch stride may exceed the live batch; slots 0..n_live-1 attended; fp32 scores, softmax,
+    probabilities and P.V; bf16 output."""
+    return ops.cp_attn_op(q, K, V, int(n_live), float(scale))
+
+
+def cp_step(q, k, v, K, V, p, scale):
+    """``K[:, :, p] = k; V[:, :, p] = v`` (engine/code_predictor.py:58) then the attention of code_predictor.py:46-47
+    over slots 0..p, in one launch -> [B, 2048]."""
+    return ops.cp_step(q, k, v, K, V, int(p), float(scale))

@@ -26,6 +26,15 @@ NH, NKV, HD = 16, 8, 128
 _ws = {}                     # (device index, stream handle) -> uint8 workspace tensor
 
 
+def _paired_rows(k: torch.Tensor, v: torch.Tensor):
+    """k and v with one shared row stride, as the kernels take them. The engine often passes k as a fresh tensor (the
+    output of RoPE) and v as a strided view of the QKV projection rows (engine/talker.py:159-160,
+    engine/code_predictor.py:41-42); then both are made contiguous (one copy each) so the call still works."""
+    if k.dim() >= 1 and v.dim() == k.dim() and k.stride() != v.stride():
+        return k.contiguous(), v.contiguous()
+    return k, v
+
+
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
@@ -75,6 +84,8 @@ def _decode_impl(q, k_new, v_new, k_cache, v_cache, cache_seqlens, block_table, 
     _need(block_table.dtype == torch.int32 and block_table.dim() == 2 and block_table.shape[0] == B
           and block_table.stride(1) == 1, "block_table must be int32 [B, max_pages] with unit inner stride")
     kvs = 0
+    if k_new is not None and v_new is not None:
+        k_new, v_new = _paired_rows(k_new, v_new)
     if k_new is not None:
         _check_cuda_bf16("k", k_new)
         _check_cuda_bf16("v", v_new)
@@ -195,7 +206,7 @@ def kv_append_slots(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_c
                     slots: torch.Tensor) -> None:
     """k_cache.view(-1,8,128).index_copy_(0, slots, k) and the same for v (engine/talker.py:72-73)."""
     lib = _lib.load()
-    k, v = _rows("k", k), _rows("v", v)
+    k, v = _paired_rows(_rows("k", k), _rows("v", v))
     _check_cuda_bf16("k_cache", k_cache)
     _check_cuda_bf16("v_cache", v_cache)
     _need(k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.shape == v_cache.shape
@@ -215,7 +226,7 @@ def kv_append_paged(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_c
                     seat_of_row: Optional[torch.Tensor] = None) -> None:
     """Row i -> token positions[i] of seat seat_of_row[i] (default: seat i) through the block table."""
     lib = _lib.load()
-    k, v = _rows("k", k), _rows("v", v)
+    k, v = _paired_rows(_rows("k", k), _rows("v", v))
     _check_cuda_bf16("k_cache", k_cache)
     _check_cuda_bf16("v_cache", v_cache)
     _need(k_cache.dim() == 4 and k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.shape == v_cache.shape,
@@ -415,7 +426,7 @@ def cp_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, K: torch.Tensor, 
     lib = _lib.load()
     q2 = _cp_check(q, K, V)
     B = q2.shape[0]
-    k3, v3 = _rows("k", k), _rows("v", v)
+    k3, v3 = _paired_rows(_rows("k", k), _rows("v", v))
     _need(k3.shape[0] == B and v3.shape == k3.shape and v3.stride(0) == k3.stride(0), "k/v must be [B, 8, 128]")
     out = torch.empty(B, NH * HD, dtype=torch.bfloat16, device=q.device)
     with torch.cuda.device(q.device):
@@ -544,6 +555,7 @@ def _prefill_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_sca
     _check_cuda_bf16("q", q)
     _check_cuda_bf16("k", k)
     _check_cuda_bf16("v", v)
+    k, v = _paired_rows(k, v)
     _need(q.dim() == 3 and q.shape[1] == NH and q.shape[2] == HD and q.stride(2) == 1 and q.stride(1) == HD,
           "q must be packed rows [T, 16, 128]")
     _need(k.dim() == 3 and k.shape[1] == NKV and k.shape[2] == HD and k.stride(2) == 1 and k.stride(1) == HD

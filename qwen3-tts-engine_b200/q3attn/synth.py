@@ -153,3 +153,38 @@ def decode_bytes(ctx_after: torch.Tensor, append: bool = True) -> int:
     n = int(c.numel())
     pages = int(((c + 15) // 16).sum())
     return int(4096 * int(c.sum()) + 8192 * n + (4096 * n if append else 0) + 4 * pages)
+
+
+# --------------------------------------------------------------------------- device-independent K/V history
+_M32 = 0xFFFFFFFF
+
+
+def _mix32(x: torch.Tensor) -> torch.Tensor:
+    """A 32-bit xorshift-multiply mixer on int64 tensors holding values in [0, 2^32): every product stays below 2^63
+    (32-bit value x 31-bit constant), so CPU and CUDA integer arithmetic give the same bits."""
+    x = x ^ (x >> 16)
+    x = (x * 0x7FEB352D) & _M32
+    x = x ^ (x >> 15)
+    x = (x * 0x5BD1E995) & _M32
+    return x ^ (x >> 16)
+
+
+def history_block(seed: int, layer: int, kv: int, seats: torch.Tensor, n_rows: int, device="cpu") -> torch.Tensor:
+    """Token rows 0..n_rows-1 of the K (kv = 0) or V (kv = 1) history of each seat in `seats` in one layer:
+    [len(seats), n_rows, 8, 128] fp32 whose values are a pure function of (seed, layer, kv, seat, position, head, dim),
+    bit-identical on the CPU and on the GPU. Each value is (a + b + c + d - 126) / 64 for four 6-bit fields of a hashed
+    counter: symmetric, bell-shaped (Irwin-Hall of four uniforms), standard deviation 0.577, and exactly representable
+    in bf16. This lets a fixture made by the reference on the CPU and a GPU test share a K/V history far too large to
+    store."""
+    seats = torch.as_tensor(seats, dtype=torch.int64, device=device).view(-1)
+    key = ((int(seed) * 64 + int(layer)) * 2 + int(kv)) * 1_000_003 + seats
+    s = _mix32(key & _M32)
+    e = torch.arange(n_rows * ROW_ELEMS, dtype=torch.int64, device=device)
+    x = _mix32((e[None, :] + s[:, None] * 0x9E37) & _M32)
+    u = (x & 63) + ((x >> 6) & 63) + ((x >> 12) & 63) + ((x >> 18) & 63) - 126
+    return (u.to(torch.float32) * (1.0 / 64)).view(seats.numel(), n_rows, NKV, HD)
+
+
+def history_rows(seed: int, layer: int, kv: int, seat: int, n_rows: int, device="cpu") -> torch.Tensor:
+    """history_block for one seat: [n_rows, 8, 128]."""
+    return history_block(seed, layer, kv, torch.tensor([seat]), n_rows, device)[0]

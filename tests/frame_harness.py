@@ -1,4 +1,6 @@
-"""The engine's frame step on the GPU with every attention and K/V append on the q3attn kernels.
+"""Test and benchmark harness: the engine's frame step on the GPU with every attention and K/V append on the q3attn
+kernels. It is test infrastructure, not part of the q3attn package: it restates the reference engine's own host
+orchestration so the kernels can be checked and timed inside the frame they serve.
 
 Mirrors engine/talker.py (Talker: seats, paged K/V, per-seat sampling state, one CUDA graph per batch bucket) and
 engine/code_predictor.py (CodePredictor: 16-slot K/V scratch, 15 sampled steps), with the attention hot path replaced:
@@ -15,7 +17,7 @@ talker.py:25, 42), and the weights come from q3attn.weights (random init; no che
 import torch
 import torch.nn.functional as F
 
-from . import ops
+from q3attn import ops
 
 NEG = float("-inf")
 
@@ -291,3 +293,23 @@ class Talker:
                 rows = self.seat_pages[s].long()
                 self.kc[l][rows] = kv[0, l, s].view(self.P, self.page, self.nkv, self.hd).to(self.d, self.dt)
                 self.vc[l][rows] = kv[1, l, s].view(self.P, self.page, self.nkv, self.hd).to(self.d, self.dt)
+
+    @torch.inference_mode()
+    def load_history_block(self, seed, ctx, seats=None, chunk=64):
+        """Fill seats' K/V pages (positions 0..ctx[s]-1, through the block table) with synth.history_block rows,
+        generated on the device in chunks of seats; ctx is a CPU tensor over all seats."""
+        from q3attn import synth
+        seats = list(range(self.n_seats)) if seats is None else list(seats)
+        for l in range(len(self.W.layers)):
+            for a in range(0, len(seats), chunk):
+                sc = torch.tensor(seats[a:a + chunk], dtype=torch.int64)
+                n = int(ctx[sc].max())
+                if n == 0:
+                    continue
+                pos = torch.arange(n, device=self.d)
+                valid = pos[None, :] < ctx[sc].to(self.d)[:, None]                          # [c, n]
+                bt = self.seat_pages[sc.to(self.d)].long()                                  # [c, P]
+                rows = bt.gather(1, (pos // self.page)[None, :].expand(len(sc), n)) * self.page + pos % self.page
+                for kv, pool in ((0, self.kc[l]), (1, self.vc[l])):
+                    vals = synth.history_block(seed, l, kv, sc, n, self.d)                  # [c, n, 8, 128]
+                    pool.view(-1, self.nkv, self.hd)[rows[valid]] = vals[valid].to(self.dt)

@@ -41,6 +41,12 @@ def digest(*ts) -> str:
     return h.hexdigest()[:32]
 
 
+def b16(t: torch.Tensor) -> torch.Tensor:
+    """fp32 values rounded to the nearest bf16: the inputs a bf16 kernel sees, so its output can be held to the bf16
+    output tolerance against the reference's fp32 result on exactly those inputs."""
+    return t.to(torch.bfloat16).float()
+
+
 def ref_modules():
     if not REF:
         raise RuntimeError("set Q3_REFERENCE to the reference checkout to regenerate the fixtures")
@@ -73,6 +79,8 @@ def gen_decode(talker):
         ns = types.SimpleNamespace(kc=[torch.cat(rowsK)], vc=[torch.cat(rowsV)], nkv=8, hd=128, nh=16, scale=128 ** -0.5)
         o = talker.Talker._attn_ref(ns, d["q"], 0, torch.tensor(slot), lay.ctx)
         out[f"s{seed}_out"] = o.numpy()
+        ns.kc, ns.vc = [b16(ns.kc[0])], [b16(ns.vc[0])]          # the same case on bf16-representable inputs
+        out[f"s{seed}_b16_out"] = talker.Talker._attn_ref(ns, b16(d["q"]), 0, torch.tensor(slot), lay.ctx).numpy()
         out[f"s{seed}_ctx"] = lay.ctx.numpy()
         out[f"s{seed}_bt"] = lay.block_table.numpy()
         out[f"s{seed}_digest"] = np.array(digest(d["q"], d["k_pool"], d["v_pool"]))
@@ -102,6 +110,7 @@ def gen_prefill(arrivals):
         ns = types.SimpleNamespace(T=types.SimpleNamespace(nkv=8, nh=16, hd=128, scale=128 ** -0.5))
         o = arrivals.FastAdmit._attn_ref(ns, q, K, V)
         out[f"{name}_out"] = o.numpy()
+        out[f"{name}_b16_out"] = arrivals.FastAdmit._attn_ref(ns, b16(q), b16(K), b16(V)).numpy()
         out[f"{name}_digest"] = np.array(digest(q, K, V))
     np.savez_compressed(os.path.join(HERE, "prefill.npz"), **out)
 
@@ -116,9 +125,11 @@ def gen_cp(code_predictor):
         cp.nh, cp.nkv, cp.hd, cp.scale, cp.ffn = 16, 8, 128, 128 ** -0.5, 8
         mask = torch.full((16, 16), float("-inf")).triu(1)
         x = torch.zeros(B, 2048)
-        o = code_predictor.CodePredictor._post(cp, x, d["q"], d["K"], d["V"], mask[p], torch.eye(2048), torch.ones(2048),
-                                               torch.zeros(16, 2048), torch.zeros(2048, 8))
+        args = (mask[p], torch.eye(2048), torch.ones(2048), torch.zeros(16, 2048), torch.zeros(2048, 8))
+        o = code_predictor.CodePredictor._post(cp, x, d["q"], d["K"], d["V"], *args)
         out[f"p{p}_out"] = o.numpy()
+        out[f"p{p}_b16_out"] = code_predictor.CodePredictor._post(cp, x, b16(d["q"]), b16(d["K"]), b16(d["V"]),
+                                                                  *args).numpy()
         out[f"p{p}_digest"] = np.array(digest(d["q"], d["K"], d["V"]))
     np.savez_compressed(os.path.join(HERE, "cp_attn.npz"), **out)
 
@@ -153,8 +164,9 @@ def frame_state(size, n_layers, n_seats, n_live, seat_len, ctx_rng, seed):
     return W, dict(live=live, ctx=ctx, kv=kv, x_in=x_in, trail=trail, trail_len=trail_len, ngen=ngen, max_text=max_text)
 
 
-def ref_talker(talker_mod, code_predictor_mod, W, n_seats, seat_len, bucket, st):
-    """A reference Talker built without CUDA (object.__new__ + the attributes of engine/talker.py:24-54), fp32, top_k=1."""
+def ref_talker(talker_mod, code_predictor_mod, W, n_seats, seat_len, bucket, st, kc=None, vc=None):
+    """A reference Talker built without CUDA (object.__new__ + the attributes of engine/talker.py:24-54), fp32, top_k=1.
+    The K/V pools come from st["kv"] unless kc / vc (lists of per-layer pools in the reference layout) are given."""
     T = object.__new__(talker_mod.Talker)
     T.W = W
     T.d, T.dt = torch.device("cpu"), torch.float32
@@ -163,8 +175,10 @@ def ref_talker(talker_mod, code_predictor_mod, W, n_seats, seat_len, bucket, st)
     T.scale = float(T.hd) ** -0.5
     T.temperature, T.top_k, T.rep, T.min_new = 0.9, 1, 1.05, 2
     S1 = n_seats + 1
-    T.kc = [st["kv"][0, l].reshape(S1 * T.P, 256, 8, 128).clone() for l in range(len(W.layers))]
-    T.vc = [st["kv"][1, l].reshape(S1 * T.P, 256, 8, 128).clone() for l in range(len(W.layers))]
+    if kc is None:
+        kc = [st["kv"][0, l].reshape(S1 * T.P, 256, 8, 128).clone() for l in range(len(W.layers))]
+        vc = [st["kv"][1, l].reshape(S1 * T.P, 256, 8, 128).clone() for l in range(len(W.layers))]
+    T.kc, T.vc = kc, vc
     T.pos = st["ctx"].clone()
     T.x_in = st["x_in"].clone()
     T.seen = torch.zeros(S1, W.vocab, dtype=torch.bool)
@@ -218,6 +232,81 @@ def gen_frames(talker, code_predictor):
                             cp_tf_logits1=cp1.numpy().astype(np.float16),
                             digest=np.array(digest(st["kv"][:, :, :, :8], st["x_in"], W.layers[0].qkv, W.cp_head[3])))
         print(f"[golden] {name}: codes {tuple(torch.stack(codes).shape)}", flush=True)
+
+
+# --------------------------------------------------------------------------- the config-5 frame (e2e criterion)
+# The GPU side runs a 576-seat bucket (all seats live, ctx U[200,1200], 28 layers, 16-token shuffled pages); the
+# reference computes `checked` of those seats (seats are independent, so their results do not depend on the others).
+# The K/V history comes from synth.history_rows (a hash of the position, identical on the CPU and the GPU), so it is
+# regenerated on both sides instead of stored.
+FRAME_C5 = dict(size="0.6B", n_seats=576, checked=128, seat_len=1280, ctx=(200, 1200), frames=2, seed=9, n_full=16)
+
+
+def c5_state(c=FRAME_C5):
+    """bf16-rounded weights (fp32 tensors) and the state of all n_seats + 1 seats: ctx, pending inputs, trailing text,
+    generation counters, and the checked seats (sorted)."""
+    W = weights.cast(weights.cast(weights.random_weights(c["seed"], c["size"], max_pos=c["seat_len"] + 64),
+                                  torch.bfloat16), torch.float32)
+    g = synth.cpu_gen(c["seed"] + 500)
+    n, S1 = c["n_seats"], c["n_seats"] + 1
+    ctx = torch.zeros(S1, dtype=torch.int64)
+    ctx[:n] = torch.randint(c["ctx"][0], c["ctx"][1] + 1, (n,), generator=g)
+    sel = torch.randperm(n, generator=g)[:c["checked"]].sort().values
+    max_text = 16
+    x_in = synth.randn((S1, W.H), g, 0.1, torch.bfloat16).float()
+    trail = synth.randn((S1, max_text + 1, W.H), g, 0.02, torch.bfloat16).float()
+    trail_len = torch.randint(0, max_text + 1, (S1,), generator=g)
+    ngen = torch.randint(0, 6, (S1,), generator=g)
+    return W, dict(ctx=ctx, sel=sel, x_in=x_in, trail=trail, trail_len=trail_len, ngen=ngen, max_text=max_text)
+
+
+def c5_history_digest(c=FRAME_C5, st=None, device="cpu"):
+    """Digest of a few history rows (first checked seat, layers 0 and 27, K and V): pins the generator across devices."""
+    seat = int(st["sel"][0])
+    n = int(st["ctx"][seat])
+    return digest(*[synth.history_rows(c["seed"], l, kv, seat, n, device).cpu() for l in (0, 27) for kv in (0, 1)])
+
+
+def gen_frame_c5(talker, code_predictor):
+    c = FRAME_C5
+    W, st = c5_state(c)
+    sel, n, L = st["sel"], c["checked"], c["seat_len"]
+    P = L // 256
+    # the checked seats' pools in the reference layout (seat i of the reference = seat sel[i]); only the history rows
+    # are written (torch.empty pages never touched stay unbacked), and the reference reads no other row
+    kc = [torch.empty((n + 1) * P, 256, 8, 128) for _ in W.layers]
+    vc = [torch.empty((n + 1) * P, 256, 8, 128) for _ in W.layers]
+    for l in range(len(W.layers)):
+        for i, s in enumerate(sel.tolist()):
+            m = int(st["ctx"][s])
+            kc[l].view(-1, 8, 128)[i * L:i * L + m] = synth.history_rows(c["seed"], l, 0, s, m)
+            vc[l].view(-1, 8, 128)[i * L:i * L + m] = synth.history_rows(c["seed"], l, 1, s, m)
+    rows = torch.cat([sel, torch.tensor([c["n_seats"]])])        # + the scratch seat
+    sub = dict(ctx=st["ctx"][rows].clone(), x_in=st["x_in"][rows], trail=st["trail"][rows],
+               trail_len=st["trail_len"][rows], ngen=st["ngen"][rows], max_text=st["max_text"])
+    sub["ctx"][n] = 0
+    T = ref_talker(talker, code_predictor, W, n, L, n, sub, kc=kc, vc=vc)
+    T.s_seat[:n] = torch.arange(n)
+    codes, hs = [], []
+    dec = T._decode
+    T.decode = lambda *args: hs.append(dec(*args)) or hs[-1]
+    with torch.inference_mode():
+        for f in range(c["frames"]):
+            T.pos[n] = 0
+            T._frame(n)
+            codes.append(T.o_codes[:n].clone())
+        h1 = hs[0][:n].clone()
+        lg1 = torch.nn.functional.linear(h1, W.codec_head).float()
+        cp1 = T.cp.tf_logits(h1, codes[0])                          # engine/code_predictor.py:74-82
+    top2 = cp1.topk(2, -1).values
+    np.savez_compressed(os.path.join(HERE, "frame_c5.npz"), sel=sel.numpy(), codes=torch.stack(codes).numpy().astype(np.int16),
+                        h1=h1.numpy(), c0_logits1=lg1.numpy().astype(np.float16),
+                        cp_tf_argmax=cp1.argmax(-1).numpy().astype(np.int16),
+                        cp_tf_gap=(top2[..., 0] - top2[..., 1]).numpy().astype(np.float16),
+                        cp_tf_logits_head=cp1[:c["n_full"]].numpy().astype(np.float16),
+                        digest=np.array(digest(st["x_in"], W.layers[0].qkv, W.cp_head[3])),
+                        history_digest=np.array(c5_history_digest(c, st)))
+    print(f"[golden] frame_c5: {n} of {c['n_seats']} seats, codes {tuple(torch.stack(codes).shape)}", flush=True)
 
 
 # --------------------------------------------------------------------------- admission (shared prefix + graphed prefill)
@@ -413,6 +502,8 @@ if __name__ == "__main__":
         gen_cp(code_predictor)
     if not only or "frames" in only:
         gen_frames(talker, code_predictor)
+    if not only or "frame_c5" in only:
+        gen_frame_c5(talker, code_predictor)
     if not only or "admit" in only:
         gen_admit(talker, arrivals, code_predictor)
     if not only or "ring" in only:

@@ -57,7 +57,7 @@ def _rel(a, b):
 
 def test_admission_matches_reference_fastadmit(q3, golden_dir):
     from q3attn.admit import Admit
-    from q3attn.frame import Talker
+    from frame_harness import Talker
     c = mg.ADMIT
     W, st, prefix, tab, rem, trail_ids, tlen = mg.admit_inputs()
     gold = np.load(os.path.join(golden_dir, "admit.npz"))

@@ -72,14 +72,17 @@ def test_decode_c1(q3, seed, append):
 
 
 def test_decode_c1_against_reference_golden(q3, golden_dir):
-    """The GPU kernel against the reference's own Talker._attn_ref output (fp32 inputs rounded to bf16 here)."""
+    """The GPU kernel against the reference's own Talker._attn_ref output: at the north-star bounds against the
+    reference run on the bf16-rounded inputs the kernel sees, and against the reference on the original fp32 inputs
+    with the input rounding's share added to the max-abs bound (rounding N(0,1) inputs to bf16 moves outputs by up to
+    ~1e-2 by itself)."""
     import make_golden as mg
     g = np.load(os.path.join(golden_dir, "decode_c1.npz"))
     for seed in (1, 11, 12):
         lay, d = mg.c1_inputs(seed)
         out, _ = _run_decode(q3, lay, {k: v.to(torch.bfloat16) for k, v in d.items()}, append=False)
-        # bf16 rounding of N(0,1) inputs moves outputs by up to ~1e-2; the reference output is fp32 on fp32 inputs
-        assert_close_attn(out, torch.from_numpy(g[f"s{seed}_out"]), atol=2e-2, rtol=2e-2, what=f"golden seed {seed}")
+        assert_close_attn(out, torch.from_numpy(g[f"s{seed}_b16_out"]), what=f"golden seed {seed} (bf16 inputs)")
+        assert_close_attn(out, torch.from_numpy(g[f"s{seed}_out"]), atol=2e-2, what=f"golden seed {seed} (fp32 inputs)")
 
 
 EDGE_CTX = [1, 2, 15, 16, 17, 31, 32, 33, 255, 256, 257]

@@ -1,5 +1,5 @@
 """GPU: a whole random-init frame step (talker decode over paged K/V + codebook-0 sampling + the 15 code-predictor
-steps) through q3attn.frame.Talker under CUDA-graph replay, against what the reference's own Talker._frame computed in
+steps) through the frame harness (tests/frame_harness.py) under CUDA-graph replay, against what the reference's own Talker._frame computed in
 fp32 on the same bf16-representable weights and state (tests/golden/frame*.npz)."""
 import os
 
@@ -10,7 +10,7 @@ import torch.nn.functional as F
 
 import make_golden as mg
 from q3attn import synth, weights
-from q3attn.frame import CodePredictor, Talker, mlp, rms, rope
+from frame_harness import CodePredictor, Talker, mlp, rms, rope
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -149,4 +149,87 @@ def test_frame_against_reference(golden_dir, name):
     assert m["h_rel"] < 0.05 and m["c0_rel"] < 0.05 and m["cp_rel"] < 0.03
     assert m["h_rel"] <= 1.2 * mt["h_rel"] + 1e-3 and m["cp_rel"] <= 1.2 * mt["cp_rel"] + 1e-3
     # every position decided by more than the noise floor picks the reference's code (>= 99%)
+    assert m["c0_decisive_agree"] >= 0.99 and m["cp_decisive_agree"] >= 0.99
+    # teacher-forced argmax agreement over ALL positions (codebook 0 of frame 1 and the 15 CP heads given the
+    # reference's codes; no cascade): no worse than the twin that uses the reference's own attention expressions
+    n_live = len(g["live"])
+    tf = (m["c0_argmax"] * n_live + m["cp_argmax"] * 15 * n_live) / (16 * n_live)
+    tf_t = (mt["c0_argmax"] * n_live + mt["cp_argmax"] * 15 * n_live) / (16 * n_live)
+    print(f"[frame] {name} teacher-forced all-position agreement: q3attn {tf:.4f}, torch twin {tf_t:.4f}", flush=True)
+    assert tf >= tf_t - 0.005
+
+
+def c5_run(cls, g, W, st, bt):
+    """Config 5's frame for `cls` (q3attn Talker or the torch twin): 576 live seats in a 576-seat bucket, 28 layers,
+    ctx U[200,1200], 16-token shuffled pages, greedy. Returns the teacher-forced values of the checked seats, their
+    free-running codes over the fixture's frames, and the continuous errors."""
+    c = mg.FRAME_C5
+    n_seats, L = c["n_seats"], c["seat_len"]
+    T = cls(weights.cast(W, torch.bfloat16, DEV), n_seats, L, buckets=[n_seats], page=16, block_table=bt,
+            max_text=st["max_text"], top_k=1)
+    T.load_history_block(c["seed"], st["ctx"])
+    T.pos.copy_(st["ctx"])
+    T.x_in.copy_(st["x_in"])
+    T.ngen.copy_(st["ngen"])
+    T.trail.copy_(st["trail"])
+    T.trail_len.copy_(st["trail_len"])
+    sel = torch.from_numpy(g["sel"]).long().to(DEV)
+    ref_h1 = torch.from_numpy(g["h1"])
+    ref_codes = torch.from_numpy(g["codes"].astype(np.int64))
+    seats = torch.arange(n_seats, device=DEV)
+    with torch.inference_mode():
+        pos = T.pos[seats].clone()
+        h = T.decode(T.x_in[seats], T.W.cos[pos][:, None, :], T.W.sin[pos][:, None, :], pos, T.seat_pages[seats])
+        h1 = h[sel]
+        lg1 = F.linear(h1, T.W.codec_head).float()
+        cp_tf = T.cp.tf_logits(ref_h1.to(DEV, torch.bfloat16), ref_codes[0].to(DEV))
+    T.capture()
+    codes = torch.stack([T.step(list(range(n_seats))).clone().cpu() for _ in range(c["frames"])])[:, sel.cpu()]
+    out = dict(h1=h1.float().cpu(), lg1=lg1.cpu(), cp_tf=cp_tf.cpu(), codes=codes)
+    del T
+    torch.cuda.empty_cache()
+    return out
+
+
+def test_frame_c5_shape_against_reference(golden_dir):
+    """The north star's end-to-end criterion at config 5's shape, against the reference's own fp32 Talker._frame
+    (tests/golden/frame_c5.npz; 128 checked seats of the 576). Asserted: the talker hidden and the logits within bf16
+    reach of the fp32 result; teacher-forced greedy agreement over ALL positions (codebook 0 of frame 1, and the 15 CP
+    heads given the reference's codes, which do not cascade) no worse than a twin that runs the reference's own
+    attention expressions in the same frame; >= 99% agreement on every position decided by more than the bf16 noise
+    floor. The free-running agreement (one flipped near-tie changes every later code) is reported."""
+    g = np.load(os.path.join(golden_dir, "frame_c5.npz"))
+    c = mg.FRAME_C5
+    W, st = mg.c5_state(c)
+    assert str(g["digest"]) == mg.digest(st["x_in"], W.layers[0].qkv, W.cp_head[3]), "state generator drifted"
+    assert str(g["history_digest"]) == mg.c5_history_digest(c, st, DEV), "history generator differs on the GPU"
+    bt = _shuffled_table(c["n_seats"] + 1, c["seat_len"] // 16, c["seed"] + 77)
+    ref_h1 = torch.from_numpy(g["h1"])
+    ref_lg1 = torch.from_numpy(g["c0_logits1"].astype(np.float32))
+    ref_cp_arg = torch.from_numpy(g["cp_tf_argmax"].astype(np.int64))
+    ref_cp_gap = torch.from_numpy(g["cp_tf_gap"].astype(np.float32))
+    ref_cp_head = torch.from_numpy(g["cp_tf_logits_head"].astype(np.float32))
+    ref_codes = torch.from_numpy(g["codes"].astype(np.int64))
+    n, nf = c["checked"], c["n_full"]
+    res = {}
+    for name, cls in (("q3attn", Talker), ("torch twin", TorchAttnTalker)):
+        r = c5_run(cls, g, W, st, bt)
+        c0_same = r["lg1"].argmax(-1) == ref_lg1.argmax(-1)
+        cp_same = r["cp_tf"].argmax(-1) == ref_cp_arg
+        sigma = (r["cp_tf"][:nf] - ref_cp_head).pow(2).mean().sqrt()
+        dec = ref_cp_gap > 4 * sigma
+        c0_dec, c0_frac = decisive_agreement(r["lg1"], ref_lg1)
+        res[name] = m = dict(
+            h_rel=rel(r["h1"], ref_h1), c0_rel=rel(r["lg1"], ref_lg1), cp_rel=rel(r["cp_tf"][:nf], ref_cp_head),
+            c0_argmax=float(c0_same.float().mean()), cp_argmax=float(cp_same.float().mean()),
+            tf_all=float((c0_same.sum() + cp_same.sum()) / (n + 15 * n)),
+            c0_decisive_agree=c0_dec, c0_decisive_frac=c0_frac,
+            cp_decisive_agree=float(cp_same[dec].float().mean()), cp_decisive_frac=float(dec.float().mean()),
+            free_run_agree=float((r["codes"] == ref_codes).float().mean()),
+            frame1_agree=float((r["codes"][0] == ref_codes[0]).float().mean()))
+        print(f"[frame_c5] {name}: " + ", ".join(f"{k} {v:.4f}" for k, v in m.items()), flush=True)
+    m, mt = res["q3attn"], res["torch twin"]
+    assert m["h_rel"] < 0.05 and m["c0_rel"] < 0.05 and m["cp_rel"] < 0.03
+    assert m["h_rel"] <= 1.2 * mt["h_rel"] + 1e-3 and m["cp_rel"] <= 1.2 * mt["cp_rel"] + 1e-3
+    assert m["tf_all"] >= mt["tf_all"] - 0.005
     assert m["c0_decisive_agree"] >= 0.99 and m["cp_decisive_agree"] >= 0.99

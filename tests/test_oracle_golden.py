@@ -24,6 +24,9 @@ def test_decode_c1_matches_reference(golden_dir, seed):
     assert np.array_equal(g[f"s{seed}_bt"], lay.block_table.numpy())
     o = OA.decode_attention(d["q"], d["k_pool"], d["v_pool"], lay.ctx, lay.block_table, 128 ** -0.5)
     np.testing.assert_allclose(o.numpy(), g[f"s{seed}_out"], rtol=1e-5, atol=1e-6)
+    o = OA.decode_attention(mg.b16(d["q"]), mg.b16(d["k_pool"]), mg.b16(d["v_pool"]), lay.ctx, lay.block_table,
+                            128 ** -0.5)
+    np.testing.assert_allclose(o.numpy(), g[f"s{seed}_b16_out"], rtol=1e-5, atol=1e-6)
 
 
 @pytest.mark.parametrize("name", list(mg.PREFILL_CASES))
@@ -33,6 +36,8 @@ def test_prefill_matches_reference(golden_dir, name):
     assert str(g[f"{name}_digest"]) == mg.digest(q, K, V)
     o = OA.prefill_prefix(q, K, V, 128 ** -0.5)
     np.testing.assert_allclose(o.numpy(), g[f"{name}_out"], rtol=1e-5, atol=1e-6)
+    o = OA.prefill_prefix(mg.b16(q), mg.b16(K), mg.b16(V), 128 ** -0.5)
+    np.testing.assert_allclose(o.numpy(), g[f"{name}_b16_out"], rtol=1e-5, atol=1e-6)
 
 
 def test_prefill_varlen_equals_per_sequence(golden_dir):
@@ -54,6 +59,8 @@ def test_cp_attention_matches_reference(golden_dir, p):
     assert str(g[f"p{p}_digest"]) == mg.digest(d["q"], d["K"], d["V"])
     o = OA.cp_attention(d["q"], d["K"], d["V"], p + 1, 128 ** -0.5)
     np.testing.assert_allclose(o.numpy(), g[f"p{p}_out"], rtol=1e-5, atol=1e-6)
+    o = OA.cp_attention(mg.b16(d["q"]), mg.b16(d["K"]), mg.b16(d["V"]), p + 1, 128 ** -0.5)
+    np.testing.assert_allclose(o.numpy(), g[f"p{p}_b16_out"], rtol=1e-5, atol=1e-6)
 
 
 def test_append_placement_identity_table_equals_flat_slot():
@@ -116,3 +123,13 @@ def test_frame_oracle_matches_reference(golden_dir, name):
     page = 16
     kr = torch.stack([O.kc[0].view(-1, 8, 128)[OA.slot_of(bt, int(s), int(st["ctx"][s]), page)] for s in live])
     np.testing.assert_allclose(kr.numpy(), g["krow0"], rtol=1e-5, atol=1e-6)
+
+
+def test_c5_frame_fixture_inputs_regenerate(golden_dir):
+    """The config-5 frame fixture's inputs come back from their seeds: the engine state and the hashed K/V history
+    (the GPU test regenerates the same history on the device and checks the same digest there)."""
+    g = _load(golden_dir, "frame_c5.npz")
+    W, st = mg.c5_state(mg.FRAME_C5)
+    assert str(g["digest"]) == mg.digest(st["x_in"], W.layers[0].qkv, W.cp_head[3])
+    assert str(g["history_digest"]) == mg.c5_history_digest(mg.FRAME_C5, st)
+    assert np.array_equal(g["sel"], st["sel"].numpy())
