@@ -51,6 +51,7 @@ def parse():
     p.add_argument("--seed", type=int, default=2)
     p.add_argument("--variant", type=int, default=0, help="decode kernel variant (q3_set_decode_variant)")
     p.add_argument("--num-splits", type=int, default=0)
+    p.add_argument("--prefill-kernel", type=int, default=0, help="prefill kernel (q3_set_prefill_kernel): 0 TMA, 1 single")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -437,6 +438,7 @@ def bench_aux(a):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     peak, peak_kind = hbm_peak()
+    q3attn.set_prefill_kernel(a.prefill_kernel)
 
     def timed(fn, n):
         s = torch.cuda.Stream(device=dev)

@@ -120,14 +120,21 @@ int q3_kv_append_paged(const void* k, const void* v, int64_t row_stride,
  * (N_i >= R_i) of k/v [Tk, 8, 128], and prefix_lens[i] keys already in the pages of block-table row seat_ids[i]
  * (prefix_lens NULL: none; seat_ids NULL: row i). Keys are indexed prefix first; with causal, query j sees keys
  * 0 .. prefix + N - R + j (bottom-right alignment). write_kv: the new rows also go to positions prefix + r of the
- * seat's pages. max_seqlen_q must be >= every R_i. Output rows [Tq, 16, 128] bf16. */
-int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v, int64_t kv_row_stride,
+ * seat's pages. max_seqlen_q must be >= every R_i; q_rows = Tq and kv_rows = Tk are the row counts of q and k/v (no
+ * row at or past them is read). Output rows [Tq, 16, 128] bf16. */
+int q3_prefill(const void* q, int64_t q_row_stride, int64_t q_rows,
+               const void* k, const void* v, int64_t kv_row_stride, int64_t kv_rows,
                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t num_seqs, int32_t max_seqlen_q,
                const int32_t* prefix_lens, const int32_t* seat_ids,
                void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,
                const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
                int32_t write_kv, int32_t causal, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
                float softmax_scale, void* out, int64_t out_row_stride, void* stream);
+
+/* Prefill kernel used by q3_prefill: 0 = the warp-specialised TMA kernel wherever the call fits it (default; other
+ * calls use kernel 1), 1 = the single-warpgroup kernel for every call. Other values leave the selection unchanged.
+ * Returns the previous value. No reference counterpart (a tuning knob of this library). */
+int q3_set_prefill_kernel(int kernel);
 
 /* ---------------------------------------------------------------- code-predictor attention
  * Replaces cp_attn(q, K, V, n_live, scale) (engine/cp_attn.py:33-39), i.e. the attention expression of

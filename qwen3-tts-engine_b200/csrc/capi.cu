@@ -662,7 +662,14 @@ int q3_ring_window_attn(const void* q, const void* k_new, const void* v_new, int
   return record(q3::launch_ring_attn(a, static_cast<cudaStream_t>(stream)));
 }
 
-int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v, int64_t kv_row_stride,
+int q3_set_prefill_kernel(int kernel) {
+  const int prev = q3::g_prefill_kernel;
+  if (kernel == 0 || kernel == 1) q3::g_prefill_kernel = kernel;
+  return prev;
+}
+
+int q3_prefill(const void* q, int64_t q_row_stride, int64_t q_rows, const void* k, const void* v,
+               int64_t kv_row_stride, int64_t kv_rows,
                const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t num_seqs, int32_t max_seqlen_q,
                const int32_t* prefix_lens, const int32_t* seat_ids, void* k_pool, void* v_pool, int32_t num_pages,
                int32_t page_size, const int32_t* block_table, int64_t block_table_stride, int32_t max_pages_per_seat,
@@ -670,8 +677,8 @@ int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v
                float softmax_scale, void* out, int64_t out_row_stride, void* stream) {
   int rc = check_family(num_heads, num_kv_heads, head_dim);
   if (rc != Q3_OK) return rc;
-  if (num_seqs < 0 || max_seqlen_q < 0) return Q3_ERR_INVALID;
-  if (num_seqs == 0) return Q3_OK;
+  if (num_seqs < 0 || max_seqlen_q < 0 || q_rows < 0 || kv_rows < 0) return Q3_ERR_INVALID;
+  if (num_seqs == 0 || q_rows == 0) return Q3_OK;
   if (!q || !k || !v || !cu_seqlens_q || !cu_seqlens_k || !out) return Q3_ERR_INVALID;
   if (q_row_stride < q3::kQHeads * q3::kHeadDim || out_row_stride < q3::kQHeads * q3::kHeadDim ||
       kv_row_stride < q3::kKvHeads * q3::kHeadDim)
@@ -691,9 +698,11 @@ int q3_prefill(const void* q, int64_t q_row_stride, const void* k, const void* v
   q3::PrefillArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.q_stride = q_row_stride;
+  a.q_rows = q_rows;
   a.k = static_cast<const __nv_bfloat16*>(k);
   a.v = static_cast<const __nv_bfloat16*>(v);
   a.kv_stride = kv_row_stride;
+  a.kv_rows = kv_rows;
   a.cu_q = cu_seqlens_q;
   a.cu_k = cu_seqlens_k;
   a.num_seqs = num_seqs;

@@ -21,8 +21,7 @@
 // shared memory in the canonical no-swizzle core-matrix layout (8 rows x 16 bytes per core matrix) described by the
 // UMMA shared-memory descriptors below. A single thread issues the MMAs; tcgen05.commit arrives on an mbarrier that
 // the other threads wait on (bounded waits).
-#include "q3_common.cuh"
-#include "q3_kernels.h"
+#include "prefill_common.cuh"
 
 namespace q3 {
 
@@ -43,86 +42,6 @@ struct PfSmem {
   static constexpr int kBytes = kTmemSlot + 16;
 };
 
-// ---------------------------------------------------------------- UMMA descriptors
-// Shared-memory matrix descriptor, no swizzle: start address, leading and stride byte offsets (all >> 4), version 1.
-__device__ __forceinline__ uint64_t umma_smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((addr >> 4) & 0x3fff);
-  d |= static_cast<uint64_t>((lbo >> 4) & 0x3fff) << 16;
-  d |= static_cast<uint64_t>((sbo >> 4) & 0x3fff) << 32;
-  d |= static_cast<uint64_t>(1) << 46;                       // descriptor version for sm_100
-  return d;                                                  // base offset 0, lbo mode 0, layout type 0 (no swizzle)
-}
-
-// Instruction descriptor of kind::f16: bf16 A and B, fp32 D, M x N, A/B major-ness (0 = K-major, 1 = MN-major).
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int a_mn_major, int b_mn_major) {
-  return (1u << 4)                                           // D format: f32
-         | (1u << 7)                                         // A format: bf16
-         | (1u << 10)                                        // B format: bf16
-         | (static_cast<uint32_t>(a_mn_major) << 15) | (static_cast<uint32_t>(b_mn_major) << 16)
-         | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      :
-      : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
-}
-
-// 2^x by the PTX approximate base-2 exponential (relative error ~2^-22, flushes denormals): the probabilities are
-// rounded to bf16 right after.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// 32 consecutive fp32 columns of this thread's TMEM lane (warp w reads lanes 32w..32w+31).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
-      :
-      : "r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])),
-        "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
-        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
-        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
-        "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
-        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
-        "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
-        "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
-        "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
-      : "memory");
-}
-
 // Shared-memory offsets of the canonical no-swizzle layouts (element = one bf16).
 //   K-major [rows][128 or 64 k]: core matrix (8 rows x 8 k) = 128 contiguous bytes; k-chunks 128 B apart (LBO),
 //   8-row groups `sbo` bytes apart (SBO).
@@ -133,41 +52,6 @@ __device__ __forceinline__ uint32_t kmajor_off(int row, int kchunk, int sbo) {
 //   128 B apart (LBO), 8-dim groups 1024 B apart (SBO).
 __device__ __forceinline__ uint32_t v_off(int key, int dchunk) {
   return dchunk * 1024 + (key >> 3) * 128 + (key & 7) * 16;
-}
-
-struct PfSeq {
-  int q0, R, k0, Nn, P, seat;
-};
-
-__device__ __forceinline__ PfSeq pf_seq(const PrefillArgs& a, int i) {
-  PfSeq s;
-  s.q0 = a.cu_q[i];
-  s.R = a.cu_q[i + 1] - s.q0;
-  s.k0 = a.cu_k[i];
-  s.Nn = a.cu_k[i + 1] - s.k0;
-  s.P = a.prefix_lens ? a.prefix_lens[i] : 0;
-  s.seat = a.seat_ids ? a.seat_ids[i] : i;
-  return s;
-}
-
-// Row of the paged pool holding token `tok` of `seat` (bounds-checked page id).
-__device__ __forceinline__ long long pf_pool_row(const PrefillArgs& a, int seat, int tok) {
-  const int pidx = tok / a.page_size;
-  int pg = (pidx < a.max_pages) ? a.block_table[static_cast<long long>(seat) * a.bt_stride + pidx] : -1;
-  if (pg < 0 || pg >= a.num_pages) {
-    atomicOr(a.status, kStatusBadPage);
-    pg = 0;
-  }
-  return static_cast<long long>(pg) * a.page_size + (tok - pidx * a.page_size);
-}
-
-// Address of head h of key `kk` (combined index: prefix first, then new rows) in K (which = 0) or V (which = 1).
-__device__ __forceinline__ const __nv_bfloat16* pf_key_ptr(const PrefillArgs& a, const PfSeq& s, int h, int kk, int which) {
-  if (kk < s.P) {
-    const long long row = pf_pool_row(a, s.seat, kk);
-    return (which ? a.v_pool : a.k_pool) + row * (kKvHeads * kHeadDim) + h * kHeadDim;
-  }
-  return (which ? a.v : a.k) + static_cast<long long>(s.k0 + kk - s.P) * a.kv_stride + h * kHeadDim;
 }
 
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const PrefillArgs a) {
@@ -428,7 +312,19 @@ __global__ void __launch_bounds__(256) prefill_page_write_kernel(const PrefillAr
   }
 }
 
+int g_prefill_kernel = 0;
+
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
+  if (a.num_seqs == 0) return cudaSuccess;
+  bool launched = false;
+  if (g_prefill_kernel == 0) {
+    cudaError_t e = launch_prefill_tma(a, stream, &launched);
+    if (e != cudaSuccess) return e;
+  }
+  if (launched) {
+    if (a.write_kv) prefill_page_write_kernel<<<dim3(16, a.num_seqs), 256, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
   static thread_local int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);

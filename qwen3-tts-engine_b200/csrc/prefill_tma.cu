@@ -1,0 +1,491 @@
+// Prompt prefill attention, warp-specialised and TMA-fed, on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+// Same contract as prefill_kernel (prefill.cu): replaces flash_attn_varlen_func (engine/talker.py:169) and
+// flash_attn_func over a cached prefix (engine/arrivals.py:148); sequence i has R_i query rows, N_i new key rows and
+// P_i cached prefix keys in its pages, keys indexed prefix first, causal aligned to the bottom right.
+//
+// One CTA = (64-position query tile, KV head h, sequence); its 128 accumulator rows are the 64 positions of q heads 2h
+// and 2h+1, which share every K/V tile. Six warps with fixed roles:
+//   warp 4 (producer)   lane 0 issues TMA tensor copies (cp.async.bulk.tensor, no multicast, this GPU's memory only):
+//                       the Q tile once, then K and V tiles of 64 keys into a 2-stage ring, 128-byte swizzled so they
+//                       are UMMA operands as they land. Prefix keys come page by page out of the pool, new keys as one
+//                       box per 64 rows.
+//   warp 5 (MMA)        lane 0 issues S(t) = Q K(t)^T into one of two TMEM S buffers, then O += P(t-1) V(t-1) into
+//                       the TMEM O accumulator; tcgen05.commit arrives on mbarriers (S ready; K/V stage free; P.V done).
+//   warps 0-3 (softmax) thread r owns TMEM lane r = accumulator row r: reads S(t) (tcgen05.ld), online softmax in the
+//                       exp2 domain with a lazy running max (O rescaled in TMEM only when a max grows by more than 2^8),
+//                       writes P(t) as bf16 into the K slot of its stage (K(t) is dead once S(t) is done), and at the
+//                       end divides O by the row sums and stores the output rows.
+// While the softmax warps work on S(t), the tensor core computes S(t+1) and P(t-1) V(t-1), and the producer loads tile
+// t+2 into the stage P.V(t) frees. Shared memory: Q 32 KB + 2 stages x (K 16 KB + V 16 KB) = 96 KB, TMEM 256 columns
+// (S0, S1, O): two CTAs per SM. Every mbarrier wait is bounded (2 s); a timed-out role raises the status bit and an
+// abort flag the other roles poll, in-flight copies and MMAs are waited for (bounded), and TMEM is always freed.
+#include <cuda.h>
+
+#include <cstring>
+
+#include "prefill_common.cuh"
+
+namespace q3 {
+
+namespace {
+
+constexpr int kTwProducerWarp = 4, kTwMmaWarp = 5;
+constexpr int kTwThreads = 6 * 32;
+constexpr int kTwTmemCols = 256;
+constexpr uint32_t kTwOCol = 128;             // S(t) at column 64 * (t & 1), O at 128
+
+struct TwSmem {
+  static constexpr int kQ = 0;                // [2 dim halves][128 rows][128 B]: 32 KB, SW128 K-major
+  static constexpr int kStage0 = 32768;       // stage s: K [2 halves][64 keys][128 B], then V the same (32 KB)
+  static constexpr int kStageBytes = 32768;
+  static constexpr int kHalf = 8192;          // one dim half of a K or V tile
+  static constexpr int kV = 16384;            // V within a stage
+  static constexpr int kBars = kStage0 + 2 * kStageBytes;
+  static constexpr int kQFull = 0, kKvFull = 1, kKvEmpty = 3, kSFull = 5, kPFull = 7, kPvDone = 9, kFinal = 10;
+  static constexpr int kNumBars = 11;
+  static constexpr int kTmemSlot = kBars + 8 * kNumBars;
+  static constexpr int kAbort = kTmemSlot + 4;
+  static constexpr int kIssued = kAbort + 4;  // K/V tiles the producer has issued (read on the abort path)
+  static constexpr int kBytes = kIssued + 4;
+  static constexpr int kAlloc = kBytes + 1024;   // + slack to align the base to 1024 B (128-byte swizzle atoms)
+};
+
+struct PfTmaParams {
+  PrefillArgs a;
+  CUtensorMap tq;    // q rows    [q_rows][16 heads][128]
+  CUtensorMap tk;    // new keys  [kv_rows][8 heads][128]
+  CUtensorMap tv;
+  CUtensorMap tkp;   // pools     [num_pages * page_size][8 heads][128] (used when a prefix is given)
+  CUtensorMap tvp;
+  int box_rows;      // rows per pool box: min(page_size, 64)
+};
+
+// UMMA shared-memory descriptor of a 128-byte-swizzled operand: 8-row groups `sbo` bytes apart; `lbo` = the distance
+// between 64-element column blocks for an MN-major operand (unused, 16, for K-major).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t sbo, uint32_t lbo) {
+  uint64_t d = static_cast<uint64_t>((addr >> 4) & 0x3fff);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3fff) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3fff) << 32;
+  d |= static_cast<uint64_t>(1) << 46;        // descriptor version for sm_100
+  d |= static_cast<uint64_t>(2) << 61;        // layout: 128-byte swizzle
+  return d;
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Wait for phase `parity` of `bar`; false after 2 s or once another role has raised the abort flag.
+__device__ __forceinline__ bool tw_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+#pragma unroll 1
+  for (int i = 0; i < 1024; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+#pragma unroll 1
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > 2000000000ull) return false;
+  }
+}
+
+__device__ __forceinline__ void tw_fail(uint32_t* status, volatile int* abort_flag) {
+  atomicOr(status, kStatusWaitTimeout);
+  *abort_flag = 1;
+}
+
+__global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid_constant__ PfTmaParams p) {
+  const PrefillArgs& a = p.a;
+  extern __shared__ uint8_t tw_raw[];
+  uint8_t* smem = tw_raw + ((1024u - (smem_addr(tw_raw) & 1023u)) & 1023u);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.y;
+  const PfSeq s = pf_seq(a, blockIdx.z);
+  if (s.R <= 0) return;
+  const int ntq = (s.R + 63) / 64;
+  const int qt = ntq - 1 - static_cast<int>(blockIdx.x);     // heavy (late) query tiles take the low block indices
+  if (qt < 0) return;                                         // uniform per CTA; nothing allocated yet
+
+  // ---- key tiles: the prefix keys [0, P) in tiles of 64, then the new keys [0, N) in tiles of 64 (combined index
+  //      P + j), each tile from one source; only the keys some row of this query tile can see are visited
+  const int L = s.P + s.Nn, shift = L - s.R;
+  const int last_row = min(s.R - 1, qt * 64 + 63);
+  const int key_end = a.causal ? min(L, shift + last_row + 1) : L;
+  const int n_pre = (min(key_end, s.P) + 63) / 64;
+  const int n_new = (max(key_end - s.P, 0) + 63) / 64;
+  const int ntk = n_pre + n_new;                              // >= 1: key 0 is visible to every row
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TwSmem::kBars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TwSmem::kTmemSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TwSmem::kAbort);
+  volatile int* issued = reinterpret_cast<volatile int*>(smem + TwSmem::kIssued);
+  const uint32_t sbase = smem_addr(smem);
+
+  if (warp == kTwMmaWarp) {   // TMEM: 256 columns; shared memory limits an SM to two CTAs, so 512 columns suffice
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(kTwTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == kTwProducerWarp * 32) {
+    mbar_init(&bars[TwSmem::kQFull], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[TwSmem::kKvFull + i], 1);
+      mbar_init(&bars[TwSmem::kKvEmpty + i], 1);
+      mbar_init(&bars[TwSmem::kSFull + i], 1);
+      mbar_init(&bars[TwSmem::kPFull + i], 4);               // one arrival per softmax warp
+    }
+    mbar_init(&bars[TwSmem::kPvDone], 1);
+    mbar_init(&bars[TwSmem::kFinal], 1);
+    *abort_flag = 0;
+    *issued = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kTwProducerWarp) {
+    // ------------------------------------------------------------------ producer: TMA copies
+    if (lane == 0) {
+      prefetch_map(&p.tq);
+      prefetch_map(&p.tk);
+      prefetch_map(&p.tv);
+      const uint32_t qbar = smem_addr(&bars[TwSmem::kQFull]);
+      mbar_arrive_expect_tx(&bars[TwSmem::kQFull], 32768u);
+      for (int g = 0; g < 2; ++g)
+        for (int half = 0; half < 2; ++half)
+          tma_load_3d(sbase + TwSmem::kQ + half * 16384 + g * 8192, &p.tq, half * 64, 2 * h + g, s.q0 + qt * 64, qbar);
+      for (int t = 0; t < ntk; ++t) {
+        const int st = t & 1;
+        if (t >= 2 && !tw_wait(&bars[TwSmem::kKvEmpty + st], ((t >> 1) - 1) & 1, abort_flag)) {
+          tw_fail(a.status, abort_flag);
+          break;
+        }
+        uint64_t* fb = &bars[TwSmem::kKvFull + st];
+        const uint32_t fbar = smem_addr(fb);
+        mbar_arrive_expect_tx(fb, 32768u);
+        const uint32_t kdst = sbase + TwSmem::kStage0 + st * TwSmem::kStageBytes, vdst = kdst + TwSmem::kV;
+        if (t < n_pre) {
+          for (int r0 = 0; r0 < 64; r0 += p.box_rows) {
+            const int tok = t * 64 + r0;
+            // rows past the prefix in its last tile: any valid pool row (their V rows are zeroed before P.V)
+            const int row = tok < s.P ? static_cast<int>(pf_pool_row(a, s.seat, tok)) : 0;
+            for (int half = 0; half < 2; ++half) {
+              tma_load_3d(kdst + half * TwSmem::kHalf + r0 * 128, &p.tkp, half * 64, h, row, fbar);
+              tma_load_3d(vdst + half * TwSmem::kHalf + r0 * 128, &p.tvp, half * 64, h, row, fbar);
+            }
+          }
+        } else {
+          const int row = s.k0 + (t - n_pre) * 64;            // rows past the tensor are zero-filled by the copy
+          for (int half = 0; half < 2; ++half) {
+            tma_load_3d(kdst + half * TwSmem::kHalf, &p.tk, half * 64, h, row, fbar);
+            tma_load_3d(vdst + half * TwSmem::kHalf, &p.tv, half * 64, h, row, fbar);
+          }
+        }
+        *issued = t + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp == kTwMmaWarp) {
+    // ------------------------------------------------------------------ MMA issue
+    constexpr uint32_t kIdescQK = umma_idesc_bf16(128, 64, 0, 0);
+    constexpr uint32_t kIdescPV = umma_idesc_bf16(128, kHeadDim, 0, 1);
+    // every wait's outcome is agreed across the warp (__all_sync), so the lanes leave the loop together
+    bool ok = __all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kQFull], 0, abort_flag));
+    if (!ok && lane == 0) tw_fail(a.status, abort_flag);
+    for (int t = 0; ok && t <= ntk; ++t) {
+      if (t < ntk) {
+        const int st = t & 1;
+        if (!__all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kKvFull + st], (t >> 1) & 1, abort_flag))) {
+          if (lane == 0) tw_fail(a.status, abort_flag);
+          ok = false;
+          break;
+        }
+        // a tile's rows past the end of its source (the prefix's last tile: stale page contents; the new keys' last
+        // tile: rows of another sequence or of no sequence) may hold anything, non-finite included: zero their V rows,
+        // whole 128-byte rows, so P = 0 meets V = 0 there
+        const int first = t < n_pre ? s.P - t * 64 : s.Nn - (t - n_pre) * 64;
+        if (first < 64) {
+          uint8_t* vt = smem + TwSmem::kStage0 + st * TwSmem::kStageBytes + TwSmem::kV;
+          for (int i = lane; i < (64 - first) * 16; i += 32) {
+            const int r = first + (i >> 4), half = (i >> 3) & 1, c = i & 7;
+            *reinterpret_cast<uint4*>(vt + half * TwSmem::kHalf + r * 128 + c * 16) = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sq = sbase + TwSmem::kQ, sk = sbase + TwSmem::kStage0 + st * TwSmem::kStageBytes;
+          const uint32_t t_s = tmem + 64u * static_cast<uint32_t>(t & 1);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_bf16(t_s, sw128_desc(sq + (ks >> 2) * 16384 + (ks & 3) * 32, 1024, 16),
+                      sw128_desc(sk + (ks >> 2) * TwSmem::kHalf + (ks & 3) * 32, 1024, 16), kIdescQK, ks > 0 ? 1u : 0u);
+          umma_commit(&bars[TwSmem::kSFull + (t & 1)]);
+        }
+        __syncwarp();
+      }
+      if (t > 0) {
+        const int tp = t - 1, stp = tp & 1;
+        if (!__all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kPFull + (tp & 1)], (tp >> 1) & 1, abort_flag))) {
+          if (lane == 0) tw_fail(a.status, abort_flag);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sp = sbase + TwSmem::kStage0 + stp * TwSmem::kStageBytes;   // P sits in the K slot
+          const uint32_t sv = sp + TwSmem::kV;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16(tmem + kTwOCol, sw128_desc(sp + ks * 32, 1024, 16), sw128_desc(sv + ks * 2048, 1024, TwSmem::kHalf),
+                      kIdescPV, (tp > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&bars[TwSmem::kKvEmpty + stp]);
+          umma_commit(&bars[TwSmem::kPvDone]);
+        }
+        __syncwarp();
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue (warps 0-3)
+    const int row = tid;                                       // TMEM lane = accumulator row
+    const int row_g = row >> 6, row_j = qt * 64 + (row & 63);
+    const bool row_valid = row_j < s.R;
+    const int my_limit = (a.causal && row_valid) ? shift + row_j : L - 1;   // last visible key of this row
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int t = 0; t < ntk; ++t) {
+      const int b = t & 1;
+      ok = tw_wait(&bars[TwSmem::kSFull + b], (t >> 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) tw_fail(a.status, abort_flag);
+        break;
+      }
+      tc_fence_after();
+      float sv[2][32];
+      tmem_ld32(tmem + 64u * b + lane_base, sv[0]);
+      tmem_ld32(tmem + 64u * b + 32u + lane_base, sv[1]);
+      tc_wait_ld();
+      int kbase, kcount;
+      if (t < n_pre) {
+        kbase = t * 64;
+        kcount = min(64, s.P - kbase);
+      } else {
+        const int u = t - n_pre;
+        kbase = s.P + u * 64;
+        kcount = min(64, s.Nn - u * 64);
+      }
+      const int vis_n = min(kcount, my_limit - kbase + 1);     // keys [0, vis_n) of this tile are visible
+      float cm4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (__all_sync(0xffffffffu, vis_n >= 64)) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            sv[u][i] *= a.scale_log2;
+            cm4[i & 3] = fmaxf(cm4[i & 3], sv[u][i]);
+          }
+      } else {
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            sv[u][i] = (u * 32 + i < vis_n) ? sv[u][i] * a.scale_log2 : -INFINITY;
+            cm4[i & 3] = fmaxf(cm4[i & 3], sv[u][i]);
+          }
+      }
+      const float cmax = fmaxf(fmaxf(cm4[0], cm4[1]), fmaxf(cm4[2], cm4[3]));
+      // the running max moves (and O is rescaled) only when it would grow by more than 8 (a factor 256 in P)
+      const bool grow = cmax > m_run + 8.f || (m_run == -INFINITY && cmax > -INFINITY);
+      const float m_new = grow ? cmax : m_run;
+      const float alpha = grow ? exp2f(m_run - m_new) : 1.f;  // 0 on the first visible tile
+      const float mm = m_new == -INFINITY ? 0.f : m_new;
+      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[32];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = ex2_approx(sv[u][i] - mm);
+          const float p1 = ex2_approx(sv[u][i + 1] - mm);
+          ls4[(i >> 1) & 3] += p0 + p1;
+          pk[u * 16 + i / 2] = pack_bf16x2(p0, p1);
+        }
+      l_run = l_run * alpha + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
+      m_run = m_new;
+      // ---- rescale O where a max moved: O must hold P(t-1) V(t-1) first (tile 0 starts O from zero instead)
+      if (t > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        ok = tw_wait(&bars[TwSmem::kPvDone], (t - 1) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) {
+          if (lane == 0) tw_fail(a.status, abort_flag);
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(tmem + kTwOCol + lane_base + c * 32, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(tmem + kTwOCol + lane_base + c * 32, ov);
+        }
+        tc_wait_st();
+      }
+      // ---- P(t) as bf16 into the K slot of stage t & 1 (S(t) is done, so K(t) is dead): 128-byte-swizzled K-major,
+      //      row r at (r / 8) * 1024 + (r % 8) * 128, its 16-byte chunk c at position c ^ (r % 8)
+      uint8_t* prow = smem + TwSmem::kStage0 + b * TwSmem::kStageBytes + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[TwSmem::kPFull + b]);
+    }
+    // ---- epilogue: O / l -> bf16 rows (every thread takes part in the warp-collective TMEM loads)
+    if (ok) {
+      ok = tw_wait(&bars[TwSmem::kPvDone], (ntk - 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && lane == 0) tw_fail(a.status, abort_flag);
+    }
+    if (ok) {
+      tc_fence_after();
+      __nv_bfloat16* dst = a.out + static_cast<long long>(s.q0 + (row_valid ? row_j : 0)) * a.out_stride +
+                           (2 * h + row_g) * kHeadDim;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float ov[32];
+        tmem_ld32(tmem + kTwOCol + lane_base + c * 32, ov);
+        tc_wait_ld();
+        if (row_valid) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack_bf16x2(ov[i] * inv, ov[i + 1] * inv);
+            w.y = pack_bf16x2(ov[i + 2] * inv, ov[i + 3] * inv);
+            w.z = pack_bf16x2(ov[i + 4] * inv, ov[i + 5] * inv);
+            w.w = pack_bf16x2(ov[i + 6] * inv, ov[i + 7] * inv);
+            reinterpret_cast<uint4*>(dst + c * 32 + i)[0] = w;
+          }
+        }
+      }
+    }
+  }
+
+  // ------------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    // a role gave up: let the copies and MMAs already in flight finish (bounded) before TMEM and shared memory go away
+    if (tid == kTwMmaWarp * 32) {
+      umma_commit(&bars[TwSmem::kFinal]);
+      mbar_wait_bounded(&bars[TwSmem::kFinal], 0, 200000000ull);
+    }
+    if (tid == kTwProducerWarp * 32) {
+      mbar_wait_bounded(&bars[TwSmem::kQFull], 0, 200000000ull);
+      const int n = *issued;
+      for (int st = 0; st < 2; ++st) {
+        const int last = (n - 1 - st) >= 0 ? ((n - 1 - st) & ~1) + st : -1;   // last tile issued into stage st
+        if (last >= 0) mbar_wait_bounded(&bars[TwSmem::kKvFull + st], (last >> 1) & 1, 200000000ull);
+      }
+    }
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kTwMmaWarp) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTwTmemCols));
+  }
+}
+
+// ---------------------------------------------------------------- host side
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static const EncodeTiled fn = []() -> EncodeTiled {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiled>(f);
+  }();
+  return fn;
+}
+
+// 3-D map over rows of `heads` x 128 bf16 (heads 256 bytes apart, rows row_bytes apart); box = 64 dims x 1 head x
+// box_rows rows, 128-byte swizzle, zero fill past the last row.
+bool make_rows_map(CUtensorMap* m, const void* base, long long rows, int heads, long long row_bytes, int box_rows) {
+  const EncodeTiled enc = encode_fn();
+  if (!enc || rows <= 0 || rows > (1ll << 31) - 1) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(heads),
+                              static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHeadBytes), static_cast<cuuint64_t>(row_bytes)};
+  const cuuint32_t box[3] = {64u, 1u, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+// The warp-specialised kernel when the call fits it: row counts known, strides in whole 16-byte units, and, with a
+// prefix, page sizes whose boxes tile a 64-key tile (8, 16, 32 or a multiple of 64 tokens). Otherwise *launched stays
+// false and the caller runs prefill_kernel.
+cudaError_t launch_prefill_tma(const PrefillArgs& a, cudaStream_t stream, bool* launched) {
+  *launched = false;
+  if (a.q_rows <= 0 || a.kv_rows <= 0 || (a.q_stride * 2) % 16 || (a.kv_stride * 2) % 16) return cudaSuccess;
+  PfTmaParams p;
+  memset(&p, 0, sizeof(p));
+  p.a = a;
+  if (!make_rows_map(&p.tq, a.q, a.q_rows, kQHeads, a.q_stride * 2, 64) ||
+      !make_rows_map(&p.tk, a.k, a.kv_rows, kKvHeads, a.kv_stride * 2, 64) ||
+      !make_rows_map(&p.tv, a.v, a.kv_rows, kKvHeads, a.kv_stride * 2, 64))
+    return cudaSuccess;
+  if (a.prefix_lens != nullptr) {
+    const int ps = a.page_size;
+    const int box = ps >= 64 ? 64 : ps;
+    if (!(ps % 64 == 0 || ps == 8 || ps == 16 || ps == 32)) return cudaSuccess;
+    const long long rows = static_cast<long long>(a.num_pages) * ps;
+    if (!make_rows_map(&p.tkp, a.k_pool, rows, kKvHeads, kRowBytes, box) ||
+        !make_rows_map(&p.tvp, a.v_pool, rows, kKvHeads, kRowBytes, box))
+      return cudaSuccess;
+    p.box_rows = box;
+  } else {
+    p.box_rows = 64;
+  }
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    e = cudaFuncSetAttribute(prefill_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TwSmem::kAlloc);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const int qtiles = a.max_seqlen_q > 0 ? (a.max_seqlen_q + 63) / 64 : 1;
+  prefill_tma_kernel<<<dim3(qtiles, kKvHeads, a.num_seqs), kTwThreads, TwSmem::kAlloc, stream>>>(p);
+  *launched = true;
+  return cudaGetLastError();
+}
+
+}  // namespace q3

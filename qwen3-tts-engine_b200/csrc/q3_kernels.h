@@ -205,9 +205,11 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);
 struct PrefillArgs {
   const __nv_bfloat16* q;          // [Tq, 16, 128] rows, row stride q_stride (elements)
   long long q_stride;
+  long long q_rows;                // Tq
   const __nv_bfloat16* k;          // [Tk, 8, 128] new key rows, row stride kv_stride
   const __nv_bfloat16* v;
   long long kv_stride;
+  long long kv_rows;               // Tk
   const int32_t* cu_q;             // [num_seqs + 1] query row offsets
   const int32_t* cu_k;             // [num_seqs + 1] new key row offsets (N_i >= R_i)
   int num_seqs;
@@ -230,6 +232,11 @@ struct PrefillArgs {
 };
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
+// The warp-specialised TMA kernel (prefill_tma.cu); *launched = false when the call does not fit it.
+cudaError_t launch_prefill_tma(const PrefillArgs& a, cudaStream_t stream, bool* launched);
+// Which prefill kernel q3_prefill uses: 0 = the warp-specialised TMA kernel where the call fits it (default), 1 = the
+// single-warpgroup kernel always.
+extern int g_prefill_kernel;
 
 // Host-side helpers of capi.cu shared with the allocation-free decode entry (decode_noalloc.cu).
 int record_cuda_error(cudaError_t e);   // keeps the error text for q3_last_cuda_error(); returns Q3_ERR_CUDA

@@ -47,7 +47,8 @@ SIGNATURES = {
                                            _I32, _I32, _I32, _I32, _F32, _P, _I64, _P, _SZ, _I32, _P]),
     "q3_set_decode_variant": (ctypes.c_int, [ctypes.c_int]),
     "q3_paged_decode_resident_ctas": (ctypes.c_int, [ctypes.c_int]),
-    "q3_prefill": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P, _I32, _I32, _P, _P, _P, _P, _I32, _I32, _P, _I64,
+    "q3_set_prefill_kernel": (ctypes.c_int, [ctypes.c_int]),
+    "q3_prefill": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _I32, _I32, _P, _P, _P, _P, _I32, _I32, _P, _I64,
                                   _I32, _I32, _I32, _I32, _I32, _I32, _F32, _P, _I64, _P]),
     "q3_kv_append_slots": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _I32, _I32, _P, _I32, _P]),
     "q3_kv_append_paged": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _I64, _I32,

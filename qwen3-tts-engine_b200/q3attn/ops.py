@@ -579,7 +579,8 @@ def _prefill_impl(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_sca
         return out
     with torch.cuda.device(q.device):
         rc = lib.q3_prefill(
-            q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k.stride(0), cu_seqlens_q.data_ptr(),
+            q.data_ptr(), q.stride(0), q.shape[0], k.data_ptr(), v.data_ptr(), k.stride(0), k.shape[0],
+            cu_seqlens_q.data_ptr(),
             cu_seqlens_k.data_ptr(), n, int(max_seqlen_q), _ptr(pl), _ptr(si),
             _ptr(k_cache) if paged else None, _ptr(v_cache) if paged else None,
             k_cache.shape[0] if paged else 0, k_cache.shape[1] if paged else 0,
@@ -618,6 +619,12 @@ def prefill_paged(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: to
 def _(q, k, v, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, prefix_lens, seat_ids, block_table,
       softmax_scale, causal=True, write_kv=True):
     return q.new_empty(q.shape[0], NH, HD)
+
+
+def set_prefill_kernel(kernel: int) -> int:
+    """Select the prefill kernel (0: the warp-specialised TMA kernel where the call fits it, else the single-warpgroup
+    kernel; 1: the single-warpgroup kernel always). Returns the previous selection."""
+    return int(_lib.load().q3_set_prefill_kernel(int(kernel)))
 
 
 def set_decode_variant(variant: int) -> int:

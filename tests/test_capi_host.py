@@ -223,13 +223,15 @@ def test_prefix_copy_rejects_bad_arguments_before_cuda():
 
 def test_prefill_rejects_bad_arguments_before_cuda():
     lib = _lib.load()
-    base = dict(q=16, qs=2048, k=16, v=16, kvs=1024, cuq=64, cuk=64, ns=2, mq=320, pl=None, seat=None, kp=32, vp=48,
-                npg=100, page=16, bt=128, bts=20, maxp=20, wkv=0, causal=1, nh=16, nkv=8, hd=128, out=16, os_=2048)
+    base = dict(q=16, qs=2048, qr=640, k=16, v=16, kvs=1024, kvr=640, cuq=64, cuk=64, ns=2, mq=320, pl=None, seat=None,
+                kp=32, vp=48, npg=100, page=16, bt=128, bts=20, maxp=20, wkv=0, causal=1, nh=16, nkv=8, hd=128, out=16,
+                os_=2048)
 
     def call(**kw):
         a = dict(base)
         a.update(kw)
-        return lib.q3_prefill(a["q"], a["qs"], a["k"], a["v"], a["kvs"], a["cuq"], a["cuk"], a["ns"], a["mq"], a["pl"],
+        return lib.q3_prefill(a["q"], a["qs"], a["qr"], a["k"], a["v"], a["kvs"], a["kvr"], a["cuq"], a["cuk"], a["ns"],
+                              a["mq"], a["pl"],
                               a["seat"], a["kp"], a["vp"], a["npg"], a["page"], a["bt"], a["bts"], a["maxp"], a["wkv"],
                               a["causal"], a["nh"], a["nkv"], a["hd"], 0.088, a["out"], a["os_"], None)
     assert call(nh=32) == _lib.Q3_ERR_UNSUPPORTED                               # the model family: 16 / 8 x 128
@@ -240,6 +242,9 @@ def test_prefill_rejects_bad_arguments_before_cuda():
     assert call(wkv=1, bts=10) == _lib.Q3_ERR_INVALID                           # table stride < pages per seat
     assert call(q=24) == _lib.Q3_ERR_ALIGNMENT
     assert call(ns=70000) == _lib.Q3_ERR_INVALID                                # beyond the grid's z extent
+    assert call(qr=-1) == _lib.Q3_ERR_INVALID                                   # negative row counts
+    assert call(kvr=-5) == _lib.Q3_ERR_INVALID
+    assert call(qr=0) == _lib.Q3_OK                                             # no query rows: nothing to do
     assert call(ns=0) == _lib.Q3_OK
 
 

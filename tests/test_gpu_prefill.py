@@ -22,6 +22,15 @@ def q3():
     return q3attn
 
 
+@pytest.fixture(params=[0, 1], ids=["tma", "single"], autouse=True)
+def prefill_kernel(q3, request):
+    """Every test runs on both prefill kernels: the warp-specialised TMA kernel (default) and the single-warpgroup one
+    (used for calls the TMA kernel does not fit)."""
+    prev = q3.set_prefill_kernel(request.param)
+    yield request.param
+    q3.set_prefill_kernel(prev)
+
+
 def _check_status(q3):
     torch.cuda.synchronize()
     assert q3._lib.read_status() == 0
@@ -73,7 +82,7 @@ def test_flash_attn_func_bottom_right_against_reference(q3, golden_dir, name):
     assert_close_attn(out, ref, what=f"oracle {name}")
 
 
-@pytest.mark.parametrize("page", [16, 256])
+@pytest.mark.parametrize("page", [8, 16, 32, 48, 256])
 def test_paged_chunk_prefill_writes_pages_and_attends_over_prefix(q3, page):
     """Chunked prefill: sequence i has prefix_lens[i] tokens cached in its pages; its new rows are written at
     prefix_lens[i].. (bit-exact placement) and its queries attend over prefix + new (bottom-right causal)."""
@@ -124,3 +133,40 @@ def test_c3_ten_prompts_of_320_tokens_into_fresh_pages(q3):
         got = OA.gather_seat(kp.cpu(), lay.block_table[s], L).to(torch.bfloat16)
         assert bits_equal(got, d["k"][i * L:(i + 1) * L]), f"seat {s} pages"
     assert pps * 16 >= L
+
+
+@pytest.mark.parametrize("page", [16, 256])
+def test_stale_non_finite_rows_never_reach_the_output(q3, page):
+    """Page rows past each sequence's prefix and packed K/V rows that belong to no sequence hold NaN / inf: the
+    attention reads whole tiles, but such rows get zero weight and must not leak (0 * NaN) into any output."""
+    g = synth.cpu_gen(5 + page)
+    seats, pps = 3, 512 // page
+    n_pages = seats * pps
+    bt = torch.randperm(n_pages, generator=g).view(seats, pps).to(torch.int32)
+    kp = synth.randn((n_pages, page, 8, 128), g, 0.5, torch.bfloat16)
+    vp = synth.randn((n_pages, page, 8, 128), g, 0.5, torch.bfloat16)
+    prefix = torch.tensor([35, 100, 1], dtype=torch.int32)
+    seat_ids = torch.tensor([2, 0, 1], dtype=torch.int32)
+    for s_, P in zip(seat_ids.tolist(), prefix.tolist()):    # everything past the prefix in the seat's pages: NaN / inf
+        pos = torch.arange(P, pps * page)
+        rows = bt[s_, pos // page].long() * page + pos % page
+        kp.view(-1, 8, 128)[rows] = float("nan")
+        vp.view(-1, 8, 128)[rows] = float("inf")
+    lens = [42, 20, 70]
+    d = synth.prefill_case(13, lens, scale=0.5)
+    pad = 40                                                  # packed rows after the last sequence: NaN
+    k = torch.cat([d["k"], torch.full((pad, 8, 128), float("nan"), dtype=torch.bfloat16)])
+    v = torch.cat([d["v"], torch.full((pad, 8, 128), float("nan"), dtype=torch.bfloat16)])
+    out = q3.prefill_paged(d["q"].to(DEV), k.to(DEV), v.to(DEV), kp.to(DEV), vp.to(DEV), d["cu_seqlens"].to(DEV),
+                           d["cu_seqlens"].to(DEV), max(lens), prefix.to(DEV), seat_ids.to(DEV), bt.to(DEV), SCALE, True,
+                           False)
+    _check_status(q3)
+    assert torch.isfinite(out.float()).all()
+    ref = torch.zeros(sum(lens), 16, 128)
+    for i in range(len(lens)):
+        a, b = int(d["cu_seqlens"][i]), int(d["cu_seqlens"][i + 1])
+        P = int(prefix[i])
+        K = torch.cat([OA.gather_seat(kp, bt[int(seat_ids[i])], P), d["k"][a:b].float()])
+        V = torch.cat([OA.gather_seat(vp, bt[int(seat_ids[i])], P), d["v"][a:b].float()])
+        ref[a:b] = OA.prefill_prefix(d["q"][a:b][None], K[None], V[None], SCALE)[0]
+    assert_close_attn(out, ref, what=f"stale rows, page {page}")
