@@ -321,10 +321,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     cudaError_t e = launch_prefill_tma(a, stream, &launched);
     if (e != cudaSuccess) return e;
   }
-  if (launched) {
-    if (a.write_kv) prefill_page_write_kernel<<<dim3(16, a.num_seqs), 256, 0, stream>>>(a);
-    return cudaGetLastError();
-  }
+  if (launched) return cudaSuccess;                          // the TMA kernel does the page writes itself
   static thread_local int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);

@@ -15,7 +15,9 @@
 //   warps 0-3 (softmax) thread r owns TMEM lane r = accumulator row r: reads S(t) (tcgen05.ld), online softmax in the
 //                       exp2 domain with a lazy running max (O rescaled in TMEM only when a max grows by more than 2^8),
 //                       writes P(t) as bf16 into the K slot of its stage (K(t) is dead once S(t) is done), and at the
-//                       end divides O by the row sums and stores the output rows.
+//                       end divides O by the row sums and stores the output rows. With write_kv they first copy their
+//                       query tile's share of the new K/V rows into the pages (head h; the last query tile also takes
+//                       any new rows past the queries), while the first copies and S(0) are in flight.
 // While the softmax warps work on S(t), the tensor core computes S(t+1) and P(t-1) V(t-1), and the producer loads tile
 // t+2 into the stage P.V(t) frees. Shared memory: Q 32 KB + 2 stages x (K 16 KB + V 16 KB) = 96 KB, TMEM 256 columns
 // (S0, S1, O): two CTAs per SM. Every mbarrier wait is bounded (2 s); a timed-out role raises the status bit and an
@@ -42,8 +44,11 @@ struct TwSmem {
   static constexpr int kHalf = 8192;          // one dim half of a K or V tile
   static constexpr int kV = 16384;            // V within a stage
   static constexpr int kBars = kStage0 + 2 * kStageBytes;
-  static constexpr int kQFull = 0, kKvFull = 1, kKvEmpty = 3, kSFull = 5, kPFull = 7, kPvDone = 9, kFinal = 10;
-  static constexpr int kNumBars = 11;
+  // Barriers, every one waited with a parity that is never ambiguous: a waiter is at most one phase away from its
+  // barrier's next completion. S, P and P.V alternate between two barriers each so that no role can run two phases
+  // ahead of the role that waits (P.V in particular: the softmax warps wait for it only now and then).
+  static constexpr int kQFull = 0, kKvFull = 1, kKvEmpty = 3, kSFull = 5, kPFull = 7, kPvDone = 9, kFinal = 11;
+  static constexpr int kNumBars = 12;
   static constexpr int kTmemSlot = kBars + 8 * kNumBars;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kIssued = kAbort + 4;  // K/V tiles the producer has issued (read on the abort path)
@@ -103,6 +108,35 @@ __device__ __forceinline__ void tw_fail(uint32_t* status, volatile int* abort_fl
   *abort_flag = 1;
 }
 
+// The page writes of a chunked prefill (write_kv) for KV head h: new rows [r0, r1) of the sequence go to positions
+// P + r of its seat's pages, K and V (256 bytes each per row and head), by 128 threads with 16-byte accesses, eight loads
+// in flight before their stores. The attention reads new keys from the input rows and only the prefix from the pages,
+// so these writes never race with its reads of valid keys.
+__device__ __forceinline__ void write_new_rows(const PrefillArgs& a, const PfSeq& s, int h, int r0, int r1, int tid) {
+  const int n = (r1 - r0) * 32;                               // 16-byte pieces: 16 per row for K and 16 for V
+#pragma unroll 1
+  for (int base = 0; base < n; base += 8 * 128) {
+    uint4 v[8];
+    uint4* dst[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * 128 + tid;
+      dst[u] = nullptr;
+      if (i < n) {
+        const int r = r0 + (i >> 5), which = (i >> 4) & 1, c = i & 15;
+        const __nv_bfloat16* src = (which ? a.v : a.k) + static_cast<long long>(s.k0 + r) * a.kv_stride + h * kHeadDim;
+        v[u] = __ldg(reinterpret_cast<const uint4*>(src) + c);
+        __nv_bfloat16* pool = which ? a.v_pool : a.k_pool;
+        dst[u] = reinterpret_cast<uint4*>(pool + pf_pool_row(a, s.seat, s.P + r) * (kKvHeads * kHeadDim) +
+                                          h * kHeadDim) + c;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (dst[u] != nullptr) *dst[u] = v[u];
+  }
+}
+
 __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid_constant__ PfTmaParams p) {
   const PrefillArgs& a = p.a;
   extern __shared__ uint8_t tw_raw[];
@@ -110,7 +144,10 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.y;
   const PfSeq s = pf_seq(a, blockIdx.z);
-  if (s.R <= 0) return;
+  if (s.R <= 0) {                                             // no queries: CTA 0 still writes the new rows (write_kv)
+    if (a.write_kv && blockIdx.x == 0 && tid < 128) write_new_rows(a, s, h, 0, s.Nn, tid);
+    return;
+  }
   const int ntq = (s.R + 63) / 64;
   const int qt = ntq - 1 - static_cast<int>(blockIdx.x);     // heavy (late) query tiles take the low block indices
   if (qt < 0) return;                                         // uniform per CTA; nothing allocated yet
@@ -144,6 +181,7 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
       mbar_init(&bars[TwSmem::kPFull + i], 4);               // one arrival per softmax warp
     }
     mbar_init(&bars[TwSmem::kPvDone], 1);
+    mbar_init(&bars[TwSmem::kPvDone + 1], 1);
     mbar_init(&bars[TwSmem::kFinal], 1);
     *abort_flag = 0;
     *issued = 0;
@@ -252,7 +290,7 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
             umma_bf16(tmem + kTwOCol, sw128_desc(sp + ks * 32, 1024, 16), sw128_desc(sv + ks * 2048, 1024, TwSmem::kHalf),
                       kIdescPV, (tp > 0 || ks > 0) ? 1u : 0u);
           umma_commit(&bars[TwSmem::kKvEmpty + stp]);
-          umma_commit(&bars[TwSmem::kPvDone]);
+          umma_commit(&bars[TwSmem::kPvDone + (tp & 1)]);
         }
         __syncwarp();
       }
@@ -264,6 +302,8 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
     const bool row_valid = row_j < s.R;
     const int my_limit = (a.causal && row_valid) ? shift + row_j : L - 1;   // last visible key of this row
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    if (a.write_kv)   // this query tile's share of the page writes, while the first copies and S(0) are in flight
+      write_new_rows(a, s, h, min(qt * 64, s.Nn), qt == ntq - 1 ? s.Nn : min(qt * 64 + 64, s.Nn), tid);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int t = 0; t < ntk; ++t) {
@@ -289,46 +329,48 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
         kcount = min(64, s.Nn - u * 64);
       }
       const int vis_n = min(kcount, my_limit - kbase + 1);     // keys [0, vis_n) of this tile are visible
+      // raw maxima (the scale is positive, so it is applied once to the maximum), masked keys set to -inf
       float cm4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (__all_sync(0xffffffffu, vis_n >= 64)) {
 #pragma unroll
         for (int u = 0; u < 2; ++u)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            sv[u][i] *= a.scale_log2;
-            cm4[i & 3] = fmaxf(cm4[i & 3], sv[u][i]);
-          }
+          for (int i = 0; i < 32; ++i) cm4[i & 3] = fmaxf(cm4[i & 3], sv[u][i]);
       } else {
 #pragma unroll
         for (int u = 0; u < 2; ++u)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            sv[u][i] = (u * 32 + i < vis_n) ? sv[u][i] * a.scale_log2 : -INFINITY;
+            sv[u][i] = (u * 32 + i < vis_n) ? sv[u][i] : -INFINITY;
             cm4[i & 3] = fmaxf(cm4[i & 3], sv[u][i]);
           }
       }
-      const float cmax = fmaxf(fmaxf(cm4[0], cm4[1]), fmaxf(cm4[2], cm4[3]));
+      const float cmax = fmaxf(fmaxf(cm4[0], cm4[1]), fmaxf(cm4[2], cm4[3])) * a.scale_log2;
       // the running max moves (and O is rescaled) only when it would grow by more than 8 (a factor 256 in P)
       const bool grow = cmax > m_run + 8.f || (m_run == -INFINITY && cmax > -INFINITY);
       const float m_new = grow ? cmax : m_run;
       const float alpha = grow ? exp2f(m_run - m_new) : 1.f;  // 0 on the first visible tile
       const float mm = m_new == -INFINITY ? 0.f : m_new;
-      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+      // p = 2^(s * scale - m) by packed FMAs into the approximate exp2; row sums by packed adds in 4 chains
+      const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-mm, -mm);
+      float2 ls2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       uint32_t pk[32];
 #pragma unroll
       for (int u = 0; u < 2; ++u)
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float p0 = ex2_approx(sv[u][i] - mm);
-          const float p1 = ex2_approx(sv[u][i + 1] - mm);
-          ls4[(i >> 1) & 3] += p0 + p1;
-          pk[u * 16 + i / 2] = pack_bf16x2(p0, p1);
+          const float2 x = __ffma2_rn(make_float2(sv[u][i], sv[u][i + 1]), sc2, nm2);
+          const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          ls2[(i >> 1) & 3] = __fadd2_rn(ls2[(i >> 1) & 3], pp);
+          pk[u * 16 + i / 2] = pack_bf16x2(pp.x, pp.y);
         }
-      l_run = l_run * alpha + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
+      const float2 lsa = __fadd2_rn(__fadd2_rn(ls2[0], ls2[1]), __fadd2_rn(ls2[2], ls2[3]));
+      l_run = l_run * alpha + (lsa.x + lsa.y);
       m_run = m_new;
-      // ---- rescale O where a max moved: O must hold P(t-1) V(t-1) first (tile 0 starts O from zero instead)
+      // ---- rescale O where a max moved: O must hold P(t-1) V(t-1) first (tile 0 starts O from zero instead). The
+      //      barrier of P.V(t-1) last completed for P.V(t-3), which S(t) (issued after P.V(t-2)) has seen finish.
       if (t > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        ok = tw_wait(&bars[TwSmem::kPvDone], (t - 1) & 1, abort_flag);
+        ok = tw_wait(&bars[TwSmem::kPvDone + ((t - 1) & 1)], ((t - 1) >> 1) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) {
           if (lane == 0) tw_fail(a.status, abort_flag);
@@ -360,7 +402,7 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
     }
     // ---- epilogue: O / l -> bf16 rows (every thread takes part in the warp-collective TMEM loads)
     if (ok) {
-      ok = tw_wait(&bars[TwSmem::kPvDone], (ntk - 1) & 1, abort_flag);
+      ok = tw_wait(&bars[TwSmem::kPvDone + ((ntk - 1) & 1)], ((ntk - 1) >> 1) & 1, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok && lane == 0) tw_fail(a.status, abort_flag);
     }
@@ -448,12 +490,13 @@ bool make_rows_map(CUtensorMap* m, const void* base, long long rows, int heads, 
 
 }  // namespace
 
-// The warp-specialised kernel when the call fits it: row counts known, strides in whole 16-byte units, and, with a
-// prefix, page sizes whose boxes tile a 64-key tile (8, 16, 32 or a multiple of 64 tokens). Otherwise *launched stays
+// The warp-specialised kernel when the call fits it: row counts known, strides in whole 16-byte units, a positive
+// softmax scale, and, with a prefix, page sizes whose boxes tile a 64-key tile (8, 16, 32 or a multiple of 64 tokens). Otherwise *launched stays
 // false and the caller runs prefill_kernel.
 cudaError_t launch_prefill_tma(const PrefillArgs& a, cudaStream_t stream, bool* launched) {
   *launched = false;
-  if (a.q_rows <= 0 || a.kv_rows <= 0 || (a.q_stride * 2) % 16 || (a.kv_stride * 2) % 16) return cudaSuccess;
+  if (a.q_rows <= 0 || a.kv_rows <= 0 || (a.q_stride * 2) % 16 || (a.kv_stride * 2) % 16 || !(a.scale_log2 > 0.f))
+    return cudaSuccess;
   PfTmaParams p;
   memset(&p, 0, sizeof(p));
   p.a = a;
