@@ -7,21 +7,25 @@
 // One CTA = (64-position query tile, KV head h, sequence); its 128 accumulator rows are the 64 positions of q heads 2h
 // and 2h+1, which share every K/V tile. Six warps with fixed roles:
 //   warp 4 (producer)   lane 0 issues TMA tensor copies (cp.async.bulk.tensor, no multicast, this GPU's memory only):
-//                       the Q tile once, then K and V tiles of 64 keys into a 2-stage ring, 128-byte swizzled so they
-//                       are UMMA operands as they land. Prefix keys come page by page out of the pool, new keys as one
-//                       box per 64 rows.
-//   warp 5 (MMA)        lane 0 issues S(t) = Q K(t)^T into one of two TMEM S buffers, then O += P(t-1) V(t-1) into
-//                       the TMEM O accumulator; tcgen05.commit arrives on mbarriers (S ready; K/V stage free; P.V done).
+//                       the Q tile once, then K and V tiles of 64 keys into two 2-slot rings, 128-byte swizzled so they
+//                       are UMMA operands as they land; K(t+2) goes out as soon as S(t) has read K(t), V(t+2) once
+//                       P(t) V(t) is done. Prefix keys come page by page out of the pool, new keys as one box per 64
+//                       rows. With write_kv it also stores the new K/V tiles this CTA owns into the pages (TMA tensor
+//                       stores from the same shared-memory tiles, page-aligned boxes).
+//   warp 5 (MMA)        lane 0 issues S(t) = Q K(t)^T into one of two TMEM S buffers and O += P(t) V(t) into the TMEM
+//                       O accumulator, each as soon as its inputs are ready (S(t+1) may go before or after P(t) V(t));
+//                       tcgen05.commit arrives on mbarriers (K slot free + S ready; V slot free + P.V done).
 //   warps 0-3 (softmax) thread r owns TMEM lane r = accumulator row r: reads S(t) (tcgen05.ld), online softmax in the
 //                       exp2 domain with a lazy running max (O rescaled in TMEM only when a max grows by more than 2^8),
-//                       writes P(t) as bf16 into the K slot of its stage (K(t) is dead once S(t) is done), and at the
-//                       end divides O by the row sums and stores the output rows. With write_kv they first copy their
-//                       query tile's share of the new K/V rows into the pages (head h; the last query tile also takes
-//                       any new rows past the queries), while the first copies and S(0) are in flight.
-// While the softmax warps work on S(t), the tensor core computes S(t+1) and P(t-1) V(t-1), and the producer loads tile
-// t+2 into the stage P.V(t) frees. Shared memory: Q 32 KB + 2 stages x (K 16 KB + V 16 KB) = 96 KB, TMEM 256 columns
-// (S0, S1, O): two CTAs per SM. Every mbarrier wait is bounded (2 s); a timed-out role raises the status bit and an
-// abort flag the other roles poll, in-flight copies and MMAs are waited for (bounded), and TMEM is always freed.
+//                       writes P(t) as bf16 into the P buffer once P(t-1) V(t-1) is done, and at the end divides O by
+//                       the row sums and stores the output rows. Page-write rows that do not fill a page-aligned box
+//                       (a prefix not aligned to the box, a last partial box) are copied by these threads at the start.
+// While the softmax warps work on S(t), the tensor core computes S(t+1) and P(t-1) V(t-1), and the producer loads the
+// next tiles. Shared memory: Q 32 KB + K 2 x 16 KB + V 2 x 16 KB + P 16 KB = 112 KB, TMEM 256 columns (S0, S1, O): two
+// CTAs per SM (the 112 KB leave no room for alignment slack: the kernel checks that its shared memory starts on a
+// 1024-byte boundary and otherwise raises a status bit and returns). Every mbarrier wait is bounded (2 s); a timed-out
+// role raises the status bit and an abort flag the other roles poll, in-flight copies and MMAs are waited for
+// (bounded), and TMEM is always freed.
 #include <cuda.h>
 
 #include <cstring>
@@ -39,21 +43,23 @@ constexpr uint32_t kTwOCol = 128;             // S(t) at column 64 * (t & 1), O 
 
 struct TwSmem {
   static constexpr int kQ = 0;                // [2 dim halves][128 rows][128 B]: 32 KB, SW128 K-major
-  static constexpr int kStage0 = 32768;       // stage s: K [2 halves][64 keys][128 B], then V the same (32 KB)
-  static constexpr int kStageBytes = 32768;
+  static constexpr int kK = 32768;            // K slot s at kK + s * kTile: [2 dim halves][64 keys][128 B]
+  static constexpr int kV = 65536;            // V slot s at kV + s * kTile: same layout (MN-major B operand)
+  static constexpr int kTile = 16384;
   static constexpr int kHalf = 8192;          // one dim half of a K or V tile
-  static constexpr int kV = 16384;            // V within a stage
-  static constexpr int kBars = kStage0 + 2 * kStageBytes;
+  static constexpr int kP = 98304;            // P [128 rows][64 keys] bf16, SW128 K-major (16 KB)
+  static constexpr int kBars = kP + 16384;
   // Barriers, every one waited with a parity that is never ambiguous: a waiter is at most one phase away from its
-  // barrier's next completion. S, P and P.V alternate between two barriers each so that no role can run two phases
-  // ahead of the role that waits (P.V in particular: the softmax warps wait for it only now and then).
-  static constexpr int kQFull = 0, kKvFull = 1, kKvEmpty = 3, kSFull = 5, kPFull = 7, kPvDone = 9, kFinal = 11;
-  static constexpr int kNumBars = 12;
+  // barrier's next completion (each role waits for every phase of the barriers it waits on, in order, and no role can
+  // complete a barrier twice before its waiter has seen the first completion).
+  static constexpr int kQFull = 0, kKFull = 1, kVFull = 3, kKEmpty = 5, kVEmpty = 7, kSFull = 9, kPFull = 11,
+                       kPvDone = 13, kFinal = 15;
+  static constexpr int kNumBars = 16;
   static constexpr int kTmemSlot = kBars + 8 * kNumBars;
   static constexpr int kAbort = kTmemSlot + 4;
-  static constexpr int kIssued = kAbort + 4;  // K/V tiles the producer has issued (read on the abort path)
-  static constexpr int kBytes = kIssued + 4;
-  static constexpr int kAlloc = kBytes + 1024;   // + slack to align the base to 1024 B (128-byte swizzle atoms)
+  static constexpr int kIssuedK = kAbort + 4;  // K and V tiles the producer has issued (read on the abort path)
+  static constexpr int kIssuedV = kIssuedK + 4;
+  static constexpr int kBytes = kIssuedV + 4;
 };
 
 struct PfTmaParams {
@@ -61,9 +67,10 @@ struct PfTmaParams {
   CUtensorMap tq;    // q rows    [q_rows][16 heads][128]
   CUtensorMap tk;    // new keys  [kv_rows][8 heads][128]
   CUtensorMap tv;
-  CUtensorMap tkp;   // pools     [num_pages * page_size][8 heads][128] (used when a prefix is given)
+  CUtensorMap tkp;   // pools     [num_pages * page_size][8 heads][128] (prefix reads, page-write stores)
   CUtensorMap tvp;
   int box_rows;      // rows per pool box: min(page_size, 64)
+  int pool_maps;     // tkp / tvp are valid
 };
 
 // UMMA shared-memory descriptor of a 128-byte-swizzled operand: 8-row groups `sbo` bytes apart; `lbo` = the distance
@@ -87,6 +94,39 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
 
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Shared -> global tensor store (a page-aligned box of new K or V rows into the pool), in this thread's bulk group.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// This thread's bulk stores have finished reading shared memory (the slot may be refilled).
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// This thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Non-blocking test of phase `parity` of `bar`.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Number of new-key tiles the query tile q of a sequence visits (the key tiles past the prefix).
+__device__ __forceinline__ int new_tiles_of(const PfSeq& s, int q, int causal) {
+  const int L = s.P + s.Nn, shift = L - s.R;
+  const int key_end = causal ? min(L, shift + min(s.R - 1, q * 64 + 63) + 1) : L;
+  return (max(key_end - s.P, 0) + 63) / 64;
 }
 
 // Wait for phase `parity` of `bar`; false after 2 s or once another role has raised the abort flag.
@@ -139,8 +179,7 @@ __device__ __forceinline__ void write_new_rows(const PrefillArgs& a, const PfSeq
 
 __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid_constant__ PfTmaParams p) {
   const PrefillArgs& a = p.a;
-  extern __shared__ uint8_t tw_raw[];
-  uint8_t* smem = tw_raw + ((1024u - (smem_addr(tw_raw) & 1023u)) & 1023u);
+  extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.y;
   const PfSeq s = pf_seq(a, blockIdx.z);
@@ -151,6 +190,10 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
   const int ntq = (s.R + 63) / 64;
   const int qt = ntq - 1 - static_cast<int>(blockIdx.x);     // heavy (late) query tiles take the low block indices
   if (qt < 0) return;                                         // uniform per CTA; nothing allocated yet
+  if (smem_addr(smem) & 1023u) {                              // the swizzled tiles need 1024-byte aligned atoms
+    if (tid == 0) atomicOr(a.status, kStatusSmemAlign);
+    return;
+  }
 
   // ---- key tiles: the prefix keys [0, P) in tiles of 64, then the new keys [0, N) in tiles of 64 (combined index
   //      P + j), each tile from one source; only the keys some row of this query tile can see are visited
@@ -161,10 +204,19 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
   const int n_new = (max(key_end - s.P, 0) + 63) / 64;
   const int ntk = n_pre + n_new;                              // >= 1: key 0 is visible to every row
 
+  // ---- page writes (write_kv): this CTA owns new-key tiles [u_lo, n_new), the ones the previous query tile does not
+  //      visit (a partition of all new tiles over the query tiles). Rows in whole page-aligned boxes go out by TMA
+  //      stores from the loaded tiles; the rest (misaligned prefix, last partial box) by the softmax threads.
+  const int u_lo = qt > 0 ? new_tiles_of(s, qt - 1, a.causal) : 0;
+  const bool tma_store = a.write_kv && p.pool_maps && (s.P % p.box_rows) == 0;
+  const int box_end = tma_store ? (s.Nn / p.box_rows) * p.box_rows : 64 * u_lo;   // rows [64 u_lo, box_end): TMA
+  const int own_end = min(s.Nn, 64 * n_new);                                        // rows [64 u_lo, own_end) owned
+
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TwSmem::kBars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TwSmem::kTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TwSmem::kAbort);
-  volatile int* issued = reinterpret_cast<volatile int*>(smem + TwSmem::kIssued);
+  volatile int* issued_k = reinterpret_cast<volatile int*>(smem + TwSmem::kIssuedK);
+  volatile int* issued_v = reinterpret_cast<volatile int*>(smem + TwSmem::kIssuedV);
   const uint32_t sbase = smem_addr(smem);
 
   if (warp == kTwMmaWarp) {   // TMEM: 256 columns; shared memory limits an SM to two CTAs, so 512 columns suffice
@@ -175,16 +227,18 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
   if (tid == kTwProducerWarp * 32) {
     mbar_init(&bars[TwSmem::kQFull], 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[TwSmem::kKvFull + i], 1);
-      mbar_init(&bars[TwSmem::kKvEmpty + i], 1);
+      mbar_init(&bars[TwSmem::kKFull + i], 1);
+      mbar_init(&bars[TwSmem::kVFull + i], 1);
+      mbar_init(&bars[TwSmem::kKEmpty + i], 1);
+      mbar_init(&bars[TwSmem::kVEmpty + i], 1);
       mbar_init(&bars[TwSmem::kSFull + i], 1);
       mbar_init(&bars[TwSmem::kPFull + i], 4);               // one arrival per softmax warp
+      mbar_init(&bars[TwSmem::kPvDone + i], 1);
     }
-    mbar_init(&bars[TwSmem::kPvDone], 1);
-    mbar_init(&bars[TwSmem::kPvDone + 1], 1);
     mbar_init(&bars[TwSmem::kFinal], 1);
     *abort_flag = 0;
-    *issued = 0;
+    *issued_k = 0;
+    *issued_v = 0;
     fence_mbar_init();
   }
   tc_fence_before();
@@ -193,7 +247,7 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
   const uint32_t tmem = *tmem_slot;
 
   if (warp == kTwProducerWarp) {
-    // ------------------------------------------------------------------ producer: TMA copies
+    // ------------------------------------------------------------------ producer: TMA copies and page stores
     if (lane == 0) {
       prefetch_map(&p.tq);
       prefetch_map(&p.tk);
@@ -203,58 +257,110 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
       for (int g = 0; g < 2; ++g)
         for (int half = 0; half < 2; ++half)
           tma_load_3d(sbase + TwSmem::kQ + half * 16384 + g * 8192, &p.tq, half * 64, 2 * h + g, s.q0 + qt * 64, qbar);
-      for (int t = 0; t < ntk; ++t) {
+      // one K or V tile of key tile t into slot t & 1
+      auto load_tile = [&](int t, bool is_v) {
         const int st = t & 1;
-        if (t >= 2 && !tw_wait(&bars[TwSmem::kKvEmpty + st], ((t >> 1) - 1) & 1, abort_flag)) {
-          tw_fail(a.status, abort_flag);
-          break;
-        }
-        uint64_t* fb = &bars[TwSmem::kKvFull + st];
+        uint64_t* fb = &bars[(is_v ? TwSmem::kVFull : TwSmem::kKFull) + st];
         const uint32_t fbar = smem_addr(fb);
-        mbar_arrive_expect_tx(fb, 32768u);
-        const uint32_t kdst = sbase + TwSmem::kStage0 + st * TwSmem::kStageBytes, vdst = kdst + TwSmem::kV;
+        const uint32_t dst = sbase + (is_v ? TwSmem::kV : TwSmem::kK) + st * TwSmem::kTile;
+        mbar_arrive_expect_tx(fb, static_cast<uint32_t>(TwSmem::kTile));
         if (t < n_pre) {
+          const CUtensorMap* m = is_v ? &p.tvp : &p.tkp;
           for (int r0 = 0; r0 < 64; r0 += p.box_rows) {
             const int tok = t * 64 + r0;
             // rows past the prefix in its last tile: any valid pool row (their V rows are zeroed before P.V)
             const int row = tok < s.P ? static_cast<int>(pf_pool_row(a, s.seat, tok)) : 0;
-            for (int half = 0; half < 2; ++half) {
-              tma_load_3d(kdst + half * TwSmem::kHalf + r0 * 128, &p.tkp, half * 64, h, row, fbar);
-              tma_load_3d(vdst + half * TwSmem::kHalf + r0 * 128, &p.tvp, half * 64, h, row, fbar);
-            }
+            for (int half = 0; half < 2; ++half) tma_load_3d(dst + half * TwSmem::kHalf + r0 * 128, m, half * 64, h, row, fbar);
           }
         } else {
           const int row = s.k0 + (t - n_pre) * 64;            // rows past the tensor are zero-filled by the copy
-          for (int half = 0; half < 2; ++half) {
-            tma_load_3d(kdst + half * TwSmem::kHalf, &p.tk, half * 64, h, row, fbar);
-            tma_load_3d(vdst + half * TwSmem::kHalf, &p.tv, half * 64, h, row, fbar);
-          }
+          const CUtensorMap* m = is_v ? &p.tv : &p.tk;
+          for (int half = 0; half < 2; ++half) tma_load_3d(dst + half * TwSmem::kHalf, m, half * 64, h, row, fbar);
         }
-        *issued = t + 1;
+      };
+      // the page stores of key tile t (a new-key tile this CTA owns), from slot t & 1: whole boxes below box_end
+      auto store_tile = [&](int t, bool is_v) {
+        const int u = t - n_pre;
+        if (!tma_store || u < u_lo) return;
+        const uint32_t src = sbase + (is_v ? TwSmem::kV : TwSmem::kK) + (t & 1) * TwSmem::kTile;
+        const CUtensorMap* m = is_v ? &p.tvp : &p.tkp;
+        for (int r0 = 0; r0 < 64 && 64 * u + r0 + p.box_rows <= box_end; r0 += p.box_rows) {
+          const int row = static_cast<int>(pf_pool_row(a, s.seat, s.P + 64 * u + r0));
+          for (int half = 0; half < 2; ++half) tma_store_3d(m, src + half * TwSmem::kHalf + r0 * 128, half * 64, h, row);
+        }
+        bulk_commit();
+      };
+      bool ok = true;
+      for (int t = 0; t < ntk && ok; ++t) {
+        for (int is_v = 0; is_v < 2; ++is_v) {
+          if (t >= 2) {
+            // the slot's previous tile (t - 2): its MMA reads are done; store it to the pages if this CTA owns it,
+            // and let the stores finish reading before the slot is refilled
+            const int e = (is_v ? TwSmem::kVEmpty : TwSmem::kKEmpty) + (t & 1);
+            if (!tw_wait(&bars[e], ((t >> 1) - 1) & 1, abort_flag)) {
+              tw_fail(a.status, abort_flag);
+              ok = false;
+              break;
+            }
+            store_tile(t - 2, is_v != 0);
+            bulk_wait_read();
+          }
+          load_tile(t, is_v != 0);
+          if (is_v) *issued_v = t + 1; else *issued_k = t + 1;
+        }
       }
+      // the last two tiles' page stores, once their data has landed
+      if (ok && tma_store)
+        for (int t = max(ntk - 2, n_pre + u_lo); t < ntk; ++t)
+          for (int is_v = 0; is_v < 2; ++is_v) {
+            const int f = (is_v ? TwSmem::kVFull : TwSmem::kKFull) + (t & 1);
+            if (!tw_wait(&bars[f], (t >> 1) & 1, abort_flag)) {
+              tw_fail(a.status, abort_flag);
+              break;
+            }
+            store_tile(t, is_v != 0);
+          }
+      bulk_wait_all();                                        // page stores complete before the CTA exits
     }
     __syncwarp();
   } else if (warp == kTwMmaWarp) {
-    // ------------------------------------------------------------------ MMA issue
+    // ------------------------------------------------------------------ MMA issue, in whichever order inputs arrive
     constexpr uint32_t kIdescQK = umma_idesc_bf16(128, 64, 0, 0);
     constexpr uint32_t kIdescPV = umma_idesc_bf16(128, kHeadDim, 0, 1);
-    // every wait's outcome is agreed across the warp (__all_sync), so the lanes leave the loop together
+    // every wait's outcome is agreed across the warp (__all_sync), so the lanes leave together
     bool ok = __all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kQFull], 0, abort_flag));
     if (!ok && lane == 0) tw_fail(a.status, abort_flag);
-    for (int t = 0; ok && t <= ntk; ++t) {
-      if (t < ntk) {
-        const int st = t & 1;
-        if (!__all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kKvFull + st], (t >> 1) & 1, abort_flag))) {
-          if (lane == 0) tw_fail(a.status, abort_flag);
-          ok = false;
-          break;
+    int ns = 0, npv = 0;                                      // next S and next P.V to issue
+    uint64_t t0 = global_timer_ns();
+    while (ok && npv < ntk) {
+      // S(ns) into S buffer ns & 1, free once the softmax has handed over P(ns - 2) (observed before P.V(ns - 2))
+      if (ns < ntk && ns <= npv + 1 &&
+          __all_sync(0xffffffffu, mbar_test(&bars[TwSmem::kKFull + (ns & 1)], (ns >> 1) & 1))) {
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sq = sbase + TwSmem::kQ, sk = sbase + TwSmem::kK + (ns & 1) * TwSmem::kTile;
+          const uint32_t t_s = tmem + 64u * static_cast<uint32_t>(ns & 1);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_bf16(t_s, sw128_desc(sq + (ks >> 2) * 16384 + (ks & 3) * 32, 1024, 16),
+                      sw128_desc(sk + (ks >> 2) * TwSmem::kHalf + (ks & 3) * 32, 1024, 16), kIdescQK, ks > 0 ? 1u : 0u);
+          umma_commit(&bars[TwSmem::kKEmpty + (ns & 1)]);
+          umma_commit(&bars[TwSmem::kSFull + (ns & 1)]);
         }
-        // a tile's rows past the end of its source (the prefix's last tile: stale page contents; the new keys' last
-        // tile: rows of another sequence or of no sequence) may hold anything, non-finite included: zero their V rows,
-        // whole 128-byte rows, so P = 0 meets V = 0 there
-        const int first = t < n_pre ? s.P - t * 64 : s.Nn - (t - n_pre) * 64;
+        __syncwarp();
+        ++ns;
+        t0 = global_timer_ns();
+        continue;
+      }
+      // P(npv) V(npv) once P(npv) is written and V(npv) has landed
+      if (npv < ns && __all_sync(0xffffffffu, mbar_test(&bars[TwSmem::kPFull + (npv & 1)], (npv >> 1) & 1) &&
+                                                  mbar_test(&bars[TwSmem::kVFull + (npv & 1)], (npv >> 1) & 1))) {
+        // a tile's V rows past the end of its source (the prefix's last tile: stale page contents; the new keys'
+        // last tile: rows of another sequence or of none) may hold anything, non-finite included: zero them, whole
+        // 128-byte rows, so P = 0 meets V = 0 there
+        const int first = npv < n_pre ? s.P - npv * 64 : s.Nn - (npv - n_pre) * 64;
         if (first < 64) {
-          uint8_t* vt = smem + TwSmem::kStage0 + st * TwSmem::kStageBytes + TwSmem::kV;
+          uint8_t* vt = smem + TwSmem::kV + (npv & 1) * TwSmem::kTile;
           for (int i = lane; i < (64 - first) * 16; i += 32) {
             const int r = first + (i >> 4), half = (i >> 3) & 1, c = i & 7;
             *reinterpret_cast<uint4*>(vt + half * TwSmem::kHalf + r * 128 + c * 16) = make_uint4(0, 0, 0, 0);
@@ -264,36 +370,25 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t sq = sbase + TwSmem::kQ, sk = sbase + TwSmem::kStage0 + st * TwSmem::kStageBytes;
-          const uint32_t t_s = tmem + 64u * static_cast<uint32_t>(t & 1);
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            umma_bf16(t_s, sw128_desc(sq + (ks >> 2) * 16384 + (ks & 3) * 32, 1024, 16),
-                      sw128_desc(sk + (ks >> 2) * TwSmem::kHalf + (ks & 3) * 32, 1024, 16), kIdescQK, ks > 0 ? 1u : 0u);
-          umma_commit(&bars[TwSmem::kSFull + (t & 1)]);
-        }
-        __syncwarp();
-      }
-      if (t > 0) {
-        const int tp = t - 1, stp = tp & 1;
-        if (!__all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kPFull + (tp & 1)], (tp >> 1) & 1, abort_flag))) {
-          if (lane == 0) tw_fail(a.status, abort_flag);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t sp = sbase + TwSmem::kStage0 + stp * TwSmem::kStageBytes;   // P sits in the K slot
-          const uint32_t sv = sp + TwSmem::kV;
+          const uint32_t sp = sbase + TwSmem::kP, sv = sbase + TwSmem::kV + (npv & 1) * TwSmem::kTile;
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
             umma_bf16(tmem + kTwOCol, sw128_desc(sp + ks * 32, 1024, 16), sw128_desc(sv + ks * 2048, 1024, TwSmem::kHalf),
-                      kIdescPV, (tp > 0 || ks > 0) ? 1u : 0u);
-          umma_commit(&bars[TwSmem::kKvEmpty + stp]);
-          umma_commit(&bars[TwSmem::kPvDone + (tp & 1)]);
+                      kIdescPV, (npv > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&bars[TwSmem::kVEmpty + (npv & 1)]);
+          umma_commit(&bars[TwSmem::kPvDone + (npv & 1)]);
         }
         __syncwarp();
+        ++npv;
+        t0 = global_timer_ns();
+        continue;
       }
+      if (*abort_flag || global_timer_ns() - t0 > 2000000000ull) {
+        if (lane == 0) tw_fail(a.status, abort_flag);
+        ok = false;
+        break;
+      }
+      __nanosleep(20);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue (warps 0-3)
@@ -302,8 +397,8 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
     const bool row_valid = row_j < s.R;
     const int my_limit = (a.causal && row_valid) ? shift + row_j : L - 1;   // last visible key of this row
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    if (a.write_kv)   // this query tile's share of the page writes, while the first copies and S(0) are in flight
-      write_new_rows(a, s, h, min(qt * 64, s.Nn), qt == ntq - 1 ? s.Nn : min(qt * 64 + 64, s.Nn), tid);
+    if (a.write_kv && max(box_end, 64 * u_lo) < own_end)      // owned rows no TMA store covers
+      write_new_rows(a, s, h, max(box_end, 64 * u_lo), own_end, tid);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int t = 0; t < ntk; ++t) {
@@ -367,9 +462,9 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
       const float2 lsa = __fadd2_rn(__fadd2_rn(ls2[0], ls2[1]), __fadd2_rn(ls2[2], ls2[3]));
       l_run = l_run * alpha + (lsa.x + lsa.y);
       m_run = m_new;
-      // ---- rescale O where a max moved: O must hold P(t-1) V(t-1) first (tile 0 starts O from zero instead). The
-      //      barrier of P.V(t-1) last completed for P.V(t-3), which S(t) (issued after P.V(t-2)) has seen finish.
-      if (t > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      if (t > 0) {
+        // P(t-1) V(t-1) must be done: it reads the P buffer, and O must hold it before a rescale. Its barrier last
+        // completed for P.V(t-3), which this warp waited for at tile t-2.
         ok = tw_wait(&bars[TwSmem::kPvDone + ((t - 1) & 1)], ((t - 1) >> 1) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) {
@@ -377,20 +472,22 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
           break;
         }
         tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {   // rescale O where a max moved (tile 0 starts O from zero)
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float ov[32];
-          tmem_ld32(tmem + kTwOCol + lane_base + c * 32, ov);
-          tc_wait_ld();
+          for (int c = 0; c < 4; ++c) {
+            float ov[32];
+            tmem_ld32(tmem + kTwOCol + lane_base + c * 32, ov);
+            tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-          tmem_st32(tmem + kTwOCol + lane_base + c * 32, ov);
+            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+            tmem_st32(tmem + kTwOCol + lane_base + c * 32, ov);
+          }
+          tc_wait_st();
         }
-        tc_wait_st();
       }
-      // ---- P(t) as bf16 into the K slot of stage t & 1 (S(t) is done, so K(t) is dead): 128-byte-swizzled K-major,
-      //      row r at (r / 8) * 1024 + (r % 8) * 128, its 16-byte chunk c at position c ^ (r % 8)
-      uint8_t* prow = smem + TwSmem::kStage0 + b * TwSmem::kStageBytes + (row >> 3) * 1024 + (row & 7) * 128;
+      // ---- P(t) as bf16: 128-byte-swizzled K-major, row r at (r / 8) * 1024 + (r % 8) * 128, its 16-byte chunk c at
+      //      position c ^ (r % 8)
+      uint8_t* prow = smem + TwSmem::kP + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) =
@@ -442,10 +539,13 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
     }
     if (tid == kTwProducerWarp * 32) {
       mbar_wait_bounded(&bars[TwSmem::kQFull], 0, 200000000ull);
-      const int n = *issued;
-      for (int st = 0; st < 2; ++st) {
-        const int last = (n - 1 - st) >= 0 ? ((n - 1 - st) & ~1) + st : -1;   // last tile issued into stage st
-        if (last >= 0) mbar_wait_bounded(&bars[TwSmem::kKvFull + st], (last >> 1) & 1, 200000000ull);
+      for (int is_v = 0; is_v < 2; ++is_v) {
+        const int n = is_v ? *issued_v : *issued_k;
+        for (int st = 0; st < 2; ++st) {
+          const int last = (n - 1 - st) >= 0 ? ((n - 1 - st) & ~1) + st : -1;   // last tile issued into slot st
+          if (last >= 0)
+            mbar_wait_bounded(&bars[(is_v ? TwSmem::kVFull : TwSmem::kKFull) + st], (last >> 1) & 1, 200000000ull);
+        }
       }
     }
   }
@@ -504,29 +604,28 @@ cudaError_t launch_prefill_tma(const PrefillArgs& a, cudaStream_t stream, bool* 
       !make_rows_map(&p.tk, a.k, a.kv_rows, kKvHeads, a.kv_stride * 2, 64) ||
       !make_rows_map(&p.tv, a.v, a.kv_rows, kKvHeads, a.kv_stride * 2, 64))
     return cudaSuccess;
-  if (a.prefix_lens != nullptr) {
-    const int ps = a.page_size;
-    const int box = ps >= 64 ? 64 : ps;
-    if (!(ps % 64 == 0 || ps == 8 || ps == 16 || ps == 32)) return cudaSuccess;
+  // pool maps: needed to read a prefix (else the call does not fit this kernel) and used for the page writes
+  const int ps = a.page_size;
+  const bool box_ok = ps > 0 && (ps % 64 == 0 || ps == 8 || ps == 16 || ps == 32);
+  p.box_rows = box_ok ? (ps >= 64 ? 64 : ps) : 64;
+  p.pool_maps = 0;
+  if ((a.prefix_lens != nullptr || a.write_kv) && box_ok) {
     const long long rows = static_cast<long long>(a.num_pages) * ps;
-    if (!make_rows_map(&p.tkp, a.k_pool, rows, kKvHeads, kRowBytes, box) ||
-        !make_rows_map(&p.tvp, a.v_pool, rows, kKvHeads, kRowBytes, box))
-      return cudaSuccess;
-    p.box_rows = box;
-  } else {
-    p.box_rows = 64;
+    p.pool_maps = make_rows_map(&p.tkp, a.k_pool, rows, kKvHeads, kRowBytes, p.box_rows) &&
+                  make_rows_map(&p.tvp, a.v_pool, rows, kKvHeads, kRowBytes, p.box_rows);
   }
+  if (a.prefix_lens != nullptr && !p.pool_maps) return cudaSuccess;
   static bool configured[64] = {false};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    e = cudaFuncSetAttribute(prefill_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TwSmem::kAlloc);
+    e = cudaFuncSetAttribute(prefill_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TwSmem::kBytes);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   const int qtiles = a.max_seqlen_q > 0 ? (a.max_seqlen_q + 63) / 64 : 1;
-  prefill_tma_kernel<<<dim3(qtiles, kKvHeads, a.num_seqs), kTwThreads, TwSmem::kAlloc, stream>>>(p);
+  prefill_tma_kernel<<<dim3(qtiles, kKvHeads, a.num_seqs), kTwThreads, TwSmem::kBytes, stream>>>(p);
   *launched = true;
   return cudaGetLastError();
 }
