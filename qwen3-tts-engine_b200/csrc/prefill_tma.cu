@@ -69,6 +69,7 @@ struct PfTmaParams {
   CUtensorMap tv;
   CUtensorMap tkp;   // pools     [num_pages * page_size][8 heads][128] (prefix reads, page-write stores)
   CUtensorMap tvp;
+  CUtensorMap to;    // output rows [q_rows][16 heads][128]
   int box_rows;      // rows per pool box: min(page_size, 64)
   int pool_maps;     // tkp / tvp are valid
 };
@@ -181,6 +182,12 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
   const PrefillArgs& a = p.a;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == kTwProducerWarp * 32) {   // the descriptors travel while the sequence geometry loads
+    prefetch_map(&p.tq);
+    prefetch_map(&p.tk);
+    prefetch_map(&p.tv);
+    prefetch_map(&p.to);
+  }
   const int h = blockIdx.y;
   const PfSeq s = pf_seq(a, blockIdx.z);
   if (s.R <= 0) {                                             // no queries: CTA 0 still writes the new rows (write_kv)
@@ -249,9 +256,6 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
   if (warp == kTwProducerWarp) {
     // ------------------------------------------------------------------ producer: TMA copies and page stores
     if (lane == 0) {
-      prefetch_map(&p.tq);
-      prefetch_map(&p.tk);
-      prefetch_map(&p.tv);
       const uint32_t qbar = smem_addr(&bars[TwSmem::kQFull]);
       mbar_arrive_expect_tx(&bars[TwSmem::kQFull], 32768u);
       for (int g = 0; g < 2; ++g)
@@ -320,7 +324,7 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
             }
             store_tile(t, is_v != 0);
           }
-      bulk_wait_all();                                        // page stores complete before the CTA exits
+      bulk_wait_read();   // the page stores have read shared memory (their global writes complete on their own)
     }
     __syncwarp();
   } else if (warp == kTwMmaWarp) {
@@ -503,11 +507,45 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
       ok = __all_sync(0xffffffffu, ok);
       if (!ok && lane == 0) tw_fail(a.status, abort_flag);
     }
-    if (ok) {
-      tc_fence_after();
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    if (ok) tc_fence_after();
+    if (qt * 64 + 64 <= s.R) {
+      // a full query tile: the rows go through shared memory (the Q buffer: the last S has read it) in the layout the
+      // Q tile came in, and out as four TMA tensor stores (2 heads x 2 dim halves) issued by one thread. The named
+      // barrier is reached by all four softmax warps on every path (ok is agreed per warp, not across warps).
+      if (ok) {
+        uint8_t* orow = smem + TwSmem::kQ + row_g * 8192 + (row & 63) * 128;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(tmem + kTwOCol + lane_base + c * 32, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            const int chunk = (c * 32 + i) >> 3;              // 16-byte chunk 0..15 of the 256-byte row
+            uint4 w;
+            w.x = pack_bf16x2(ov[i] * inv, ov[i + 1] * inv);
+            w.y = pack_bf16x2(ov[i + 2] * inv, ov[i + 3] * inv);
+            w.z = pack_bf16x2(ov[i + 4] * inv, ov[i + 5] * inv);
+            w.w = pack_bf16x2(ov[i + 6] * inv, ov[i + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + (chunk >> 3) * 16384 + (((chunk & 7) ^ (row & 7)) << 4)) = w;
+          }
+        }
+        fence_proxy_async_smem();
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");            // the four softmax warps only
+      if (tid == 0 && !*abort_flag) {
+        for (int g = 0; g < 2; ++g)
+          for (int half = 0; half < 2; ++half)
+            tma_store_3d(&p.to, sbase + TwSmem::kQ + half * 16384 + g * 8192, half * 64, 2 * h + g, s.q0 + qt * 64);
+        bulk_commit();
+        bulk_wait_read();                                     // shared memory stays valid until the stores read it
+      }
+    } else if (ok) {
+      // the sequence's last, partial query tile: per-thread stores of the valid rows (a box would spill into the
+      // next sequence's rows)
       __nv_bfloat16* dst = a.out + static_cast<long long>(s.q0 + (row_valid ? row_j : 0)) * a.out_stride +
                            (2 * h + row_g) * kHeadDim;
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float ov[32];
@@ -600,7 +638,8 @@ cudaError_t launch_prefill_tma(const PrefillArgs& a, cudaStream_t stream, bool* 
   PfTmaParams p;
   memset(&p, 0, sizeof(p));
   p.a = a;
-  if (!make_rows_map(&p.tq, a.q, a.q_rows, kQHeads, a.q_stride * 2, 64) ||
+  if ((a.out_stride * 2) % 16 || !make_rows_map(&p.to, a.out, a.q_rows, kQHeads, a.out_stride * 2, 64) ||
+      !make_rows_map(&p.tq, a.q, a.q_rows, kQHeads, a.q_stride * 2, 64) ||
       !make_rows_map(&p.tk, a.k, a.kv_rows, kKvHeads, a.kv_stride * 2, 64) ||
       !make_rows_map(&p.tv, a.v, a.kv_rows, kKvHeads, a.kv_stride * 2, 64))
     return cudaSuccess;
