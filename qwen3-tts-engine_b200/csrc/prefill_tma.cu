@@ -123,6 +123,19 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Wait (suspended in hardware, for at most about `hint_ns`) for phase `parity` of `bar`; true when it completed.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Number of new-key tiles the query tile q of a sequence visits (the key tiles past the prefix).
 __device__ __forceinline__ int new_tiles_of(const PfSeq& s, int q, int causal) {
   const int L = s.P + s.Nn, shift = L - s.R;
@@ -188,14 +201,16 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
     prefetch_map(&p.tv);
     prefetch_map(&p.to);
   }
+  // grid (sequence, KV head, query tile from the last): blocks launch in linear order, so every sequence's heaviest
+  // (latest) query tile goes out in the first wave and the light ones fill the tail
   const int h = blockIdx.y;
-  const PfSeq s = pf_seq(a, blockIdx.z);
+  const PfSeq s = pf_seq(a, blockIdx.x);
   if (s.R <= 0) {                                             // no queries: CTA 0 still writes the new rows (write_kv)
-    if (a.write_kv && blockIdx.x == 0 && tid < 128) write_new_rows(a, s, h, 0, s.Nn, tid);
+    if (a.write_kv && blockIdx.z == 0 && tid < 128) write_new_rows(a, s, h, 0, s.Nn, tid);
     return;
   }
   const int ntq = (s.R + 63) / 64;
-  const int qt = ntq - 1 - static_cast<int>(blockIdx.x);     // heavy (late) query tiles take the low block indices
+  const int qt = ntq - 1 - static_cast<int>(blockIdx.z);
   if (qt < 0) return;                                         // uniform per CTA; nothing allocated yet
   if (smem_addr(smem) & 1023u) {                              // the swizzled tiles need 1024-byte aligned atoms
     if (tid == 0) atomicOr(a.status, kStatusSmemAlign);
@@ -335,6 +350,7 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
     bool ok = __all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kQFull], 0, abort_flag));
     if (!ok && lane == 0) tw_fail(a.status, abort_flag);
     int ns = 0, npv = 0;                                      // next S and next P.V to issue
+    uint32_t idle = 0;
     uint64_t t0 = global_timer_ns();
     while (ok && npv < ntk) {
       // S(ns) into S buffer ns & 1, free once the softmax has handed over P(ns - 2) (observed before P.V(ns - 2))
@@ -387,12 +403,17 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
         t0 = global_timer_ns();
         continue;
       }
-      if (*abort_flag || global_timer_ns() - t0 > 2000000000ull) {
+      // nothing ready: sleep in hardware on the event expected next (P(npv) once S(npv) is out, else K(ns)) until it
+      // completes or about 200 ns pass, then look at both again; the clock and the abort flag every 64 rounds
+      if (npv < ns)
+        mbar_try_wait_hint(&bars[TwSmem::kPFull + (npv & 1)], (npv >> 1) & 1, 200);
+      else
+        mbar_try_wait_hint(&bars[TwSmem::kKFull + (ns & 1)], (ns >> 1) & 1, 200);
+      if ((++idle & 63) == 0 && (*abort_flag || global_timer_ns() - t0 > 2000000000ull)) {
         if (lane == 0) tw_fail(a.status, abort_flag);
         ok = false;
         break;
       }
-      __nanosleep(20);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue (warps 0-3)
@@ -664,7 +685,7 @@ cudaError_t launch_prefill_tma(const PrefillArgs& a, cudaStream_t stream, bool* 
     configured[dev] = true;
   }
   const int qtiles = a.max_seqlen_q > 0 ? (a.max_seqlen_q + 63) / 64 : 1;
-  prefill_tma_kernel<<<dim3(qtiles, kKvHeads, a.num_seqs), kTwThreads, TwSmem::kBytes, stream>>>(p);
+  prefill_tma_kernel<<<dim3(a.num_seqs, kKvHeads, qtiles), kTwThreads, TwSmem::kBytes, stream>>>(p);
   *launched = true;
   return cudaGetLastError();
 }
