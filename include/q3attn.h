@@ -36,7 +36,6 @@ extern "C" {
 #define Q3_STATUS_WAIT_TIMEOUT 1u  /* a pipeline wait gave up (kernel returned early; outputs invalid) */
 #define Q3_STATUS_BAD_PAGE 2u      /* a block-table entry or slot outside the pool (access skipped / clamped) */
 #define Q3_STATUS_BAD_LENGTH 4u    /* a sequence length beyond the seat's block-table capacity (clamped) */
-#define Q3_STATUS_SMEM_ALIGN 8u    /* a kernel's shared memory base was not 1024-byte aligned (kernel returned) */
 
 int q3_version(void);
 const char* q3_error_string(int code);

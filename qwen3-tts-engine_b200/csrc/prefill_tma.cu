@@ -12,20 +12,21 @@
 //                       P(t) V(t) is done. Prefix keys come page by page out of the pool, new keys as one box per 64
 //                       rows. With write_kv it also stores the new K/V tiles this CTA owns into the pages (TMA tensor
 //                       stores from the same shared-memory tiles, page-aligned boxes).
-//   warp 5 (MMA)        lane 0 issues S(t) = Q K(t)^T into one of two TMEM S buffers and O += P(t) V(t) into the TMEM
-//                       O accumulator, each as soon as its inputs are ready (S(t+1) may go before or after P(t) V(t));
-//                       tcgen05.commit arrives on mbarriers (K slot free + S ready; V slot free + P.V done).
+//   warp 5 (MMA)        lane 0 issues S(t) = Q K(t)^T into one of two TMEM S buffers once K(t) has landed and
+//                       P(t-2) V(t-2) (whose P sat in that buffer) is done; tcgen05.commit arrives on the K-slot-free
+//                       and S-ready barriers.
 //   warps 0-3 (softmax) thread r owns TMEM lane r = accumulator row r: reads S(t) (tcgen05.ld), online softmax in the
 //                       exp2 domain with a lazy running max (O rescaled in TMEM only when a max grows by more than 2^8),
-//                       writes P(t) as bf16 into the P buffer once P(t-1) V(t-1) is done, and at the end divides O by
-//                       the row sums and stores the output rows. Page-write rows that do not fill a page-aligned box
+//                       writes P(t) as bf16 into TMEM over S(t) (tcgen05.st); lane 0 of warp 0 then issues O += P(t)
+//                       V(t) into the TMEM O accumulator itself (A from TMEM, V from shared memory) as soon as all four
+//                       warps have written P(t), committing to the V-slot-free and P.V-done barriers. At the end the
+//                       warps divide O by the row sums and store the output rows. Page-write rows that do not fill a page-aligned box
 //                       (a prefix not aligned to the box, a last partial box) are copied by these threads at the start.
 // While the softmax warps work on S(t), the tensor core computes S(t+1) and P(t-1) V(t-1), and the producer loads the
-// next tiles. Shared memory: Q 32 KB + K 2 x 16 KB + V 2 x 16 KB + P 16 KB = 112 KB, TMEM 256 columns (S0, S1, O): two
-// CTAs per SM (the 112 KB leave no room for alignment slack: the kernel checks that its shared memory starts on a
-// 1024-byte boundary and otherwise raises a status bit and returns). Every mbarrier wait is bounded (2 s); a timed-out
-// role raises the status bit and an abort flag the other roles poll, in-flight copies and MMAs are waited for
-// (bounded), and TMEM is always freed.
+// next tiles. Shared memory: Q 32 KB + K 2 x 16 KB + V 2 x 16 KB = 96 KB (+ alignment slack); TMEM 256 columns (S0,
+// S1, O; P(t) is written as bf16 over S(t) once S(t) is read, and the P.V MMA takes its A operand from there): two CTAs
+// per SM. Every mbarrier wait is bounded (2 s); a timed-out role raises the status bit and an abort flag the other
+// roles poll, in-flight copies and MMAs are waited for (bounded), and TMEM is always freed.
 #include <cuda.h>
 
 #include <cstring>
@@ -47,19 +48,19 @@ struct TwSmem {
   static constexpr int kV = 65536;            // V slot s at kV + s * kTile: same layout (MN-major B operand)
   static constexpr int kTile = 16384;
   static constexpr int kHalf = 8192;          // one dim half of a K or V tile
-  static constexpr int kP = 98304;            // P [128 rows][64 keys] bf16, SW128 K-major (16 KB)
-  static constexpr int kBars = kP + 16384;
+  static constexpr int kBars = 98304;
   // Barriers, every one waited with a parity that is never ambiguous: a waiter is at most one phase away from its
   // barrier's next completion (each role waits for every phase of the barriers it waits on, in order, and no role can
   // complete a barrier twice before its waiter has seen the first completion).
   static constexpr int kQFull = 0, kKFull = 1, kVFull = 3, kKEmpty = 5, kVEmpty = 7, kSFull = 9, kPFull = 11,
-                       kPvDone = 13, kFinal = 15;
-  static constexpr int kNumBars = 16;
+                       kPvDone = 13, kFinal = 15, kFinalPv = 16;
+  static constexpr int kNumBars = 17;
   static constexpr int kTmemSlot = kBars + 8 * kNumBars;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kIssuedK = kAbort + 4;  // K and V tiles the producer has issued (read on the abort path)
   static constexpr int kIssuedV = kIssuedK + 4;
   static constexpr int kBytes = kIssuedV + 4;
+  static constexpr int kAlloc = kBytes + 1024;   // + slack to align the base to 1024 B (128-byte swizzle atoms)
 };
 
 struct PfTmaParams {
@@ -109,32 +110,6 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // This thread's bulk stores are complete.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-// Non-blocking test of phase `parity` of `bar`.
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Wait (suspended in hardware, for at most about `hint_ns`) for phase `parity` of `bar`; true when it completed.
-__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
 
 // Number of new-key tiles the query tile q of a sequence visits (the key tiles past the prefix).
 __device__ __forceinline__ int new_tiles_of(const PfSeq& s, int q, int causal) {
@@ -193,7 +168,8 @@ __device__ __forceinline__ void write_new_rows(const PrefillArgs& a, const PfSeq
 
 __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid_constant__ PfTmaParams p) {
   const PrefillArgs& a = p.a;
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t tw_raw[];
+  uint8_t* smem = tw_raw + ((1024u - (smem_addr(tw_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == kTwProducerWarp * 32) {   // the descriptors travel while the sequence geometry loads
     prefetch_map(&p.tq);
@@ -212,10 +188,6 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
   const int ntq = (s.R + 63) / 64;
   const int qt = ntq - 1 - static_cast<int>(blockIdx.z);
   if (qt < 0) return;                                         // uniform per CTA; nothing allocated yet
-  if (smem_addr(smem) & 1023u) {                              // the swizzled tiles need 1024-byte aligned atoms
-    if (tid == 0) atomicOr(a.status, kStatusSmemAlign);
-    return;
-  }
 
   // ---- key tiles: the prefix keys [0, P) in tiles of 64, then the new keys [0, N) in tiles of 64 (combined index
   //      P + j), each tile from one source; only the keys some row of this query tile can see are visited
@@ -258,6 +230,7 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
       mbar_init(&bars[TwSmem::kPvDone + i], 1);
     }
     mbar_init(&bars[TwSmem::kFinal], 1);
+    mbar_init(&bars[TwSmem::kFinalPv], 1);
     *abort_flag = 0;
     *issued_k = 0;
     *issued_v = 0;
@@ -343,78 +316,31 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
     }
     __syncwarp();
   } else if (warp == kTwMmaWarp) {
-    // ------------------------------------------------------------------ MMA issue, in whichever order inputs arrive
+    // ------------------------------------------------------------------ MMA issue: S(t) = Q K(t)^T, in order
+    // S(t) goes into TMEM buffer t & 1 once K(t) has landed and P(t - 2) V(t - 2) is done (P(t - 2) was written over
+    // S(t - 2) in that buffer). P V is issued by softmax warp 0 the moment P is written: no hand-over through this
+    // warp. Every wait's outcome is agreed across the warp (__all_sync), so the lanes leave together.
     constexpr uint32_t kIdescQK = umma_idesc_bf16(128, 64, 0, 0);
-    constexpr uint32_t kIdescPV = umma_idesc_bf16(128, kHeadDim, 0, 1);
-    // every wait's outcome is agreed across the warp (__all_sync), so the lanes leave together
     bool ok = __all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kQFull], 0, abort_flag));
-    if (!ok && lane == 0) tw_fail(a.status, abort_flag);
-    int ns = 0, npv = 0;                                      // next S and next P.V to issue
-    uint32_t idle = 0;
-    uint64_t t0 = global_timer_ns();
-    while (ok && npv < ntk) {
-      // S(ns) into S buffer ns & 1, free once the softmax has handed over P(ns - 2) (observed before P.V(ns - 2))
-      if (ns < ntk && ns <= npv + 1 &&
-          __all_sync(0xffffffffu, mbar_test(&bars[TwSmem::kKFull + (ns & 1)], (ns >> 1) & 1))) {
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t sq = sbase + TwSmem::kQ, sk = sbase + TwSmem::kK + (ns & 1) * TwSmem::kTile;
-          const uint32_t t_s = tmem + 64u * static_cast<uint32_t>(ns & 1);
+    for (int t = 0; ok && t < ntk; ++t) {
+      ok = __all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kKFull + (t & 1)], (t >> 1) & 1, abort_flag));
+      if (ok && t >= 2)
+        ok = __all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kPvDone + (t & 1)], ((t - 2) >> 1) & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t sq = sbase + TwSmem::kQ, sk = sbase + TwSmem::kK + (t & 1) * TwSmem::kTile;
+        const uint32_t t_s = tmem + 64u * static_cast<uint32_t>(t & 1);
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            umma_bf16(t_s, sw128_desc(sq + (ks >> 2) * 16384 + (ks & 3) * 32, 1024, 16),
-                      sw128_desc(sk + (ks >> 2) * TwSmem::kHalf + (ks & 3) * 32, 1024, 16), kIdescQK, ks > 0 ? 1u : 0u);
-          umma_commit(&bars[TwSmem::kKEmpty + (ns & 1)]);
-          umma_commit(&bars[TwSmem::kSFull + (ns & 1)]);
-        }
-        __syncwarp();
-        ++ns;
-        t0 = global_timer_ns();
-        continue;
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16(t_s, sw128_desc(sq + (ks >> 2) * 16384 + (ks & 3) * 32, 1024, 16),
+                    sw128_desc(sk + (ks >> 2) * TwSmem::kHalf + (ks & 3) * 32, 1024, 16), kIdescQK, ks > 0 ? 1u : 0u);
+        umma_commit(&bars[TwSmem::kKEmpty + (t & 1)]);
+        umma_commit(&bars[TwSmem::kSFull + (t & 1)]);
       }
-      // P(npv) V(npv) once P(npv) is written and V(npv) has landed
-      if (npv < ns && __all_sync(0xffffffffu, mbar_test(&bars[TwSmem::kPFull + (npv & 1)], (npv >> 1) & 1) &&
-                                                  mbar_test(&bars[TwSmem::kVFull + (npv & 1)], (npv >> 1) & 1))) {
-        // a tile's V rows past the end of its source (the prefix's last tile: stale page contents; the new keys'
-        // last tile: rows of another sequence or of none) may hold anything, non-finite included: zero them, whole
-        // 128-byte rows, so P = 0 meets V = 0 there
-        const int first = npv < n_pre ? s.P - npv * 64 : s.Nn - (npv - n_pre) * 64;
-        if (first < 64) {
-          uint8_t* vt = smem + TwSmem::kV + (npv & 1) * TwSmem::kTile;
-          for (int i = lane; i < (64 - first) * 16; i += 32) {
-            const int r = first + (i >> 4), half = (i >> 3) & 1, c = i & 7;
-            *reinterpret_cast<uint4*>(vt + half * TwSmem::kHalf + r * 128 + c * 16) = make_uint4(0, 0, 0, 0);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-        }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t sp = sbase + TwSmem::kP, sv = sbase + TwSmem::kV + (npv & 1) * TwSmem::kTile;
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma_bf16(tmem + kTwOCol, sw128_desc(sp + ks * 32, 1024, 16), sw128_desc(sv + ks * 2048, 1024, TwSmem::kHalf),
-                      kIdescPV, (npv > 0 || ks > 0) ? 1u : 0u);
-          umma_commit(&bars[TwSmem::kVEmpty + (npv & 1)]);
-          umma_commit(&bars[TwSmem::kPvDone + (npv & 1)]);
-        }
-        __syncwarp();
-        ++npv;
-        t0 = global_timer_ns();
-        continue;
-      }
-      // nothing ready: sleep in hardware on the event expected next (P(npv) once S(npv) is out, else K(ns)) until it
-      // completes or about 200 ns pass, then look at both again; the clock and the abort flag every 64 rounds
-      if (npv < ns)
-        mbar_try_wait_hint(&bars[TwSmem::kPFull + (npv & 1)], (npv >> 1) & 1, 200);
-      else
-        mbar_try_wait_hint(&bars[TwSmem::kKFull + (ns & 1)], (ns >> 1) & 1, 200);
-      if ((++idle & 63) == 0 && (*abort_flag || global_timer_ns() - t0 > 2000000000ull)) {
-        if (lane == 0) tw_fail(a.status, abort_flag);
-        ok = false;
-        break;
-      }
+      __syncwarp();
     }
+    if (!ok && lane == 0) tw_fail(a.status, abort_flag);
   } else {
     // ------------------------------------------------------------------ softmax + epilogue (warps 0-3)
     const int row = tid;                                       // TMEM lane = accumulator row
@@ -487,9 +413,9 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
       const float2 lsa = __fadd2_rn(__fadd2_rn(ls2[0], ls2[1]), __fadd2_rn(ls2[2], ls2[3]));
       l_run = l_run * alpha + (lsa.x + lsa.y);
       m_run = m_new;
-      if (t > 0) {
-        // P(t-1) V(t-1) must be done: it reads the P buffer, and O must hold it before a rescale. Its barrier last
-        // completed for P.V(t-3), which this warp waited for at tile t-2.
+      if (t > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // rescale O where a max moved (tile 0 starts O from zero): O must hold P(t-1) V(t-1) first. Its barrier last
+        // completed for P.V(t-3), which finished before S(t) was issued (S(t) waits for P.V(t-2)).
         ok = tw_wait(&bars[TwSmem::kPvDone + ((t - 1) & 1)], ((t - 1) >> 1) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) {
@@ -497,30 +423,58 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {   // rescale O where a max moved (tile 0 starts O from zero)
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float ov[32];
-            tmem_ld32(tmem + kTwOCol + lane_base + c * 32, ov);
-            tc_wait_ld();
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(tmem + kTwOCol + lane_base + c * 32, ov);
+          tc_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-            tmem_st32(tmem + kTwOCol + lane_base + c * 32, ov);
-          }
-          tc_wait_st();
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(tmem + kTwOCol + lane_base + c * 32, ov);
         }
+        tc_wait_st();
       }
-      // ---- P(t) as bf16: 128-byte-swizzled K-major, row r at (r / 8) * 1024 + (r % 8) * 128, its 16-byte chunk c at
-      //      position c ^ (r % 8)
-      uint8_t* prow = smem + TwSmem::kP + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      fence_proxy_async_smem();
+      // ---- P(t) as bf16 into TMEM over S(t) (already read): lane r = row r, keys 2i and 2i+1 in column 64b + i, the
+      //      layout the P.V MMA reads its A operand in
+      tmem_st32u(tmem + 64u * b + lane_base, pk);
+      tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[TwSmem::kPFull + b]);
+      if (warp == 0) {
+        // ---- O += P(t) V(t), issued here once all four warps have written P(t) and V(t) has landed
+        ok = __all_sync(0xffffffffu, tw_wait(&bars[TwSmem::kPFull + b], (t >> 1) & 1, abort_flag) &&
+                                         tw_wait(&bars[TwSmem::kVFull + b], (t >> 1) & 1, abort_flag));
+        if (!ok) {
+          if (lane == 0) tw_fail(a.status, abort_flag);
+          break;
+        }
+        // a tile's V rows past the end of its source (the prefix's last tile: stale page contents; the new keys'
+        // last tile: rows of another sequence or of none) may hold anything, non-finite included: zero them, whole
+        // 128-byte rows, so P = 0 meets V = 0 there
+        const int first = t < n_pre ? s.P - t * 64 : s.Nn - (t - n_pre) * 64;
+        if (first < 64) {
+          uint8_t* vt = smem + TwSmem::kV + b * TwSmem::kTile;
+          for (int i = lane; i < (64 - first) * 16; i += 32) {
+            const int r = first + (i >> 4), half = (i >> 3) & 1, c = i & 7;
+            *reinterpret_cast<uint4*>(vt + half * TwSmem::kHalf + r * 128 + c * 16) = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          constexpr uint32_t kIdescPV = umma_idesc_bf16(128, kHeadDim, 0, 1);
+          const uint32_t svv = sbase + TwSmem::kV + b * TwSmem::kTile;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16_tmem_a(tmem + kTwOCol, tmem + 64u * b + 8u * ks, sw128_desc(svv + ks * 2048, 1024, TwSmem::kHalf),
+                             kIdescPV, (t > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&bars[TwSmem::kVEmpty + b]);
+          umma_commit(&bars[TwSmem::kPvDone + b]);
+        }
+        __syncwarp();
+      }
     }
     // ---- epilogue: O / l -> bf16 rows (every thread takes part in the warp-collective TMEM loads)
     if (ok) {
@@ -595,6 +549,10 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
     if (tid == kTwMmaWarp * 32) {
       umma_commit(&bars[TwSmem::kFinal]);
       mbar_wait_bounded(&bars[TwSmem::kFinal], 0, 200000000ull);
+    }
+    if (tid == 0) {                                           // the P.V issuer
+      umma_commit(&bars[TwSmem::kFinalPv]);
+      mbar_wait_bounded(&bars[TwSmem::kFinalPv], 0, 200000000ull);
     }
     if (tid == kTwProducerWarp * 32) {
       mbar_wait_bounded(&bars[TwSmem::kQFull], 0, 200000000ull);
@@ -680,12 +638,12 @@ cudaError_t launch_prefill_tma(const PrefillArgs& a, cudaStream_t stream, bool* 
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    e = cudaFuncSetAttribute(prefill_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TwSmem::kBytes);
+    e = cudaFuncSetAttribute(prefill_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TwSmem::kAlloc);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   const int qtiles = a.max_seqlen_q > 0 ? (a.max_seqlen_q + 63) / 64 : 1;
-  prefill_tma_kernel<<<dim3(a.num_seqs, kKvHeads, qtiles), kTwThreads, TwSmem::kBytes, stream>>>(p);
+  prefill_tma_kernel<<<dim3(a.num_seqs, kKvHeads, qtiles), kTwThreads, TwSmem::kAlloc, stream>>>(p);
   *launched = true;
   return cudaGetLastError();
 }

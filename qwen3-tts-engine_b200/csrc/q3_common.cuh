@@ -28,7 +28,6 @@ enum : uint32_t {
   kStatusWaitTimeout = 1u << 0,   // an mbarrier wait gave up after its time limit
   kStatusBadPage = 1u << 1,       // a block-table entry outside [0, num_pages)
   kStatusBadLength = 1u << 2,     // a sequence length beyond the block table's capacity
-  kStatusSmemAlign = 1u << 3,     // a kernel found its dynamic shared memory base not 1024-byte aligned (returned)
 };
 
 // ---------------------------------------------------------------- bf16 <-> fp32

@@ -9,7 +9,7 @@ import os
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libq3attn.so")
 
 Q3_OK, Q3_ERR_INVALID, Q3_ERR_UNSUPPORTED, Q3_ERR_ALIGNMENT, Q3_ERR_WORKSPACE, Q3_ERR_CUDA, Q3_ERR_SCRATCH_LIMIT = range(7)
-STATUS_WAIT_TIMEOUT, STATUS_BAD_PAGE, STATUS_BAD_LENGTH, STATUS_SMEM_ALIGN = 1, 2, 4, 8
+STATUS_WAIT_TIMEOUT, STATUS_BAD_PAGE, STATUS_BAD_LENGTH = 1, 2, 4
 
 _P, _I32, _I64, _F32, _SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 
