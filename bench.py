@@ -52,6 +52,8 @@ def parse():
     p.add_argument("--variant", type=int, default=0, help="decode kernel variant (q3_set_decode_variant)")
     p.add_argument("--num-splits", type=int, default=0)
     p.add_argument("--prefill-kernel", type=int, default=0, help="prefill kernel (q3_set_prefill_kernel): 0 TMA, 1 single")
+    p.add_argument("--ring-frame-kernel", type=int, default=0,
+                   help="one-frame ring kernel (q3_set_ring_frame_kernel): 0 heads per CTA, 1 CTA per head")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -439,6 +441,7 @@ def bench_aux(a):
     torch.cuda.set_device(dev)
     peak, peak_kind = hbm_peak()
     q3attn.set_prefill_kernel(a.prefill_kernel)
+    q3attn.set_ring_frame_kernel(a.ring_frame_kernel)
 
     def timed(fn, n):
         s = torch.cuda.Stream(device=dev)

@@ -614,6 +614,12 @@ int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
   return record(q3::launch_qk_norm_rope(a, static_cast<cudaStream_t>(stream)));
 }
 
+int q3_set_ring_frame_kernel(int kernel) {
+  const int prev = q3::g_ring_frame_kernel;
+  if (kernel == 0 || kernel == 1) q3::g_ring_frame_kernel = kernel;
+  return prev;
+}
+
 int q3_ring_window_attn(const void* q, const void* k_new, const void* v_new, int64_t qkv_batch_stride,
                         int64_t qkv_frame_stride, void* k_ring, void* v_ring, int64_t ring_stream_stride,
                         int64_t ring_slot_stride, const int64_t* ring_rows, const int64_t* pos, int32_t batch,

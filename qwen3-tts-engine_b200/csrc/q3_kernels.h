@@ -201,6 +201,9 @@ struct RingArgs {
 };
 size_t ring_smem_bytes(int ring, int past, int hd, int n);
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);
+// Which one-frame ring kernel launch_ring_attn uses: 0 = one warp per head, G heads per CTA, where the heads divide
+// (default); 1 = the one-CTA-per-(stream, head) kernel always.
+extern int g_ring_frame_kernel;
 
 struct PrefillArgs {
   const __nv_bfloat16* q;          // [Tq, 16, 128] rows, row stride q_stride (elements)

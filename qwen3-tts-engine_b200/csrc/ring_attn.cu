@@ -426,6 +426,174 @@ __global__ void __launch_bounds__(kRingThreads) ring_attn_frame_kernel(const Rin
   }
 }
 
+// One query frame, G heads per CTA, one warp per head: the streaming case with far fewer instructions per byte than
+// ring_attn_frame_kernel (no block-wide barrier after the staging wait; every phase is warp-local). The G heads of a
+// stream are contiguous in the ring rows and in q / k / v, so each ring row (distance d) of K and V for the group
+// arrives by ONE bulk copy of G x HD halves (512 bytes for 4 x 64), all on one mbarrier, in distance order.
+// Warp w = head hg * G + w: lane l scores keys l, l + 32, l + 64 (distance order, then the frame's own key) over 16-byte
+// pieces in a rotated order (the 8 lanes of a quarter-warp read 8 distinct bank groups), fp16-rounded dot products
+// scaled in fp32 (decoder_stream.py:172); the softmax runs in the warp, P rounded to fp16 (:173); lane l accumulates
+// dims [l * HD / 32, (l + 1) * HD / 32) of P_ring.V_ring over the visible rows; o = fp16(fp16(ring) + fp16(p_self
+// v_self)) (:174). Shared memory: K and V rows [nv + 1][G][HD], q [G][HD], P [G][nv + 1] floats, one mbarrier.
+template <int HD, int G>
+struct RingHeadsSmem {
+  static constexpr int kRowHalves = G * HD;                  // one staged row: the G heads of one ring slot
+  __host__ __device__ static size_t p_off(int nv) { return static_cast<size_t>(2 * (nv + 1) + 1) * kRowHalves * 2; }
+  __host__ __device__ static size_t bar_off(int nv) { return (p_off(nv) + static_cast<size_t>(G) * (nv + 1) * 4 + 7) & ~size_t(7); }
+  __host__ __device__ static size_t bytes(int nv) { return bar_off(nv) + 8; }
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(32 * G) ring_attn_frame_heads_kernel(const RingArgs a) {
+  using SM = RingHeadsSmem<HD, G>;
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int CH = HD / 8;                                 // 16-byte pieces per head row
+  constexpr int DPL = HD / 32;                               // output dims per lane (2 or 4)
+  const int hg = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int RING = a.ring;
+  const int NV = a.past < RING ? a.past : RING;              // ring rows any frame can see (launch-wide)
+  __half* sK = reinterpret_cast<__half*>(smem);              // [NV + 1][G][HD]
+  __half* sV = sK + (NV + 1) * SM::kRowHalves;
+  __half* sQ = sV + (NV + 1) * SM::kRowHalves;               // [G][HD]
+  float* sP = reinterpret_cast<float*>(smem + SM::p_off(NV)) + w * (NV + 1);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM::bar_off(NV));
+
+  const long long row = a.ring_rows[b];
+  const long long pos = a.pos[b];
+  const long long pm1 = pos - 1;
+  const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+  int nvis = NV;                                             // distance d lives in slot (pos-1-d) mod RING
+  if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
+  const int nk = nvis + 1;                                   // keys: nvis ring rows, then the frame itself
+  constexpr uint32_t kRowBytes = SM::kRowHalves * sizeof(__half);
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(2 * nk + 1) * kRowBytes);
+  }
+  __syncthreads();
+  const long long fo = b * a.qkv_batch_stride + hg * SM::kRowHalves;   // the frame's q / k / v rows of the group
+  const __half* kr = a.k_ring + row * a.ring_stream_stride + hg * SM::kRowHalves;
+  const __half* vr = a.v_ring + row * a.ring_stream_stride + hg * SM::kRowHalves;
+  for (int i = tid; i < 2 * nk + 1; i += 32 * G) {
+    const __half* src;
+    __half* dst;
+    if (i == 2 * nk) {
+      src = a.q + fo;
+      dst = sQ;
+    } else {
+      const int r = i >> 1;
+      const bool v = (i & 1) != 0;
+      if (r < nvis) {
+        int j = pm1_mod - r;
+        if (j < 0) j += RING;
+        src = (v ? vr : kr) + j * a.ring_slot_stride;
+      } else {
+        src = (v ? a.v_new : a.k_new) + fo;
+      }
+      dst = (v ? sV : sK) + r * SM::kRowHalves;
+    }
+    bulk_g2s(dst, src, kRowBytes, bar);
+  }
+  if (!mbar_wait_bounded(bar, 0)) {
+    // the copies did not land in time: flag it, keep the shared memory alive (bounded) until they are done, leave the
+    // outputs untouched
+    if (lane == 0) {
+      atomicOr(a.status, kStatusWaitTimeout);
+      mbar_wait_bounded(bar, 0, 100000000ull);
+    }
+    return;
+  }
+
+  // ---- scores of keys lane, lane + 32, ... : fp16-rounded dot products scaled in fp32
+  const __half* qrow = sQ + w * HD;
+  float sc[3];
+  float m = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < 3; ++u) {
+    const int r = lane + 32 * u;
+    sc[u] = -INFINITY;
+    if (r < nk) {
+      const __half* krow = sK + r * SM::kRowHalves + w * HD;
+      float2 acc0 = make_float2(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+      for (int pc = 0; pc < CH; ++pc) {
+        const int pp = (pc + r) & (CH - 1);
+        const uint4 kw = *reinterpret_cast<const uint4*>(krow + pp * 8);
+        const uint4 qw = *reinterpret_cast<const uint4*>(qrow + pp * 8);
+        const __half2* kh = reinterpret_cast<const __half2*>(&kw);
+        const __half2* qh = reinterpret_cast<const __half2*>(&qw);
+        acc0 = __ffma2_rn(__half22float2(kh[0]), __half22float2(qh[0]), acc0);
+        acc1 = __ffma2_rn(__half22float2(kh[1]), __half22float2(qh[1]), acc1);
+        acc0 = __ffma2_rn(__half22float2(kh[2]), __half22float2(qh[2]), acc0);
+        acc1 = __ffma2_rn(__half22float2(kh[3]), __half22float2(qh[3]), acc1);
+      }
+      sc[u] = round_fp16((acc0.x + acc0.y) + (acc1.x + acc1.y)) * a.scale;
+      m = fmaxf(m, sc[u]);
+    }
+  }
+  m = warp_max(m);
+  // ---- softmax in the warp, P rounded to fp16
+  float e[3], sum = 0.f;
+#pragma unroll
+  for (int u = 0; u < 3; ++u) {
+    e[u] = (lane + 32 * u < nk) ? expf(sc[u] - m) : 0.f;
+    sum += e[u];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv = 1.f / sum;                               // the frame always sees itself: sum > 0
+#pragma unroll
+  for (int u = 0; u < 3; ++u)
+    if (lane + 32 * u < nk) sP[lane + 32 * u] = round_fp16(e[u] * inv);
+  __syncwarp();
+
+  // ---- P_ring.V_ring: lane l owns DPL consecutive dims; o = fp16(fp16(ring) + fp16(p_self * v_self))
+  const int d0 = lane * DPL;
+  float acc[DPL];
+#pragma unroll
+  for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
+  for (int r = 0; r < nvis; ++r) {
+    const float pr = sP[r];
+    const __half* vrow = sV + r * SM::kRowHalves + w * HD + d0;
+    if constexpr (DPL == 2) {
+      const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(vrow));
+      acc[0] = fmaf(pr, v2.x, acc[0]);
+      acc[1] = fmaf(pr, v2.y, acc[1]);
+    } else {
+      const uint2 vw = *reinterpret_cast<const uint2*>(vrow);
+      const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vw.x));
+      const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vw.y));
+      acc[0] = fmaf(pr, v01.x, acc[0]);
+      acc[1] = fmaf(pr, v01.y, acc[1]);
+      acc[2] = fmaf(pr, v23.x, acc[2]);
+      acc[3] = fmaf(pr, v23.y, acc[3]);
+    }
+  }
+  const float pself = sP[nvis];
+  const __half* vself = sV + nvis * SM::kRowHalves + w * HD + d0;
+  __half* op = a.out + b * a.out_batch_stride + (hg * G + w) * HD + d0;
+#pragma unroll
+  for (int j = 0; j < DPL; j += 2) {
+    const float2 vs = __half22float2(*reinterpret_cast<const __half2*>(vself + j));
+    *reinterpret_cast<__half2*>(op + j) = __floats2half2_rn(round_fp16(acc[j]) + round_fp16(pself * vs.x),
+                                                            round_fp16(acc[j + 1]) + round_fp16(pself * vs.y));
+  }
+
+  // ---- the frame's columns into the ring (a slot outside every window of this launch, never staged)
+  if (a.write_new) {
+    const long long slot = ((pos % RING) + RING) % RING;
+    const long long off = row * a.ring_stream_stride + slot * a.ring_slot_stride + (hg * G + w) * HD + d0;
+    const __half* ks = sK + nvis * SM::kRowHalves + w * HD + d0;
+#pragma unroll
+    for (int j = 0; j < DPL; j += 2) {
+      *reinterpret_cast<__half2*>(a.k_ring + off + j) = *reinterpret_cast<const __half2*>(ks + j);
+      *reinterpret_cast<__half2*>(a.v_ring + off + j) = *reinterpret_cast<const __half2*>(vself + j);
+    }
+  }
+}
+
 static size_t frame_smem_bytes(int ring, int past, int hd) {
   const int nv = past < ring ? past : ring;
   return static_cast<size_t>(2 * (nv + 1) + 1) * hd * sizeof(__half) + static_cast<size_t>((nv + 1 + 3) & ~3) * 4 +
@@ -433,6 +601,8 @@ static size_t frame_smem_bytes(int ring, int past, int hd) {
 }
 
 size_t ring_smem_bytes(int ring, int past, int hd, int n) { return RingGeom(ring, past, n).bytes(hd, n); }
+
+int g_ring_frame_kernel = 0;
 
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
   // the shared-memory limits are raised once per device, for the largest ring and chunk supported, so a call made
@@ -452,10 +622,32 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
       e = cudaFuncSetAttribute(ring_attn_frame_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, s64);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(ring_attn_frame_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, s128);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ring_attn_frame_heads_kernel<64, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(RingHeadsSmem<64, 4>::bytes(95)));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ring_attn_frame_heads_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(RingHeadsSmem<128, 2>::bytes(95)));
     if (e != cudaSuccess) return e;
     configured_device = dev;
   }
   if (a.B == 0 || a.n == 0) return cudaSuccess;
+  const int nv = a.past < a.ring ? a.past : a.ring;
+  if (a.n == 1 && g_ring_frame_kernel == 0 && nv <= 95) {
+    // one frame, G heads per CTA (4 x 64 or 2 x 128 halves per staged row); shared memory below 76 KB per CTA
+    const int G = a.hd == 64 ? 4 : 2;
+    if (a.H % G == 0) {
+      const dim3 hgrid(a.H / G, a.B);
+      if (a.hd == 64) {
+        const size_t bytes = RingHeadsSmem<64, 4>::bytes(nv);
+        ring_attn_frame_heads_kernel<64, 4><<<hgrid, 128, bytes, stream>>>(a);
+      } else {
+        const size_t bytes = RingHeadsSmem<128, 2>::bytes(nv);
+        ring_attn_frame_heads_kernel<128, 2><<<hgrid, 64, bytes, stream>>>(a);
+      }
+      return cudaGetLastError();
+    }
+  }
   dim3 grid(a.B, a.H);
   if (a.n == 1) {
     const size_t bytes = frame_smem_bytes(a.ring, a.past, a.hd);

@@ -621,6 +621,12 @@ def _(q, k, v, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, prefi
     return q.new_empty(q.shape[0], NH, HD)
 
 
+def set_ring_frame_kernel(kernel: int) -> int:
+    """Select the one-frame ring attention kernel (0: one warp per head, several heads per CTA, where the heads divide;
+    1: one CTA per (stream, head) always). Returns the previous selection."""
+    return int(_lib.load().q3_set_ring_frame_kernel(int(kernel)))
+
+
 def set_prefill_kernel(kernel: int) -> int:
     """Select the prefill kernel (0: the warp-specialised TMA kernel where the call fits it, else the single-warpgroup
     kernel; 1: the single-warpgroup kernel always). Returns the previous selection."""

@@ -30,7 +30,16 @@ def q3():
     return q3attn
 
 
-@pytest.mark.parametrize("hd,H", [(64, 8), (128, 4)])
+@pytest.fixture(params=[0, 1], ids=["heads_per_cta", "cta_per_head"], autouse=True)
+def ring_frame_kernel(q3, request):
+    """Every test runs on both one-frame kernels: one warp per head with several heads per CTA (default), and one CTA
+    per (stream, head) (used where the heads do not divide)."""
+    prev = q3.set_ring_frame_kernel(request.param)
+    yield request.param
+    q3.set_ring_frame_kernel(prev)
+
+
+@pytest.mark.parametrize("hd,H", [(64, 8), (128, 4), (64, 6), (128, 3)])
 @pytest.mark.parametrize("n", [1, 4, 17])
 def test_ring_attention_matches_oracle(q3, hd, H, n):
     g = synth.cpu_gen(hd + n)
