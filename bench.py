@@ -52,8 +52,12 @@ def parse():
     p.add_argument("--variant", type=int, default=0, help="decode kernel variant (q3_set_decode_variant)")
     p.add_argument("--num-splits", type=int, default=0)
     p.add_argument("--prefill-kernel", type=int, default=0, help="prefill kernel (q3_set_prefill_kernel): 0 TMA, 1 single")
-    p.add_argument("--ring-frame-kernel", type=int, default=0,
-                   help="one-frame ring kernel (q3_set_ring_frame_kernel): 0 heads per CTA, 1 CTA per head")
+    p.add_argument("--ring-frame-kernel", type=int, default=2,
+                   help="one-frame ring kernel (q3_set_ring_frame_kernel): 0 tensor cores 4x64 heads per CTA, "
+                        "3 / 4 the same with 2 / 1 heads, 2 scalar heads per CTA, 1 scalar CTA per head")
+    p.add_argument("--ring-chunk-kernel", type=int, default=1,
+                   help="multi-frame ring kernel (q3_set_ring_chunk_kernel): 0 tensor cores 2x64 heads per CTA, "
+                        "2 / 3 the same with 4 / 1 heads, 1 one CTA per head")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -442,6 +446,7 @@ def bench_aux(a):
     peak, peak_kind = hbm_peak()
     q3attn.set_prefill_kernel(a.prefill_kernel)
     q3attn.set_ring_frame_kernel(a.ring_frame_kernel)
+    q3attn.set_ring_chunk_kernel(a.ring_chunk_kernel)
 
     def timed(fn, n):
         s = torch.cuda.Stream(device=dev)

@@ -616,7 +616,13 @@ int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
 
 int q3_set_ring_frame_kernel(int kernel) {
   const int prev = q3::g_ring_frame_kernel;
-  if (kernel == 0 || kernel == 1) q3::g_ring_frame_kernel = kernel;
+  if (kernel >= 0 && kernel <= 4) q3::g_ring_frame_kernel = kernel;
+  return prev;
+}
+
+int q3_set_ring_chunk_kernel(int kernel) {
+  const int prev = q3::g_ring_chunk_kernel;
+  if (kernel >= 0 && kernel <= 3) q3::g_ring_chunk_kernel = kernel;
   return prev;
 }
 

@@ -201,9 +201,15 @@ struct RingArgs {
 };
 size_t ring_smem_bytes(int ring, int past, int hd, int n);
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);
-// Which one-frame ring kernel launch_ring_attn uses: 0 = one warp per head, G heads per CTA, where the heads divide
-// (default); 1 = the one-CTA-per-(stream, head) kernel always.
+// Which one-frame ring kernel launch_ring_attn uses: 0 = tensor cores, one warp per head, 4 x 64 / 2 x 128 heads per
+// CTA (default); 3 = the same with 2 x 64 / 1 x 128 and 4 = one head per CTA; 2 = scalar math, one warp per head,
+// 4 x 64 / 2 x 128 heads per CTA; 1 = scalar math, one CTA per (stream, head), always (also where the heads do not
+// divide).
 extern int g_ring_frame_kernel;
+// Which kernel runs chunks of 2 .. 16 frames: 0 = tensor cores, one warp per head, 2 x 64 / 1 x 128 heads per CTA
+// (default); 2 = 4 x 64 / 2 x 128; 3 = one head per CTA; 1 = one CTA per (stream, head) (also for 17 frames and where
+// the heads do not divide).
+extern int g_ring_chunk_kernel;
 
 struct PrefillArgs {
   const __nv_bfloat16* q;          // [Tq, 16, 128] rows, row stride q_stride (elements)

@@ -594,6 +594,475 @@ __global__ void __launch_bounds__(32 * G) ring_attn_frame_heads_kernel(const Rin
   }
 }
 
+// One query frame on the tensor cores, G heads per CTA, one warp per head. The staging is that of
+// ring_attn_frame_heads_kernel (ring rows of the G heads by distance, then the frame's row; one bulk copy per row),
+// except that K (with q) and V complete on two mbarriers, so scores and softmax run while V lands, and that each
+// staged row is padded by 16 bytes: the 8 rows an ldmatrix reads at one column offset then sit in 8 distinct bank
+// groups. Per warp (head w), with the query as row 0 of a 16-row A operand (rows 1-15 zero):
+//   S = q.K^T      mma.sync m16n8k16 over 8-key tiles, K fragments by ldmatrix.x4 (4 x 8 dims of 8 keys);
+//   softmax        on the lanes holding row 0 (lanes 0-3, two keys per tile each): fp16-rounded scores scaled in
+//                  fp32 (decoder_stream.py:172), P rounded to fp16 (:173);
+//   O = P_ring.V   mma.sync over 16-key steps with P taken straight from the score fragments (a tile's C layout is
+//                  the next contraction's A layout) and V fragments by ldmatrix.x4.trans; the frame's own key enters
+//                  as fp16(p_self v_self) (:174).
+// Key rows past the staged ones read a 16-byte zero row instead (ldmatrix takes one row address per lane), so no
+// padding rows are copied or cleared, and a zero probability never meets stale shared memory.
+template <int HD, int G>
+struct RingMmaSmem {
+  static constexpr int kRB = G * HD * 2;                     // bytes of a staged row: the G heads of one slot
+  static constexpr int kRS = kRB + 16;                       // row stride in shared memory
+  __host__ __device__ static size_t v_off(int nk) { return static_cast<size_t>(nk) * kRS; }
+  __host__ __device__ static size_t q_off(int nk) { return 2 * static_cast<size_t>(nk) * kRS; }
+  __host__ __device__ static size_t zero_off(int nk) { return q_off(nk) + kRB; }
+  __host__ __device__ static size_t bar_off(int nk) { return zero_off(nk) + 16; }
+  __host__ __device__ static size_t bytes(int nk) { return bar_off(nk) + 16; }
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+constexpr int kRingMmaMaxKeys = 96;                          // key tiles of 8 held in registers: 12
+
+template <int HD, int G>
+__global__ void __launch_bounds__(32 * G) ring_attn_frame_mma_kernel(const RingArgs a) {
+  using SM = RingMmaSmem<HD, G>;
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int RB = SM::kRB, RS = SM::kRS;
+  constexpr int NT = kRingMmaMaxKeys / 8;                    // score tiles (upper bound)
+  constexpr int NTO = HD / 8;                                // output tiles of 8 dims
+  const int hg = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int t4 = lane & 3;
+  const int RING = a.ring;
+  const int NV = a.past < RING ? a.past : RING;              // ring rows any frame can see (launch-wide)
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + SM::v_off(NV + 1);
+  uint8_t* sQ = smem + SM::q_off(NV + 1);
+  uint8_t* sZero = smem + SM::zero_off(NV + 1);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM::bar_off(NV + 1));   // [0]: q and K rows, [1]: V rows
+
+  const long long row = a.ring_rows[b];
+  const long long pos = a.pos[b];
+  const long long pm1 = pos - 1;
+  const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+  int nvis = NV;                                             // distance d lives in slot (pos-1-d) mod RING
+  if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
+  const int nk = nvis + 1;                                   // keys: nvis ring rows, then the frame itself
+
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&bar[0], static_cast<uint32_t>(nk + 1) * RB);
+    mbar_arrive_expect_tx(&bar[1], static_cast<uint32_t>(nk) * RB);
+  }
+  if (tid < 4) reinterpret_cast<uint32_t*>(sZero)[tid] = 0u;
+  __syncthreads();
+  const long long fo = b * a.qkv_batch_stride + hg * (G * HD);   // the frame's q / k / v rows of the group
+  const __half* kr = a.k_ring + row * a.ring_stream_stride + hg * (G * HD);
+  const __half* vr = a.v_ring + row * a.ring_stream_stride + hg * (G * HD);
+  for (int i = tid; i < 2 * nk + 1; i += 32 * G) {           // q, then the K rows, then the V rows
+    if (i == 0) {
+      bulk_g2s(sQ, a.q + fo, RB, &bar[0]);
+    } else {
+      const bool v = i > nk;
+      const int r = v ? i - 1 - nk : i - 1;
+      const __half* src;
+      if (r < nvis) {
+        int j = pm1_mod - r;
+        if (j < 0) j += RING;
+        src = (v ? vr : kr) + j * a.ring_slot_stride;
+      } else {
+        src = (v ? a.v_new : a.k_new) + fo;
+      }
+      bulk_g2s((v ? sV : sK) + r * RS, src, RB, &bar[v ? 1 : 0]);
+    }
+  }
+  auto give_up = [&]() {
+    // the copies did not land in time: flag it, keep the shared memory alive (bounded) until they are done, leave
+    // the outputs untouched
+    if (lane == 0) {
+      atomicOr(a.status, kStatusWaitTimeout);
+      mbar_wait_bounded(&bar[0], 0, 100000000ull);
+      mbar_wait_bounded(&bar[1], 0, 100000000ull);
+    }
+  };
+  if (!mbar_wait_bounded(&bar[0], 0)) {
+    give_up();
+    return;
+  }
+
+  const uint32_t zero_addr = smem_addr(sZero);
+  const uint32_t k_base = smem_addr(sK) + w * HD * 2;
+  const uint32_t v_base = smem_addr(sV) + w * HD * 2;
+  const int nt = (nk + 7) >> 3;
+
+  // ---- S = q.K^T on the tensor cores: A rows 1-15 are zero, so only lanes 0-3 carry q (row 0)
+  uint32_t qa[HD / 16][2];
+#pragma unroll
+  for (int ks = 0; ks < HD / 16; ++ks) {
+    const uint32_t* qw = reinterpret_cast<const uint32_t*>(sQ + w * HD * 2 + ks * 32);
+    qa[ks][0] = lane < 4 ? qw[t4] : 0u;                      // dims 16ks + 2t4, +1
+    qa[ks][1] = lane < 4 ? qw[4 + t4] : 0u;                  // dims 16ks + 8 + 2t4, +1
+  }
+  float s[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    if (j < nt) {
+      const int key = 8 * j + (lane & 7);
+      const uint32_t ra = k_base + key * RS + (lane >> 3) * 16;
+#pragma unroll
+      for (int kp = 0; kp < HD / 32; ++kp) {                 // 32 dims (two k-steps) per ldmatrix.x4
+        uint32_t bf[4];
+        ldsm_x4(key < nk ? ra + kp * 64 : zero_addr, bf);
+        mma_f16(s[j], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, bf[0], bf[1]);
+        mma_f16(s[j], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, bf[2], bf[3]);
+      }
+    }
+  }
+
+  // ---- softmax over row 0 (lanes 0-3 hold keys 8j + 2t4, +1 of every tile j); P rounded to fp16
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int key = 8 * j + 2 * t4 + e;
+      const float x = (j < nt && key < nk) ? round_fp16(s[j][e]) * a.scale : -INFINITY;
+      s[j][e] = x;
+      m = fmaxf(m, x);
+    }
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float x = (j < nt) ? expf(s[j][e] - m) : 0.f;   // masked keys: exp(-inf) = 0
+      s[j][e] = x;
+      sum += x;
+    }
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  const float inv = 1.f / sum;                               // the frame always sees itself: sum > 0 (lanes 0-3)
+  float pmine = 0.f;
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int key = 8 * j + 2 * t4 + e;
+      float p = round_fp16(s[j][e] * inv);
+      if (key == nvis) {                                     // the frame's own key: kept apart from the ring sum
+        pmine = p;
+        p = 0.f;
+      }
+      s[j][e] = lane < 4 ? p : 0.f;                          // rows 1-15 of the P operand are zero
+    }
+  const float pself = __shfl_sync(0xffffffffu, pmine, (nvis & 7) >> 1);
+
+  if (!mbar_wait_bounded(&bar[1], 0)) {
+    give_up();
+    return;
+  }
+  // ---- O_ring = P_ring.V_ring: 16-key steps; ldmatrix.x4.trans gives the V fragments of two 8-dim tiles
+  float o[NTO][4];
+#pragma unroll
+  for (int jn = 0; jn < NTO; ++jn) o[jn][0] = o[jn][1] = o[jn][2] = o[jn][3] = 0.f;
+  const int ksteps = (nk + 15) >> 4;
+#pragma unroll
+  for (int kk = 0; kk < NT / 2; ++kk) {
+    if (kk < ksteps) {
+      const uint32_t pa0 = pack_half2(s[2 * kk][0], s[2 * kk][1]);        // keys 16kk + 2t4, +1
+      const uint32_t pa2 = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);  // keys 16kk + 8 + 2t4, +1
+      const int key = 16 * kk + ((lane >> 3) & 1) * 8 + (lane & 7);
+      const uint32_t ra = v_base + key * RS + (lane >> 4) * 16;
+#pragma unroll
+      for (int np = 0; np < NTO / 2; ++np) {
+        uint32_t bf[4];
+        ldsm_x4_trans(key < nk ? ra + np * 32 : zero_addr, bf);
+        mma_f16(o[2 * np], pa0, 0u, pa2, 0u, bf[0], bf[1]);
+        mma_f16(o[2 * np + 1], pa0, 0u, pa2, 0u, bf[2], bf[3]);
+      }
+    }
+  }
+
+  // ---- o = fp16(fp16(ring) + fp16(p_self v_self)): lanes 0-3 hold dims 8jn + 2t4, +1
+  if (lane < 4) {
+    const __half* vself = reinterpret_cast<const __half*>(sV + nvis * RS) + w * HD;
+    __half* op = a.out + b * a.out_batch_stride + (hg * G + w) * HD;
+#pragma unroll
+    for (int jn = 0; jn < NTO; ++jn) {
+      const int d = 8 * jn + 2 * t4;
+      const float2 vs = __half22float2(*reinterpret_cast<const __half2*>(vself + d));
+      *reinterpret_cast<__half2*>(op + d) = __floats2half2_rn(round_fp16(o[jn][0]) + round_fp16(pself * vs.x),
+                                                              round_fp16(o[jn][1]) + round_fp16(pself * vs.y));
+    }
+  }
+
+  // ---- the frame's columns into the ring (a slot outside every window of this launch, never staged)
+  if (a.write_new) {
+    constexpr int DPL = HD / 32;
+    const long long slot = ((pos % RING) + RING) % RING;
+    const long long off = row * a.ring_stream_stride + slot * a.ring_slot_stride + (hg * G + w) * HD + lane * DPL;
+    const __half* ks = reinterpret_cast<const __half*>(sK + nvis * RS) + w * HD + lane * DPL;
+    const __half* vs = reinterpret_cast<const __half*>(sV + nvis * RS) + w * HD + lane * DPL;
+#pragma unroll
+    for (int j = 0; j < DPL; j += 2) {
+      *reinterpret_cast<__half2*>(a.k_ring + off + j) = *reinterpret_cast<const __half2*>(ks + j);
+      *reinterpret_cast<__half2*>(a.v_ring + off + j) = *reinterpret_cast<const __half2*>(vs + j);
+    }
+  }
+}
+
+// A chunk of 2 .. 16 frames on the tensor cores, G heads per CTA, one warp per head: the design of
+// ring_attn_frame_mma_kernel with the n query rows as rows 0 .. n-1 of the A operand (Q fragments by ldmatrix.x4 from
+// padded rows, rows past n read the zero row). Each lane holds rows g and g + 8 of every score tile and applies the
+// row's own mask in registers: ring row d is visible to query i when d < nvis and d <= past - 1 - i
+// (decoder_stream.py:152-155), the chunk's key jj when jj <= i (:156). The two halves of the output are two tensor-core
+// passes over the same V fragments, P restricted to the ring keys, then to the chunk's keys, each rounded to fp16
+// before the sum (:173-175).
+template <int HD, int G>
+struct RingChunkSmem {
+  static constexpr int kRB = G * HD * 2;                     // bytes of a staged row: the G heads of one slot / frame
+  static constexpr int kRS = kRB + 16;                       // row stride in shared memory (bank-group rotation)
+  __host__ __device__ static size_t v_off(int nk) { return static_cast<size_t>(nk) * kRS; }
+  __host__ __device__ static size_t q_off(int nk) { return 2 * static_cast<size_t>(nk) * kRS; }
+  __host__ __device__ static size_t zero_off(int nk, int n) { return q_off(nk) + static_cast<size_t>(n) * kRS; }
+  __host__ __device__ static size_t bar_off(int nk, int n) { return zero_off(nk, n) + 16; }
+  __host__ __device__ static size_t bytes(int nk, int n) { return bar_off(nk, n) + 16; }
+};
+
+constexpr int kRingChunkMaxKeys = 112;                       // ring rows + chunk keys held as score tiles: 14 x 8
+constexpr int kRingChunkMaxFrames = 16;                      // one 16-row query tile
+
+template <int HD, int G>
+__global__ void __launch_bounds__(32 * G) ring_attn_chunk_mma_kernel(const RingArgs a) {
+  using SM = RingChunkSmem<HD, G>;
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int RB = SM::kRB, RS = SM::kRS;
+  constexpr int NT = kRingChunkMaxKeys / 8;                  // score tiles (upper bound)
+  constexpr int NTO = HD / 8;                                // output tiles of 8 dims
+  const int hg = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int n = a.n, RING = a.ring, PAST = a.past;
+  const int NV = PAST < RING ? PAST : RING;                  // ring rows any frame can see (launch-wide)
+  const int NKL = NV + n;
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + SM::v_off(NKL);
+  uint8_t* sQ = smem + SM::q_off(NKL);
+  uint8_t* sZero = smem + SM::zero_off(NKL, n);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM::bar_off(NKL, n));   // [0]: q and K rows, [1]: V rows
+
+  const long long row = a.ring_rows[b];
+  const long long pos = a.pos[b];
+  const long long pm1 = pos - 1;
+  const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+  int nvis = NV;                                             // distance d lives in slot (pos-1-d) mod RING
+  if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
+  const int nk = nvis + n;                                   // keys: nvis ring rows, then the chunk's n frames
+
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&bar[0], static_cast<uint32_t>(n + nk) * RB);
+    mbar_arrive_expect_tx(&bar[1], static_cast<uint32_t>(nk) * RB);
+  }
+  if (tid < 4) reinterpret_cast<uint32_t*>(sZero)[tid] = 0u;
+  __syncthreads();
+  const long long fo = b * a.qkv_batch_stride + hg * (G * HD);   // frame 0's q / k / v rows of the group
+  const __half* kr = a.k_ring + row * a.ring_stream_stride + hg * (G * HD);
+  const __half* vr = a.v_ring + row * a.ring_stream_stride + hg * (G * HD);
+  for (int i = tid; i < n + 2 * nk; i += 32 * G) {           // the q rows, then the K rows, then the V rows
+    if (i < n) {
+      bulk_g2s(sQ + i * RS, a.q + fo + i * a.qkv_frame_stride, RB, &bar[0]);
+    } else {
+      const bool v = i >= n + nk;
+      const int r = v ? i - n - nk : i - n;
+      const __half* src;
+      if (r < nvis) {
+        int j = pm1_mod - r;
+        if (j < 0) j += RING;
+        src = (v ? vr : kr) + j * a.ring_slot_stride;
+      } else {
+        src = (v ? a.v_new : a.k_new) + fo + (r - nvis) * a.qkv_frame_stride;
+      }
+      bulk_g2s((v ? sV : sK) + r * RS, src, RB, &bar[v ? 1 : 0]);
+    }
+  }
+  auto give_up = [&]() {
+    if (lane == 0) {
+      atomicOr(a.status, kStatusWaitTimeout);
+      mbar_wait_bounded(&bar[0], 0, 100000000ull);
+      mbar_wait_bounded(&bar[1], 0, 100000000ull);
+    }
+  };
+  if (!mbar_wait_bounded(&bar[0], 0)) {
+    give_up();
+    return;
+  }
+
+  const uint32_t zero_addr = smem_addr(sZero);
+  const uint32_t k_base = smem_addr(sK) + w * HD * 2;
+  const uint32_t v_base = smem_addr(sV) + w * HD * 2;
+  const int nt = (nk + 7) >> 3;
+
+  // ---- Q fragments (rows 0 .. n-1 real) for every 16-dim step
+  uint32_t qa[HD / 16][4];
+  {
+    const int qr = ((lane >> 3) & 1) * 8 + (lane & 7);
+    const uint32_t qaddr = smem_addr(sQ) + qr * RS + w * HD * 2 + (lane >> 4) * 16;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) ldsm_x4(qr < n ? qaddr + ks * 32 : zero_addr, qa[ks]);
+  }
+  // ---- S = Q.K^T
+  float s[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    if (j < nt) {
+      const int key = 8 * j + (lane & 7);
+      const uint32_t ra = k_base + key * RS + (lane >> 3) * 16;
+#pragma unroll
+      for (int kp = 0; kp < HD / 32; ++kp) {
+        uint32_t bf[4];
+        ldsm_x4(key < nk ? ra + kp * 64 : zero_addr, bf);
+        mma_f16(s[j], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], bf[0], bf[1]);
+        mma_f16(s[j], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2], qa[2 * kp + 1][3], bf[2], bf[3]);
+      }
+    }
+  }
+
+  // ---- masked softmax of rows g (elements 0, 1) and g + 8 (elements 2, 3) across the lane quad; P rounded to fp16
+  float m[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = g + (e >> 1) * 8, c = 8 * j + 2 * t4 + (e & 1);
+      const bool ok = j < nt && i < n && c < nk && (c < nvis ? c <= PAST - 1 - i : c - nvis <= i);
+      const float x = ok ? round_fp16(s[j][e]) * a.scale : -INFINITY;
+      s[j][e] = x;
+      m[e >> 1] = fmaxf(m[e >> 1], x);
+    }
+  float sum[2];
+#pragma unroll
+  for (int h2 = 0; h2 < 2; ++h2) {
+    m[h2] = fmaxf(m[h2], __shfl_xor_sync(0xffffffffu, m[h2], 1));
+    m[h2] = fmaxf(m[h2], __shfl_xor_sync(0xffffffffu, m[h2], 2));
+    sum[h2] = 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float x = s[j][e] == -INFINITY ? 0.f : expf(s[j][e] - m[e >> 1]);   // rows past n: all masked
+      s[j][e] = x;
+      sum[e >> 1] += x;
+    }
+  float inv[2];
+#pragma unroll
+  for (int h2 = 0; h2 < 2; ++h2) {
+    sum[h2] += __shfl_xor_sync(0xffffffffu, sum[h2], 1);
+    sum[h2] += __shfl_xor_sync(0xffffffffu, sum[h2], 2);
+    inv[h2] = sum[h2] > 0.f ? 1.f / sum[h2] : 0.f;           // a real query always sees itself
+  }
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s[j][e] = round_fp16(s[j][e] * inv[e >> 1]);
+
+  if (!mbar_wait_bounded(&bar[1], 0)) {
+    give_up();
+    return;
+  }
+  // ---- O_ring = P_ring.V over the 16-key steps holding ring rows, then O_new = P_new.V over those holding the chunk's
+  //      keys; the same ldmatrix.x4.trans V fragments, P restricted by key index
+  float o[NTO][4];
+  uint32_t oring[NTO][2];                                    // fp16(O_ring), rows g and g + 8
+  const int ks_ring = (nvis + 15) >> 4, ks_first_new = nvis >> 4, ks_end = (nk + 15) >> 4;
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll
+    for (int jn = 0; jn < NTO; ++jn) o[jn][0] = o[jn][1] = o[jn][2] = o[jn][3] = 0.f;
+    const int k_lo = pass == 0 ? 0 : ks_first_new, k_hi = pass == 0 ? ks_ring : ks_end;
+#pragma unroll
+    for (int kk = 0; kk < NT / 2; ++kk) {
+      if (kk >= k_lo && kk < k_hi) {
+        uint32_t pa[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {                        // a0a1: row g, keys +2t4; a2a3: row g+8; a4..a7: keys +8
+          const int j = 2 * kk + (r >> 1), e0 = (r & 1) * 2;
+          const int c = 8 * j + 2 * t4;
+          const bool in0 = pass == 0 ? c < nvis : c >= nvis, in1 = pass == 0 ? c + 1 < nvis : c + 1 >= nvis;
+          pa[r] = pack_half2(in0 ? s[j][e0] : 0.f, in1 ? s[j][e0 + 1] : 0.f);
+        }
+        const int key = 16 * kk + ((lane >> 3) & 1) * 8 + (lane & 7);
+        const uint32_t ra = v_base + key * RS + (lane >> 4) * 16;
+#pragma unroll
+        for (int np = 0; np < NTO / 2; ++np) {
+          uint32_t bf[4];
+          ldsm_x4_trans(key < nk ? ra + np * 32 : zero_addr, bf);
+          mma_f16(o[2 * np], pa[0], pa[1], pa[2], pa[3], bf[0], bf[1]);
+          mma_f16(o[2 * np + 1], pa[0], pa[1], pa[2], pa[3], bf[2], bf[3]);
+        }
+      }
+    }
+    if (pass == 0) {
+#pragma unroll
+      for (int jn = 0; jn < NTO; ++jn) {
+        oring[jn][0] = pack_half2(o[jn][0], o[jn][1]);
+        oring[jn][1] = pack_half2(o[jn][2], o[jn][3]);
+      }
+    }
+  }
+  // ---- o = fp16(fp16(O_ring) + fp16(O_new)) for rows g, g + 8 below n
+#pragma unroll
+  for (int h2 = 0; h2 < 2; ++h2) {
+    const int i = g + 8 * h2;
+    if (i < n) {
+      __half* op = a.out + b * a.out_batch_stride + i * a.out_frame_stride + (hg * G + w) * HD + 2 * t4;
+#pragma unroll
+      for (int jn = 0; jn < NTO; ++jn) {
+        const float2 r = __half22float2(*reinterpret_cast<const __half2*>(&oring[jn][h2]));
+        *reinterpret_cast<__half2*>(op + 8 * jn) =
+            __floats2half2_rn(r.x + round_fp16(o[jn][2 * h2]), r.y + round_fp16(o[jn][2 * h2 + 1]));
+      }
+    }
+  }
+
+  // ---- the chunk's columns into ring slots (pos + jj) % RING (outside every window of this launch, never staged)
+  if (a.write_new) {
+    constexpr int DPL = HD / 32;
+    for (int jj = 0; jj < n; ++jj) {
+      const long long slot = (((pos + jj) % RING) + RING) % RING;
+      const long long off = row * a.ring_stream_stride + slot * a.ring_slot_stride + (hg * G + w) * HD + lane * DPL;
+      const __half* ks = reinterpret_cast<const __half*>(sK + (nvis + jj) * RS) + w * HD + lane * DPL;
+      const __half* vs = reinterpret_cast<const __half*>(sV + (nvis + jj) * RS) + w * HD + lane * DPL;
+#pragma unroll
+      for (int j = 0; j < DPL; j += 2) {
+        *reinterpret_cast<__half2*>(a.k_ring + off + j) = *reinterpret_cast<const __half2*>(ks + j);
+        *reinterpret_cast<__half2*>(a.v_ring + off + j) = *reinterpret_cast<const __half2*>(vs + j);
+      }
+    }
+  }
+}
+
 static size_t frame_smem_bytes(int ring, int past, int hd) {
   const int nv = past < ring ? past : ring;
   return static_cast<size_t>(2 * (nv + 1) + 1) * hd * sizeof(__half) + static_cast<size_t>((nv + 1 + 3) & ~3) * 4 +
@@ -602,7 +1071,32 @@ static size_t frame_smem_bytes(int ring, int past, int hd) {
 
 size_t ring_smem_bytes(int ring, int past, int hd, int n) { return RingGeom(ring, past, n).bytes(hd, n); }
 
-int g_ring_frame_kernel = 0;
+int g_ring_frame_kernel = 2;
+int g_ring_chunk_kernel = 1;
+
+template <int HD, int G>
+static cudaError_t set_mma_frame_smem() {
+  return cudaFuncSetAttribute(ring_attn_frame_mma_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(RingMmaSmem<HD, G>::bytes(kRingMmaMaxKeys)));
+}
+
+template <int HD, int G>
+static cudaError_t launch_mma_frame(dim3 grid, int nv, const RingArgs& a, cudaStream_t stream) {
+  ring_attn_frame_mma_kernel<HD, G><<<grid, 32 * G, RingMmaSmem<HD, G>::bytes(nv + 1), stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <int HD, int G>
+static cudaError_t set_chunk_smem() {
+  return cudaFuncSetAttribute(ring_attn_chunk_mma_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(RingChunkSmem<HD, G>::bytes(kRingChunkMaxKeys, kRingChunkMaxFrames)));
+}
+
+template <int HD, int G>
+static cudaError_t launch_chunk(dim3 grid, int nv, const RingArgs& a, cudaStream_t stream) {
+  ring_attn_chunk_mma_kernel<HD, G><<<grid, 32 * G, RingChunkSmem<HD, G>::bytes(nv + a.n, a.n), stream>>>(a);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
   // the shared-memory limits are raised once per device, for the largest ring and chunk supported, so a call made
@@ -628,13 +1122,57 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(ring_attn_frame_heads_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(RingHeadsSmem<128, 2>::bytes(95)));
+    if (e == cudaSuccess) e = set_mma_frame_smem<64, 4>();
+    if (e == cudaSuccess) e = set_mma_frame_smem<64, 2>();
+    if (e == cudaSuccess) e = set_mma_frame_smem<64, 1>();
+    if (e == cudaSuccess) e = set_mma_frame_smem<128, 2>();
+    if (e == cudaSuccess) e = set_mma_frame_smem<128, 1>();
+    if (e == cudaSuccess) e = set_chunk_smem<64, 4>();
+    if (e == cudaSuccess) e = set_chunk_smem<64, 2>();
+    if (e == cudaSuccess) e = set_chunk_smem<64, 1>();
+    if (e == cudaSuccess) e = set_chunk_smem<128, 2>();
+    if (e == cudaSuccess) e = set_chunk_smem<128, 1>();
     if (e != cudaSuccess) return e;
     configured_device = dev;
   }
   if (a.B == 0 || a.n == 0) return cudaSuccess;
   const int nv = a.past < a.ring ? a.past : a.ring;
-  if (a.n == 1 && g_ring_frame_kernel == 0 && nv <= 95) {
-    // one frame, G heads per CTA (4 x 64 or 2 x 128 halves per staged row); shared memory below 76 KB per CTA
+  if (a.n == 1 && nv < kRingMmaMaxKeys) {
+    // one frame on the tensor cores, G heads per CTA: 4 x 64 or 2 x 128 halves per staged row (selection 0; 3 and 4
+    // take fewer heads per CTA); under 75 KB of shared memory per CTA at 71 visible rows, so three CTAs per SM
+    const int sel = g_ring_frame_kernel;
+    if (sel == 0 || sel == 3 || sel == 4) {
+      const int G = sel == 4 ? 1 : (sel == 3 ? (a.hd == 64 ? 2 : 1) : (a.hd == 64 ? 4 : 2));
+      if (a.H % G == 0) {
+        const dim3 mgrid(a.H / G, a.B);
+        if (a.hd == 64) {
+          if (G == 4) return launch_mma_frame<64, 4>(mgrid, nv, a, stream);
+          if (G == 2) return launch_mma_frame<64, 2>(mgrid, nv, a, stream);
+          return launch_mma_frame<64, 1>(mgrid, nv, a, stream);
+        }
+        if (G == 2) return launch_mma_frame<128, 2>(mgrid, nv, a, stream);
+        return launch_mma_frame<128, 1>(mgrid, nv, a, stream);
+      }
+    }
+  }
+  if (a.n >= 2 && a.n <= kRingChunkMaxFrames && nv + a.n <= kRingChunkMaxKeys && g_ring_chunk_kernel != 1) {
+    // 2 .. 16 frames on the tensor cores, G heads per CTA: 2 x 64 / 1 x 128 (selection 0), 4 x 64 / 2 x 128 (2),
+    // one head (3)
+    const int sel = g_ring_chunk_kernel;
+    const int G = sel == 3 ? 1 : (sel == 2 ? (a.hd == 64 ? 4 : 2) : (a.hd == 64 ? 2 : 1));
+    if (a.H % G == 0) {
+      const dim3 cgrid(a.H / G, a.B);
+      if (a.hd == 64) {
+        if (G == 4) return launch_chunk<64, 4>(cgrid, nv, a, stream);
+        if (G == 2) return launch_chunk<64, 2>(cgrid, nv, a, stream);
+        return launch_chunk<64, 1>(cgrid, nv, a, stream);
+      }
+      if (G == 2) return launch_chunk<128, 2>(cgrid, nv, a, stream);
+      return launch_chunk<128, 1>(cgrid, nv, a, stream);
+    }
+  }
+  if (a.n == 1 && g_ring_frame_kernel == 2 && nv <= 95) {
+    // one frame, scalar math, G heads per CTA (4 x 64 or 2 x 128 halves per staged row)
     const int G = a.hd == 64 ? 4 : 2;
     if (a.H % G == 0) {
       const dim3 hgrid(a.H / G, a.B);

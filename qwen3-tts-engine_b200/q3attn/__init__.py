@@ -10,7 +10,7 @@ from . import _lib, ops  # noqa: F401
 from .flash_api import cp_attn, cp_step, flash_attn_func, flash_attn_varlen_func, flash_attn_with_kvcache  # noqa: F401
 from .ops import (SamplerRng, add_rms_norm, cp_step_qkv, kv_append_paged, kv_append_slots,  # noqa: F401
                   paged_decode, paged_decode_append, paged_decode_qkv, prefill, prefill_paged, qk_norm_rope_,
-                  ring_window_attn, sample_topk, set_decode_variant, set_prefill_kernel, set_ring_frame_kernel,
-                  silu_mul)
+                  ring_window_attn, sample_topk, set_decode_variant, set_prefill_kernel, set_ring_chunk_kernel,
+                  set_ring_frame_kernel, silu_mul)
 
 __version__ = "0.1.0"

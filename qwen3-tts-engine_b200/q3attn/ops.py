@@ -622,9 +622,18 @@ def _(q, k, v, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, prefi
 
 
 def set_ring_frame_kernel(kernel: int) -> int:
-    """Select the one-frame ring attention kernel (0: one warp per head, several heads per CTA, where the heads divide;
-    1: one CTA per (stream, head) always). Returns the previous selection."""
+    """Select the one-frame ring attention kernel. 0: tensor cores, one warp per head, 4 x 64 or 2 x 128 heads per
+    CTA; 3: the same with 2 x 64 or 1 x 128; 4: one head per CTA; 2: scalar math, one warp per head, 4 x 64 or
+    2 x 128 heads per CTA; 1: scalar math, one CTA per (stream, head), always. Where the heads do not divide, 1 is
+    used. Returns the previous selection."""
     return int(_lib.load().q3_set_ring_frame_kernel(int(kernel)))
+
+
+def set_ring_chunk_kernel(kernel: int) -> int:
+    """Select the ring attention kernel for chunks of 2 .. 16 frames. 0: tensor cores, one warp per head, 2 x 64 or
+    1 x 128 heads per CTA; 2: 4 x 64 or 2 x 128; 3: one head per CTA; 1: one CTA per (stream, head), always (also for
+    17 frames and where the heads do not divide). Returns the previous selection."""
+    return int(_lib.load().q3_set_ring_chunk_kernel(int(kernel)))
 
 
 def set_prefill_kernel(kernel: int) -> int:

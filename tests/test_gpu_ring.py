@@ -30,17 +30,28 @@ def q3():
     return q3attn
 
 
-@pytest.fixture(params=[0, 1], ids=["heads_per_cta", "cta_per_head"], autouse=True)
-def ring_frame_kernel(q3, request):
-    """Every test runs on both one-frame kernels: one warp per head with several heads per CTA (default), and one CTA
-    per (stream, head) (used where the heads do not divide)."""
-    prev = q3.set_ring_frame_kernel(request.param)
+# (one-frame kernel, multi-frame kernel) pairs; together they cover every selection of both
+RING_KERNELS = [(0, 0), (1, 1), (2, 2), (3, 3), (4, 0)]
+
+
+@pytest.fixture(params=RING_KERNELS, ids=["mma_default", "cta_per_head", "heads_wide", "heads_narrow", "mma_one"],
+                autouse=True)
+def ring_kernels(q3, request):
+    """Every test runs on each kernel selection. One frame: 0 = tensor cores with 4 x 64 / 2 x 128 heads per CTA
+    (default), 3 = 2 x 64 / 1 x 128, 4 = one head per CTA, 2 = scalar math with one warp per head, 1 = one CTA per
+    (stream, head). Chunks of 2 .. 16 frames: 0 = tensor cores with 2 x 64 / 1 x 128 heads per CTA (default),
+    2 = 4 x 64 / 2 x 128, 3 = one head per CTA, 1 = one CTA per (stream, head). Heads that do not divide fall back
+    to one CTA per (stream, head), and 17 frames always do."""
+    frame, chunk = request.param
+    prev_f = q3.set_ring_frame_kernel(frame)
+    prev_c = q3.set_ring_chunk_kernel(chunk)
     yield request.param
-    q3.set_ring_frame_kernel(prev)
+    q3.set_ring_frame_kernel(prev_f)
+    q3.set_ring_chunk_kernel(prev_c)
 
 
 @pytest.mark.parametrize("hd,H", [(64, 8), (128, 4), (64, 6), (128, 3)])
-@pytest.mark.parametrize("n", [1, 4, 17])
+@pytest.mark.parametrize("n", [1, 2, 4, 16, 17])
 def test_ring_attention_matches_oracle(q3, hd, H, n):
     g = synth.cpu_gen(hd + n)
     pos = torch.tensor([0, 1, 5, 70, 71, 72, 87, 88, 150, 1000], dtype=torch.int64)
@@ -108,7 +119,7 @@ def test_decoder_transformer_matches_reference_stream(q3, golden_dir):
 
 
 @pytest.mark.parametrize("hd,H", [(64, 8), (128, 4)])
-@pytest.mark.parametrize("n", [1, 4])
+@pytest.mark.parametrize("n", [1, 4, 16])
 def test_ring_slots_no_query_sees_are_never_used(q3, hd, H, n):
     """Ring slots outside every query's window (never written yet, or older than the window) may hold anything, NaN
     included: the outputs equal those computed with the same slots zeroed."""
