@@ -69,8 +69,9 @@ int q3_paged_decode(const void* q, int64_t q_batch_stride,
                     void* stream);
 /* Kernel variant used by q3_paged_decode: 0 = 8-token chunks x 3 stages, two CTAs per SM (default),
  * 1 = 16-token chunks x 3 stages, one CTA per SM, 2 = 8-token chunks x 2 stages, two CTAs per SM,
- * 3 / 4 = warp-MMA scoring (mma.sync) with early stage release, 8-token chunks x 3 / 2 stages, two CTAs per SM.
- * Values outside 0..4 leave the selection unchanged. Returns the previous value. No reference counterpart (a tuning
+ * 3 / 4 = warp-MMA scoring (mma.sync) with early stage release, 8-token chunks x 3 / 2 stages, two CTAs per SM,
+ * 5 = dedicated producer warps: one 20-warp CTA per SM running two 8-token x 3-stage chunk streams.
+ * Values outside 0..5 leave the selection unchanged. Returns the previous value. No reference counterpart (a tuning
  * knob of this library). */
 int q3_set_decode_variant(int variant);
 /* CTAs of the given decode variant that the runtime can keep resident on one SM of the current device. */

@@ -141,7 +141,7 @@ int q3_read_status(uint32_t* status_out, int clear) {
 
 int q3_set_decode_variant(int variant) {
   const int prev = g_decode_variant;
-  if (variant >= 0 && variant <= 4) g_decode_variant = variant;
+  if (variant >= 0 && variant <= 5) g_decode_variant = variant;
   return prev;
 }
 

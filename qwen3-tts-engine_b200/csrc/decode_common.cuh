@@ -142,6 +142,110 @@ struct DecodePlan {
   SeatCursor cur;    // positioned on the seat holding chunk c0
 };
 
+// Work split of CTAs that each run NS chunk streams (the dedicated-producer kernel): stream v of block x is split slot
+// c = NS * x + v of G, the grid's stream count. decode_plan below is the one-stream form, kept separate so the
+// register allocation of the one-stream kernels does not carry the per-stream arrays. Every thread of the CTA calls
+// it. active[v] is false for a stream
+// with no chunk. Also writes zeros for seats with nothing to attend and flags lengths beyond the block table's
+// capacity.
+template <int ROWS, int WARPS, int NS>
+__device__ __forceinline__ void decode_plan_streams(const DecodeArgs& a, int G, DecodePlan (&P)[NS],
+                                                    bool (&active)[NS]) {
+  constexpr int kThreads = WARPS * 32;
+  __shared__ long long warp_sums[WARPS];
+  __shared__ long long plan_first[NS];
+  __shared__ int plan_seat[NS];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cbase = NS * static_cast<int>(blockIdx.x);
+  const bool append = a.k_new != nullptr;
+
+  long long local = 0;
+  for (int s = tid; s < a.B; s += kThreads) {
+    const int L = seat_tokens(a, s);
+    local += (L + ROWS - 1) / ROWS;
+    if (cbase == 0) {
+      const int raw = a.seqlens[s] + (append ? 1 : 0);
+      if (raw > a.max_pages * a.page_size || a.seqlens[s] < 0) atomicOr(a.status, kStatusBadLength);
+    }
+    const int owner = s % G;   // empty cache, nothing appended: the output is zero (as flash-attn writes)
+    if (L == 0 && owner >= cbase && owner < cbase + NS) {
+      uint4* o = reinterpret_cast<uint4*>(a.out + static_cast<long long>(s) * a.out_stride);
+      for (int k = 0; k < kQHeads * kHeadDim / 8; ++k) o[k] = make_uint4(0, 0, 0, 0);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+  if (lane == 0) warp_sums[warp] = local;
+  __syncthreads();
+  long long N = 0;
+#pragma unroll
+  for (int w = 0; w < WARPS; ++w) N += warp_sums[w];
+  // Effective split count: never more streams than chunks, so every stream in [0, Ge) owns at least one chunk and the
+  // streams between a seat's first and last owner all contribute a partial (the merge counts them).
+  const int Ge = static_cast<int>(N < G ? N : G);
+  // pair weighting only for the full two-per-SM grid of one-stream CTAs and enough chunks that every CTA keeps several
+  const int H = (NS == 1 && a.pair_split > 0 && Ge == G && G == 2 * a.pair_split && N >= 4ll * Ge) ? a.pair_split : 0;
+  long long c0[NS], c1[NS];
+  bool any = false;
+#pragma unroll
+  for (int v = 0; v < NS; ++v) {
+    active[v] = cbase + v < Ge;
+    c0[v] = active[v] ? chunk_start(cbase + v, N, Ge, H) : 0;
+    c1[v] = active[v] ? chunk_start(cbase + v + 1, N, Ge, H) : 0;
+    any = any || active[v];
+  }
+  if (!any) return;  // uniform across the CTA (the scan's first barrier orders the reads of warp_sums above)
+
+  long long base = 0;
+  for (int t0 = 0; t0 < a.B; t0 += kThreads) {
+    const int s = t0 + tid;
+    const int n = s < a.B ? (seat_tokens(a, s) + ROWS - 1) / ROWS : 0;
+    long long incl = n;   // block inclusive scan of n
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    __syncthreads();
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    long long before = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) {
+      if (w < warp) before += warp_sums[w];
+      total += warp_sums[w];
+    }
+    incl += before;
+    const long long excl = incl - n;
+#pragma unroll
+    for (int v = 0; v < NS; ++v) {
+      if (active[v] && n > 0 && base + excl <= c0[v] && c0[v] < base + incl) {
+        plan_seat[v] = s;
+        plan_first[v] = base + excl;
+      }
+    }
+    base += total;
+    __syncthreads();
+    bool done = true;   // uniform: every thread sees the same base
+#pragma unroll
+    for (int v = 0; v < NS; ++v) done = done && (!active[v] || base > c0[v]);
+    if (done) break;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int v = 0; v < NS; ++v) {
+    P[v].N = N;
+    P[v].c0 = c0[v];
+    P[v].c1 = c1[v];
+    P[v].Ge = Ge;
+    P[v].H = H;
+    P[v].cur.seat = active[v] ? plan_seat[v] : 0;
+    P[v].cur.first = active[v] ? plan_first[v] : 0;
+    P[v].cur.len = active[v] ? seat_tokens(a, plan_seat[v]) : 0;
+    P[v].cur.nch = (P[v].cur.len + ROWS - 1) / ROWS;
+  }
+}
+
 // Work split of the CTA; every thread of the CTA calls it. Returns false when the CTA has no chunk. Also writes zeros
 // for seats with nothing to attend and flags lengths beyond the block table's capacity.
 template <int ROWS, int WARPS = kDecodeWarps>
@@ -255,14 +359,13 @@ __device__ __forceinline__ void merge_seat_partials(const DecodeArgs& a, const S
   if (lane == 0) a.counters[static_cast<long long>(cur.seat) * kKvHeads + h] = 0u;   // ready for the next launch
 }
 
-// End of a seat's chunks in this CTA for KV head h. o0/o1 hold this lane's dims 4*lane..4*lane+3 of q heads 2h and
+// End of a seat's chunks in split slot c (the CTA, or one chunk stream of it) for KV head h. o0/o1 hold this lane's dims 4*lane..4*lane+3 of q heads 2h and
 // 2h+1 (not yet divided by the sums); m0/m1 the running maxima (log2 domain), l0/l1 the running sums. A seat wholly
 // inside this CTA is written directly; otherwise this CTA's partial goes to the workspace and the last CTA to arrive
 // (atomic ticket) merges all partials of the seat in CTA order and writes the output.
-__device__ __forceinline__ void decode_finish_seat(const DecodeArgs& a, const DecodePlan& P, const SeatCursor& cur,
-                                                   int h, int lane, float4 o0, float4 o1, float m0, float m1,
-                                                   float l0, float l1) {
-  const int c = blockIdx.x;
+__device__ __forceinline__ void decode_finish_seat(const DecodeArgs& a, const DecodePlan& P, int c,
+                                                   const SeatCursor& cur, int h, int lane, float4 o0, float4 o1,
+                                                   float m0, float m1, float l0, float l1) {
   const int c_first = cta_of_chunk(cur.first, P.N, P.Ge, P.H);
   const int c_last = cta_of_chunk(cur.first + cur.nch - 1, P.N, P.Ge, P.H);
   __nv_bfloat16* op = a.out + static_cast<long long>(cur.seat) * a.out_stride + (2 * h) * kHeadDim + 4 * lane;

@@ -292,7 +292,7 @@ __global__ void __maxnreg__(decode_max_regs<MIN_CTAS>()) paged_decode_mma_kernel
     const float4 o0 = reinterpret_cast<const float4*>(obuf)[lane];
     const float4 o1 = reinterpret_cast<const float4*>(obuf + kHeadDim)[lane];
     __syncwarp();
-    decode_finish_seat(a, plan, cur, h, lane, o0, o1, m0, m1, l0, l1);
+    decode_finish_seat(a, plan, static_cast<int>(blockIdx.x), cur, h, lane, o0, o1, m0, m1, l0, l1);
   }
 
   // A warp that gave up may leave copies in flight into this CTA's shared memory: wait (bounded) for every issued

@@ -31,6 +31,7 @@ struct DecodeArgs {
   uint32_t* counters;              // [B, 8] zero between launches
   uint32_t* status;
   int pair_split = 0;              // SM count when the grid is two CTAs per SM on every SM (pair-weighted split)
+  int split_slots = 0;             // the dedicated-producer kernel: chunk streams of the split (two per CTA)
   // Fused q/k RMSNorm + RoPE (the kernel instantiated with FUSE): q rows and k_new rows are raw projections.
   const __nv_bfloat16* qn_w = nullptr;     // [128]
   const __nv_bfloat16* kn_w = nullptr;     // [128]

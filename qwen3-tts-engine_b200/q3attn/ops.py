@@ -644,6 +644,7 @@ def set_prefill_kernel(kernel: int) -> int:
 
 def set_decode_variant(variant: int) -> int:
     """Select the decode kernel variant (0: 8-token chunks x 3 stages, two CTAs/SM; 1: 16-token x 3, one CTA/SM;
-    2: 8-token x 2, two CTAs/SM; 3 / 4: warp-MMA scoring with early stage release, 8-token x 3 / 2, two CTAs/SM)."""
+    2: 8-token x 2, two CTAs/SM; 3 / 4: warp-MMA scoring with early stage release, 8-token x 3 / 2, two CTAs/SM;
+    5: dedicated producer warps, one CTA/SM running two 8-token x 3 chunk streams)."""
     _ws.clear()
     return int(_lib.load().q3_set_decode_variant(int(variant)))

@@ -113,10 +113,11 @@ def test_decode_split_counts(q3, num_splits):
     assert_close_attn(out, ref, what=f"splits {num_splits}")
 
 
-@pytest.mark.parametrize("variant", [0, 2, 3, 4])
+@pytest.mark.parametrize("variant", [0, 2, 3, 4, 5])
 def test_decode_pair_weighted_split(q3, variant):
     """The default grid of the two-CTAs-per-SM variants (pair-weighted chunk split: the first CTA resident on each SM
-    takes a larger share) with enough chunks to engage it; every seat checked, seats straddling CTAs of both weights."""
+    takes a larger share) with enough chunks to engage it; every seat checked, seats straddling CTAs of both weights.
+    Variant 5 (two chunk streams per CTA, uniform split) runs its own default grid through the same check."""
     prev = q3.set_decode_variant(variant)
     try:
         lay = synth.paged_layout(21, B=128, ctx_lo=100, ctx_hi=700, page=16, pages_per_seat=44)
@@ -168,7 +169,7 @@ def test_decode_c2_full_size_subset(q3):
         assert_close_attn(out[b], ref, what=f"c2 seat {b}")
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5])
 def test_decode_every_kernel_variant(q3, variant):
     """Every decode kernel variant (8/16-token chunks, 2/3 stages) against the oracle on edge lengths with 16-token
     pages, a 1-token page layout and 256-token pages, with and without the fused append."""
@@ -184,6 +185,23 @@ def test_decode_every_kernel_variant(q3, variant):
             assert_close_attn(out, ref, what=f"variant {variant} page {page} append {append}")
             if append:
                 assert bits_equal(dd["k_pool"], kp) and bits_equal(dd["v_pool"], vp)
+    finally:
+        q3.set_decode_variant(prev)
+
+
+@pytest.mark.parametrize("num_splits", [1, 2, 3, 295, 296, 1000])
+def test_decode_producer_streams_split_counts(q3, num_splits):
+    """The dedicated-producer variant (two chunk streams per CTA) at any stream count, odd ones included (the last
+    CTA's second stream then has no chunk), with the fused append."""
+    prev = q3.set_decode_variant(5)
+    try:
+        lay = synth.paged_layout(15, B=40, ctx_lo=1, ctx_hi=900, page=16, pages_per_seat=60)
+        d = synth.decode_case(15, lay, scale=0.5)
+        out, dd = _run_decode(q3, lay, d, append=True, num_splits=num_splits)
+        ref, kp, vp = _oracle(lay, d, append=True)
+        assert_close_attn(out, ref, what=f"producer streams, splits {num_splits}")
+        assert bits_equal(dd["k_pool"], kp) and bits_equal(dd["v_pool"], vp)
+        assert q3._lib.read_status() == 0
     finally:
         q3.set_decode_variant(prev)
 
