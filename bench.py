@@ -49,7 +49,7 @@ def parse():
     p.add_argument("--seats", type=int, default=576)
     p.add_argument("--layers", type=int, default=28)
     p.add_argument("--seed", type=int, default=2)
-    p.add_argument("--variant", type=int, default=0, help="decode kernel variant (q3_set_decode_variant)")
+    p.add_argument("--variant", type=int, default=5, help="decode kernel variant (q3_set_decode_variant)")
     p.add_argument("--num-splits", type=int, default=0)
     p.add_argument("--prefill-kernel", type=int, default=0, help="prefill kernel (q3_set_prefill_kernel): 0 TMA, 1 single")
     p.add_argument("--ring-frame-kernel", type=int, default=2,
@@ -673,7 +673,7 @@ def main():
     achieved = bytes_launch / launch_s / 1e9
     peak, peak_kind = hbm_peak()
     traffic = None
-    tpath = os.path.join(REPO, "profiles", "decode_traffic.json")
+    tpath = os.path.join(REPO, "profiles", "decode_traffic_ws.json" if a.variant == 5 else "decode_traffic.json")
     if os.path.exists(tpath):
         try:
             t = json.load(open(tpath))
@@ -682,7 +682,8 @@ def main():
             traffic = None
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "traffic": traffic, "peak_source": peak_kind, "bytes_per_launch": bytes_launch, "launch_us": launch_s * 1e6,
-            "kernel": "q3::paged_decode_kernel (fused append)",
+            "kernel": ("q3::paged_decode_ws_kernel (fused append, producer warps)" if a.variant == 5
+                       else "q3::paged_decode_kernel (fused append)"),
             "resident_ctas_per_sm": int(q3attn._lib.load().q3_paged_decode_resident_ctas(a.variant))}
 
     # ---------------- end to end through the public API with host buffers

@@ -67,10 +67,10 @@ int q3_paged_decode(const void* q, int64_t q_batch_stride,
                     void* out, int64_t out_batch_stride,
                     void* workspace, size_t workspace_bytes, int32_t num_splits,
                     void* stream);
-/* Kernel variant used by q3_paged_decode: 0 = 8-token chunks x 3 stages, two CTAs per SM (default),
+/* Kernel variant used by q3_paged_decode: 0 = 8-token chunks x 3 stages, two CTAs per SM,
  * 1 = 16-token chunks x 3 stages, one CTA per SM, 2 = 8-token chunks x 2 stages, two CTAs per SM,
  * 3 / 4 = warp-MMA scoring (mma.sync) with early stage release, 8-token chunks x 3 / 2 stages, two CTAs per SM,
- * 5 = dedicated producer warps: one 20-warp CTA per SM running two 8-token x 3-stage chunk streams.
+ * 5 = dedicated producer warps: one 20-warp CTA per SM running two 8-token x 3-stage chunk streams (default).
  * Values outside 0..5 leave the selection unchanged. Returns the previous value. No reference counterpart (a tuning
  * knob of this library). */
 int q3_set_decode_variant(int variant);
@@ -174,7 +174,8 @@ typedef struct q3_qk_norm_rope {
 /* One talker attention layer after the QKV GEMM: engine/talker.py:69-77 (q = rope(rms(q, qn)), k = rope(rms(k, kn)),
  * the k/v index_copy_ into the pools at position cache_seqlens[b], flash_attn_with_kvcache over cache + new row).
  * cos/sin row b must be the rotary row of position cache_seqlens[b] (W.cos[pos], talker.py:111). Pools, table,
- * workspace (q3_paged_decode_workspace_bytes) and errors as q3_paged_decode; always the default configuration. */
+ * workspace (q3_paged_decode_workspace_bytes) and errors as q3_paged_decode; the kernel of q3_set_decode_variant 5 (the
+ * default) when that is selected, else that of variant 0. */
 int q3_paged_decode_qkv(const void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rope* norm_rope,
                         void* k_pool, void* v_pool, int32_t num_pages, int32_t page_size,
                         const int32_t* cache_seqlens,
@@ -221,7 +222,9 @@ int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
  * chunk's K/V into ring slots (pos + j) % ring (the caller's index_copy_, decoder_stream.py:330-333).
  * head_dim 64 or 128, ring <= 128, n <= min(17, ring - past). out: [B, n, heads * head_dim] fp16. */
 /* One-frame ring kernel used by q3_ring_window_attn for n == 1 (and past < 96): 0 = tensor cores, one warp per head,
- * G heads per CTA (4 for head_dim 64, 2 for 128; default), 3 = the same with G = 2 / 1, 4 = G = 1; 2 = scalar math,
+ * G heads per CTA (4 for head_dim 64, 2 for 128; default), 3 = the same with G = 2 / 1, 4 = G = 1; 5 = a persistent
+ * pipeline, one CTA per SM with a producer warp staging (stream, head) items for three tensor-core consumer warps
+ * (head_dim 64 and past <= 88; other calls use kernel 1); 2 = scalar math,
  * one warp per head, G = 4 / 2; 1 = scalar math, one CTA per (stream, head), always. Where G does not divide the head
  * count, kernel 1 runs. Other values leave the selection unchanged. Returns the previous value. No reference
  * counterpart (a tuning knob of this library). */

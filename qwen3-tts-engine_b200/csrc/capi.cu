@@ -12,7 +12,7 @@ __device__ uint32_t g_status_word;   // OR of q3::kStatus* bits raised by any ke
 
 constexpr int kMaxDevices = 64;
 thread_local char t_last_cuda_error[256] = "";
-int g_decode_variant = 0;
+int g_decode_variant = 5;
 int g_sm_count[kMaxDevices] = {0};
 uint32_t* g_status_ptr[kMaxDevices] = {nullptr};
 
@@ -151,7 +151,7 @@ size_t q3_paged_decode_workspace_bytes(int32_t batch, int32_t num_splits) {
   int dev = 0;
   if (batch < 0 || current_device(&dev) != Q3_OK) return 0;
   // Upper bound over all block-table shapes and kernel configurations (the selected variant, and the default one that
-  // q3_paged_decode_qkv always uses): the grid is at most SMs x CTAs/SM (or num_splits).
+  // q3_paged_decode_qkv falls back to): the grid is at most SMs x CTAs/SM (or num_splits) split slots.
   long long G = decode_grid(dev, batch, num_splits, 0, 0, g_decode_variant);
   const long long G0 = decode_grid(dev, batch, num_splits, 0, 0, 0);
   if (G0 > G) G = G0;
@@ -215,7 +215,8 @@ int decode_common(const void* q, int64_t q_batch_stride, const void* k_new, cons
   if (rc != Q3_OK || batch == 0) return rc;
   int dev = 0;
   if ((rc = current_device(&dev)) != Q3_OK) return rc;
-  const int variant = nr ? 0 : g_decode_variant;
+  // the fused q/k norm + RoPE form exists for variants 0 and 5
+  const int variant = (nr && g_decode_variant != 5) ? 0 : g_decode_variant;
   const long long G = decode_grid(dev, batch, num_splits, max_pages_per_seat, page_size, variant);
   if (G > (1ll << 30)) return Q3_ERR_INVALID;
   const WsLayout w = ws_layout(workspace_bytes, batch, G);
@@ -261,7 +262,7 @@ int decode_common(const void* q, int64_t q_batch_stride, const void* k_new, cons
     a.rope_sin = static_cast<const __nv_bfloat16*>(nr->sin);
     a.rope_stride = nr->rope_row_stride;
     a.eps = nr->eps;
-    return record(q3::launch_paged_decode_fused(a, static_cast<int>(G), s));
+    return record(q3::launch_paged_decode_fused(a, static_cast<int>(G), variant, s));
   }
   return record(q3::launch_paged_decode(a, static_cast<int>(G), variant, s));
 }
@@ -616,7 +617,7 @@ int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
 
 int q3_set_ring_frame_kernel(int kernel) {
   const int prev = q3::g_ring_frame_kernel;
-  if (kernel >= 0 && kernel <= 4) q3::g_ring_frame_kernel = kernel;
+  if (kernel >= 0 && kernel <= 5) q3::g_ring_frame_kernel = kernel;
   return prev;
 }
 

@@ -144,13 +144,12 @@ struct DecodePlan {
 
 // Work split of CTAs that each run NS chunk streams (the dedicated-producer kernel): stream v of block x is split slot
 // c = NS * x + v of G, the grid's stream count. decode_plan below is the one-stream form, kept separate so the
-// register allocation of the one-stream kernels does not carry the per-stream arrays. Every thread of the CTA calls
-// it. active[v] is false for a stream
-// with no chunk. Also writes zeros for seats with nothing to attend and flags lengths beyond the block table's
+// register allocation of the one-stream kernels does not carry the per-stream state. Every thread of the CTA calls
+// it, naming the stream it works for (mine); P receives that stream's plan. Returns the mask of streams that have
+// chunks (bit v: stream v). Also writes zeros for seats with nothing to attend and flags lengths beyond the block table's
 // capacity.
 template <int ROWS, int WARPS, int NS>
-__device__ __forceinline__ void decode_plan_streams(const DecodeArgs& a, int G, DecodePlan (&P)[NS],
-                                                    bool (&active)[NS]) {
+__device__ __forceinline__ unsigned decode_plan_streams(const DecodeArgs& a, int G, int mine, DecodePlan& P) {
   constexpr int kThreads = WARPS * 32;
   __shared__ long long warp_sums[WARPS];
   __shared__ long long plan_first[NS];
@@ -185,16 +184,8 @@ __device__ __forceinline__ void decode_plan_streams(const DecodeArgs& a, int G, 
   const int Ge = static_cast<int>(N < G ? N : G);
   // pair weighting only for the full two-per-SM grid of one-stream CTAs and enough chunks that every CTA keeps several
   const int H = (NS == 1 && a.pair_split > 0 && Ge == G && G == 2 * a.pair_split && N >= 4ll * Ge) ? a.pair_split : 0;
-  long long c0[NS], c1[NS];
-  bool any = false;
-#pragma unroll
-  for (int v = 0; v < NS; ++v) {
-    active[v] = cbase + v < Ge;
-    c0[v] = active[v] ? chunk_start(cbase + v, N, Ge, H) : 0;
-    c1[v] = active[v] ? chunk_start(cbase + v + 1, N, Ge, H) : 0;
-    any = any || active[v];
-  }
-  if (!any) return;  // uniform across the CTA (the scan's first barrier orders the reads of warp_sums above)
+  const int nact = Ge - cbase < 0 ? 0 : (Ge - cbase > NS ? NS : Ge - cbase);   // streams 0 .. nact-1 have chunks
+  if (nact == 0) return 0u;  // uniform across the CTA (the scan's first barrier orders the reads of warp_sums above)
 
   long long base = 0;
   for (int t0 = 0; t0 < a.B; t0 += kThreads) {
@@ -217,33 +208,29 @@ __device__ __forceinline__ void decode_plan_streams(const DecodeArgs& a, int G, 
     }
     incl += before;
     const long long excl = incl - n;
-#pragma unroll
-    for (int v = 0; v < NS; ++v) {
-      if (active[v] && n > 0 && base + excl <= c0[v] && c0[v] < base + incl) {
+    for (int v = 0; v < nact; ++v) {
+      const long long cv = chunk_start(cbase + v, N, Ge, H);
+      if (n > 0 && base + excl <= cv && cv < base + incl) {
         plan_seat[v] = s;
         plan_first[v] = base + excl;
       }
     }
     base += total;
     __syncthreads();
-    bool done = true;   // uniform: every thread sees the same base
-#pragma unroll
-    for (int v = 0; v < NS; ++v) done = done && (!active[v] || base > c0[v]);
-    if (done) break;
+    if (base > chunk_start(cbase + nact - 1, N, Ge, H)) break;   // uniform; the streams' first chunks ascend
   }
   __syncthreads();
-#pragma unroll
-  for (int v = 0; v < NS; ++v) {
-    P[v].N = N;
-    P[v].c0 = c0[v];
-    P[v].c1 = c1[v];
-    P[v].Ge = Ge;
-    P[v].H = H;
-    P[v].cur.seat = active[v] ? plan_seat[v] : 0;
-    P[v].cur.first = active[v] ? plan_first[v] : 0;
-    P[v].cur.len = active[v] ? seat_tokens(a, plan_seat[v]) : 0;
-    P[v].cur.nch = (P[v].cur.len + ROWS - 1) / ROWS;
-  }
+  const bool act = mine < nact;
+  P.N = N;
+  P.Ge = Ge;
+  P.H = H;
+  P.c0 = act ? chunk_start(cbase + mine, N, Ge, H) : 0;
+  P.c1 = act ? chunk_start(cbase + mine + 1, N, Ge, H) : 0;
+  P.cur.seat = act ? plan_seat[mine] : 0;
+  P.cur.first = act ? plan_first[mine] : 0;
+  P.cur.len = act ? seat_tokens(a, plan_seat[mine]) : 0;
+  P.cur.nch = (P.cur.len + ROWS - 1) / ROWS;
+  return (1u << nact) - 1u;
 }
 
 // Work split of the CTA; every thread of the CTA calls it. Returns false when the CTA has no chunk. Also writes zeros

@@ -334,14 +334,16 @@ constexpr int kWsLaunchRegs = 96, kWsProducerRegs = 32, kWsConsumerRegs = 112;
 static_assert(128 * kWsProducerRegs + kWsStreams * kDecodeThreads * kWsConsumerRegs == kWsThreads * kWsLaunchRegs,
               "the register split must add up to what the CTA is launched with");
 
-template <int ROWS, int NSTAGES>
+template <int ROWS, int NSTAGES, bool FUSE = false>
 struct WsSmemLayout {
   static constexpr int kStageBytes = ROWS * kRowBytes;                // K (or V) of one chunk
   static constexpr int kStreamBytes = 2 * NSTAGES * kStageBytes;      // a stream's K stages, then its V stages
   static constexpr int kBarOff = kWsStreams * kStreamBytes;           // per stream: full[NSTAGES], empty[NSTAGES]
   static constexpr int kPOff = kBarOff + kWsStreams * 2 * NSTAGES * 8;
   static constexpr int kMiscOff = kPOff + kWsStreams * kDecodeWarps * 2 * ROWS * 4;
-  static constexpr int kBytes = kMiscOff + 16;
+  // FUSE: per consumer warp the normalised q [2][128] bf16, read back with 16-byte loads
+  static constexpr int kQOff = ((kMiscOff + 16 + 127) / 128) * 128;
+  static constexpr int kBytes = kQOff + (FUSE ? kWsStreams * kDecodeWarps * 2 * kHeadBytes : 0);
 };
 
 // Stages filled by a producer warp: a consumer warp releases a stage by one arrival on its `empty` barrier.
@@ -394,9 +396,9 @@ __device__ __forceinline__ void decode_produce(const DecodeArgs& a, const Decode
   }
 }
 
-template <int ROWS, int NSTAGES>
+template <int ROWS, int NSTAGES, bool FUSE = false>
 __global__ void __launch_bounds__(kWsThreads, 1) paged_decode_ws_kernel(const DecodeArgs a) {
-  using SL = WsSmemLayout<ROWS, NSTAGES>;
+  using SL = WsSmemLayout<ROWS, NSTAGES, FUSE>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SL::kBarOff);   // stream s: full at 2*NSTAGES*s, empty after
   volatile int* abort_flag = reinterpret_cast<int*>(smem + SL::kMiscOff);
@@ -412,33 +414,33 @@ __global__ void __launch_bounds__(kWsThreads, 1) paged_decode_ws_kernel(const De
     *abort_flag = 0;
     fence_mbar_init();
   }
-  DecodePlan plan[kWsStreams];
-  bool active[kWsStreams];
-  decode_plan_streams<ROWS, kWsWarps, kWsStreams>(a, a.split_slots, plan, active);   // its barriers publish the init
-  if (!active[0] && !active[1]) return;                                               // uniform across the CTA
+  // the stream this warp works for: producers 0 and 1 feed streams 0 and 1, consumer warp 4 + 8s + h reads stream s
+  const int mine = warp < 4 ? (warp < kWsStreams ? warp : 0) : (warp - 4) / kDecodeWarps;
+  DecodePlan my;
+  const unsigned active = decode_plan_streams<ROWS, kWsWarps, kWsStreams>(a, a.split_slots, mine, my);
+  if (active == 0u) return;   // uniform across the CTA; the plan's barriers also published the barrier init
 
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWsProducerRegs));
-    if (warp < kWsStreams && lane == 0 && active[warp]) {
+    if (warp < kWsStreams && lane == 0 && ((active >> warp) & 1u)) {
       uint8_t* base = smem + warp * SL::kStreamBytes;
       uint64_t* full = bars + 2 * NSTAGES * warp;
-      decode_produce<ROWS, NSTAGES>(a, plan[warp], base, base + NSTAGES * SL::kStageBytes, full, full + NSTAGES,
-                                    abort_flag);
+      decode_produce<ROWS, NSTAGES>(a, my, base, base + NSTAGES * SL::kStageBytes, full, full + NSTAGES, abort_flag);
     }
     return;
   }
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWsConsumerRegs));
-  const int s = (warp - 4) / kDecodeWarps, h = (warp - 4) % kDecodeWarps;
-  if (!active[s]) return;
+  const int s = mine, h = (warp - 4) % kDecodeWarps;
+  if (!((active >> s) & 1u)) return;
   uint8_t* base = smem + s * SL::kStreamBytes;
   uint64_t* full = bars + 2 * NSTAGES * s;
   ProducerRing<NSTAGES> ring{full, full + NSTAGES, abort_flag};
   int it = 0;
   bool aborted = false;
-  decode_consume<ROWS, NSTAGES, false>(a, plan[s], kWsStreams * static_cast<int>(blockIdx.x) + s, h, lane, base,
-                                       base + NSTAGES * SL::kStageBytes,
-                                       reinterpret_cast<float*>(smem + SL::kPOff) + (s * kDecodeWarps + h) * 2 * ROWS,
-                                       nullptr, ring, it, aborted);
+  decode_consume<ROWS, NSTAGES, FUSE>(a, my, kWsStreams * static_cast<int>(blockIdx.x) + s, h, lane, base,
+                                      base + NSTAGES * SL::kStageBytes,
+                                      reinterpret_cast<float*>(smem + SL::kPOff) + (s * kDecodeWarps + h) * 2 * ROWS,
+                                      smem + SL::kQOff + (s * kDecodeWarps + h) * 2 * kHeadBytes, ring, it, aborted);
   // a consumer that gave up leaves (bounded) only once the stages the producer may have issued have landed
   if (aborted && lane == 0) {
     for (int k = 0; k < NSTAGES; ++k)
@@ -476,10 +478,10 @@ int occupancy_of() {
 // Variant 5: grid = split slots, two per CTA. The register split assumes the CTA is launched at exactly
 // kWsLaunchRegs per thread; any other count (a different compiler) refuses the launch instead of risking a
 // setmaxnreg.inc that could never be satisfied.
-template <int ROWS, int NSTAGES>
+template <int ROWS, int NSTAGES, bool FUSE = false>
 static cudaError_t launch_decode_ws(const DecodeArgs& a, int slots, cudaStream_t stream) {
-  using SL = WsSmemLayout<ROWS, NSTAGES>;
-  auto kern = paged_decode_ws_kernel<ROWS, NSTAGES>;
+  using SL = WsSmemLayout<ROWS, NSTAGES, FUSE>;
+  auto kern = paged_decode_ws_kernel<ROWS, NSTAGES, FUSE>;
   static thread_local int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -532,7 +534,8 @@ int decode_rows_per_chunk(int variant) { return variant == 1 ? 16 : 8; }
 
 int decode_ctas_per_sm(int variant) { return variant == 1 ? 1 : 2; }
 
-cudaError_t launch_paged_decode_fused(const DecodeArgs& a, int grid, cudaStream_t stream) {
+cudaError_t launch_paged_decode_fused(const DecodeArgs& a, int grid, int variant, cudaStream_t stream) {
+  if (variant == 5) return launch_decode_ws<8, 3, true>(a, grid, stream);
   return launch_decode<8, 3, 2, true>(a, grid, stream);
 }
 

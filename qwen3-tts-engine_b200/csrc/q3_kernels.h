@@ -45,8 +45,9 @@ int decode_rows_per_chunk(int variant);
 int decode_ctas_per_sm(int variant);
 int decode_occupancy(int variant);   // resident CTAs per SM measured by the runtime (-1 on error)
 cudaError_t launch_paged_decode(const DecodeArgs& a, int grid, int variant, cudaStream_t stream);
-// Default configuration (variant 0) with the q/k RMSNorm + RoPE fused in (a.qn_w etc. set, k_new required).
-cudaError_t launch_paged_decode_fused(const DecodeArgs& a, int grid, cudaStream_t stream);
+// The q/k RMSNorm + RoPE fused in (a.qn_w etc. set, k_new required): variant 5 (dedicated producers) or, for any other
+// variant, variant 0.
+cudaError_t launch_paged_decode_fused(const DecodeArgs& a, int grid, int variant, cudaStream_t stream);
 
 struct AppendArgs {
   const __nv_bfloat16* k_rows;     // [n_rows, row_elems] with row stride rows_stride (elements)
@@ -203,7 +204,8 @@ struct RingArgs {
 size_t ring_smem_bytes(int ring, int past, int hd, int n);
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);
 // Which one-frame ring kernel launch_ring_attn uses: 0 = tensor cores, one warp per head, 4 x 64 / 2 x 128 heads per
-// CTA (default); 3 = the same with 2 x 64 / 1 x 128 and 4 = one head per CTA; 2 = scalar math, one warp per head,
+// CTA (default); 3 = the same with 2 x 64 / 1 x 128 and 4 = one head per CTA; 5 = the persistent pipeline (one CTA per
+// SM, producer warp + three tensor-core consumer warps; head_dim 64, past <= 88); 2 = scalar math, one warp per head,
 // 4 x 64 / 2 x 128 heads per CTA; 1 = scalar math, one CTA per (stream, head), always (also where the heads do not
 // divide).
 extern int g_ring_frame_kernel;

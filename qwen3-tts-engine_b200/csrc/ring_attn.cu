@@ -12,17 +12,23 @@
 // StreamDecoder._step, decoder_stream.py:330-333); those slots hold frames older than the window (n <= RING - PAST),
 // so no query of this launch can see them, and each CTA writes only its own head after reading it.
 //
-// One CTA per (stream, head), 4 warps. The ring rows that some query of the chunk sees form one contiguous range of
-// distances d = 0 .. nvis-1 back from the newest frame (the union over the chunk is query 0's window); they are staged
-// in shared memory in that order (row d), followed by the chunk's rows. Ring rows no query sees are never read. Two
-// kernels, by chunk size:
+// The ring rows that some query of the chunk sees form one contiguous range of distances d = 0 .. nvis-1 back from the
+// newest frame (the union over the chunk is query 0's window); every kernel stages them in shared memory in that order
+// (row d), followed by the chunk's rows. Ring rows no query sees are never read. The kernels (launch_ring_attn picks
+// one by chunk size and the q3_set_ring_frame_kernel / q3_set_ring_chunk_kernel selections):
+//   * ring_attn_frame_mma_kernel (one frame, default) and ring_attn_chunk_mma_kernel (2..16 frames, default): one warp
+//     per head, G heads per CTA, each staged row (the G heads of one slot) by one bulk copy into rows padded by 16
+//     bytes, both contractions on the tensor cores with P handed from the score fragments to the P.V fragments in
+//     registers; described where they are defined;
+//   * ring_attn_frame_heads_kernel (one frame): the same staging, scalar math, one warp per head;
+// and, one CTA per (stream, head) with 4 warps (used also where the heads do not divide G, and for 17 frames):
 //   * ring_attn_mma_kernel (2..17 frames): rows staged by 16-byte asynchronous copies; the two ring contractions run
 //     on the tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulation): S = Q.K^T over 8-key column tiles (the
 //     chunk's keys included) and O_ring = P_ring.V_ring over 16-key steps with V fragments by ldmatrix.trans (V rows
 //     past nvis zeroed, so a zero probability never meets stale data); O_new = P_new.V_new (n <= 17 keys) is a few
 //     scalar FMAs per output. Rows of K, V and Q are 16-byte chunks XOR-swizzled by (row & 7), which keeps every
 //     fragment load free of bank conflicts. About 23 KB of shared memory at 88 slots, head_dim 64: nine CTAs per SM.
-//   * ring_attn_frame_kernel (one frame, the streaming case): rows staged by one bulk copy each, scalar math.
+//   * ring_attn_frame_kernel (one frame): rows staged by one bulk copy each, scalar math.
 #include "q3_common.cuh"
 #include "q3_kernels.h"
 
@@ -637,15 +643,145 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 
 constexpr int kRingMmaMaxKeys = 96;                          // key tiles of 8 held in registers: 12
 
+// The tensor-core math of one query frame for one head (one warp), shared by the one-frame kernels: rows staged by
+// distance at k_rows / v_rows (shared-memory addresses of this head's columns of row 0, rows rs bytes apart, the
+// frame's own k / v as row nvis), q at q_head; keys past nvis read the 16-byte zero row at zero_addr. wait_v() is
+// called after the softmax and before V is read (false: give up, nothing written). Writes the output row of
+// (stream b, head) and, with write_new, the frame's k / v into ring slot pos % RING.
+template <int HD, class WaitV>
+__device__ __forceinline__ void ring_frame_head_mma(const RingArgs& a, uint32_t k_rows, uint32_t v_rows,
+                                                    const uint8_t* q_head, const uint8_t* k_self, const uint8_t* v_self,
+                                                    int rs, uint32_t zero_addr, int nvis, int b, int head,
+                                                    long long row, long long pos, int lane, WaitV wait_v) {
+  constexpr int NT = kRingMmaMaxKeys / 8;                    // score tiles (upper bound)
+  constexpr int NTO = HD / 8;                                // output tiles of 8 dims
+  const int t4 = lane & 3;
+  const int RING = a.ring;
+  const int nk = nvis + 1;
+  const int nt = (nk + 7) >> 3;
+
+  // ---- S = q.K^T on the tensor cores: A rows 1-15 are zero, so only lanes 0-3 carry q (row 0)
+  uint32_t qa[HD / 16][2];
+#pragma unroll
+  for (int ks = 0; ks < HD / 16; ++ks) {
+    const uint32_t* qw = reinterpret_cast<const uint32_t*>(q_head + ks * 32);
+    qa[ks][0] = lane < 4 ? qw[t4] : 0u;                      // dims 16ks + 2t4, +1
+    qa[ks][1] = lane < 4 ? qw[4 + t4] : 0u;                  // dims 16ks + 8 + 2t4, +1
+  }
+  float s[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    if (j < nt) {
+      const int key = 8 * j + (lane & 7);
+      const uint32_t ra = k_rows + key * rs + (lane >> 3) * 16;
+#pragma unroll
+      for (int kp = 0; kp < HD / 32; ++kp) {                 // 32 dims (two k-steps) per ldmatrix.x4
+        uint32_t bf[4];
+        ldsm_x4(key < nk ? ra + kp * 64 : zero_addr, bf);
+        mma_f16(s[j], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, bf[0], bf[1]);
+        mma_f16(s[j], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, bf[2], bf[3]);
+      }
+    }
+  }
+
+  // ---- softmax over row 0 (lanes 0-3 hold keys 8j + 2t4, +1 of every tile j); P rounded to fp16
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int key = 8 * j + 2 * t4 + e;
+      const float x = (j < nt && key < nk) ? round_fp16(s[j][e]) * a.scale : -INFINITY;
+      s[j][e] = x;
+      m = fmaxf(m, x);
+    }
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float x = (j < nt) ? expf(s[j][e] - m) : 0.f;   // masked keys: exp(-inf) = 0
+      s[j][e] = x;
+      sum += x;
+    }
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  const float inv = 1.f / sum;                               // the frame always sees itself: sum > 0 (lanes 0-3)
+  float pmine = 0.f;
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int key = 8 * j + 2 * t4 + e;
+      float p = round_fp16(s[j][e] * inv);
+      if (key == nvis) {                                     // the frame's own key: kept apart from the ring sum
+        pmine = p;
+        p = 0.f;
+      }
+      s[j][e] = lane < 4 ? p : 0.f;                          // rows 1-15 of the P operand are zero
+    }
+  const float pself = __shfl_sync(0xffffffffu, pmine, (nvis & 7) >> 1);
+
+  if (!wait_v()) return;
+  // ---- O_ring = P_ring.V_ring: 16-key steps; ldmatrix.x4.trans gives the V fragments of two 8-dim tiles
+  float o[NTO][4];
+#pragma unroll
+  for (int jn = 0; jn < NTO; ++jn) o[jn][0] = o[jn][1] = o[jn][2] = o[jn][3] = 0.f;
+  const int ksteps = (nk + 15) >> 4;
+#pragma unroll
+  for (int kk = 0; kk < NT / 2; ++kk) {
+    if (kk < ksteps) {
+      const uint32_t pa0 = pack_half2(s[2 * kk][0], s[2 * kk][1]);        // keys 16kk + 2t4, +1
+      const uint32_t pa2 = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);  // keys 16kk + 8 + 2t4, +1
+      const int key = 16 * kk + ((lane >> 3) & 1) * 8 + (lane & 7);
+      const uint32_t ra = v_rows + key * rs + (lane >> 4) * 16;
+#pragma unroll
+      for (int np = 0; np < NTO / 2; ++np) {
+        uint32_t bf[4];
+        ldsm_x4_trans(key < nk ? ra + np * 32 : zero_addr, bf);
+        mma_f16(o[2 * np], pa0, 0u, pa2, 0u, bf[0], bf[1]);
+        mma_f16(o[2 * np + 1], pa0, 0u, pa2, 0u, bf[2], bf[3]);
+      }
+    }
+  }
+
+  // ---- o = fp16(fp16(ring) + fp16(p_self v_self)): lanes 0-3 hold dims 8jn + 2t4, +1
+  if (lane < 4) {
+    const __half* vself = reinterpret_cast<const __half*>(v_self);
+    __half* op = a.out + b * a.out_batch_stride + head * HD;
+#pragma unroll
+    for (int jn = 0; jn < NTO; ++jn) {
+      const int d = 8 * jn + 2 * t4;
+      const float2 vs = __half22float2(*reinterpret_cast<const __half2*>(vself + d));
+      *reinterpret_cast<__half2*>(op + d) = __floats2half2_rn(round_fp16(o[jn][0]) + round_fp16(pself * vs.x),
+                                                              round_fp16(o[jn][1]) + round_fp16(pself * vs.y));
+    }
+  }
+
+  // ---- the frame's columns into the ring (a slot outside every window of this launch, never staged)
+  if (a.write_new) {
+    constexpr int DPL = HD / 32;
+    const long long slot = ((pos % RING) + RING) % RING;
+    const long long off = row * a.ring_stream_stride + slot * a.ring_slot_stride + head * HD + lane * DPL;
+    const __half* ks = reinterpret_cast<const __half*>(k_self) + lane * DPL;
+    const __half* vs = reinterpret_cast<const __half*>(v_self) + lane * DPL;
+#pragma unroll
+    for (int j = 0; j < DPL; j += 2) {
+      *reinterpret_cast<__half2*>(a.k_ring + off + j) = *reinterpret_cast<const __half2*>(ks + j);
+      *reinterpret_cast<__half2*>(a.v_ring + off + j) = *reinterpret_cast<const __half2*>(vs + j);
+    }
+  }
+}
+
 template <int HD, int G>
 __global__ void __launch_bounds__(32 * G) ring_attn_frame_mma_kernel(const RingArgs a) {
   using SM = RingMmaSmem<HD, G>;
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int RB = SM::kRB, RS = SM::kRS;
-  constexpr int NT = kRingMmaMaxKeys / 8;                    // score tiles (upper bound)
-  constexpr int NTO = HD / 8;                                // output tiles of 8 dims
   const int hg = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
-  const int t4 = lane & 3;
   const int RING = a.ring;
   const int NV = a.past < RING ? a.past : RING;              // ring rows any frame can see (launch-wide)
   uint8_t* sK = smem;
@@ -705,127 +841,172 @@ __global__ void __launch_bounds__(32 * G) ring_attn_frame_mma_kernel(const RingA
     return;
   }
 
-  const uint32_t zero_addr = smem_addr(sZero);
-  const uint32_t k_base = smem_addr(sK) + w * HD * 2;
-  const uint32_t v_base = smem_addr(sV) + w * HD * 2;
-  const int nt = (nk + 7) >> 3;
+  ring_frame_head_mma<HD>(a, smem_addr(sK) + w * HD * 2, smem_addr(sV) + w * HD * 2, sQ + w * HD * 2,
+                          sK + nvis * RS + w * HD * 2, sV + nvis * RS + w * HD * 2, RS, smem_addr(sZero), nvis, b,
+                          hg * G + w, row, pos, lane, [&]() -> bool {
+                            if (mbar_wait_bounded(&bar[1], 0)) return true;
+                            give_up();
+                            return false;
+                          });
+}
 
-  // ---- S = q.K^T on the tensor cores: A rows 1-15 are zero, so only lanes 0-3 carry q (row 0)
-  uint32_t qa[HD / 16][2];
-#pragma unroll
-  for (int ks = 0; ks < HD / 16; ++ks) {
-    const uint32_t* qw = reinterpret_cast<const uint32_t*>(sQ + w * HD * 2 + ks * 32);
-    qa[ks][0] = lane < 4 ? qw[t4] : 0u;                      // dims 16ks + 2t4, +1
-    qa[ks][1] = lane < 4 ? qw[4 + t4] : 0u;                  // dims 16ks + 8 + 2t4, +1
+// One query frame as a persistent pipeline: one CTA per SM walks the (stream, head) items c, c + grid, c + 2 grid, ...
+// of the launch. Warps 0 .. kPipeNP-1 are producers: for item k they wait until stage (k / kPipeNC) % kPipeNS of consumer
+// warp k % kPipeNC's ring is free; warp 0 writes the item's header (ring row, position, visible rows) there, and all
+// producer lanes stage the item's rows by bulk copies (q, then the visible ring rows of K and V by distance, then the
+// frame's k / v; rows padded by 16 bytes). The next kPipeNC warps are consumers, each running ring_frame_head_mma on its own items
+// in order, so one consumer's stages form a plain single-reader ring (no phase can be overtaken). While consumers
+// compute, later items stream in, so DRAM sees no gaps between waves of CTAs; the per-(stream, head) kernels wait for
+// all their rows before any math and then leave DRAM idle while they compute.
+constexpr int kPipeNC = 3, kPipeNS = 3, kPipeNP = 4;   // consumer warps, stages per consumer, producer warps
+
+template <int HD>
+struct RingPipeSmem {
+  static constexpr int kRB = HD * 2, kRS = kRB + 16;
+  __host__ __device__ static size_t v_off(int nkl) { return static_cast<size_t>(nkl) * kRS; }
+  __host__ __device__ static size_t q_off(int nkl) { return 2 * static_cast<size_t>(nkl) * kRS; }
+  __host__ __device__ static size_t hdr_off(int nkl) { return q_off(nkl) + kRS; }
+  __host__ __device__ static size_t stage_bytes(int nkl) { return hdr_off(nkl) + 32; }
+  __host__ __device__ static size_t zero_off(int nkl) { return kPipeNC * kPipeNS * stage_bytes(nkl); }
+  __host__ __device__ static size_t flag_off(int nkl) { return zero_off(nkl) + 16; }  // the 16-byte zero row, then
+  __host__ __device__ static size_t bar_off(int nkl) { return flag_off(nkl) + 16; }   // a give-up flag; full, empty
+  __host__ __device__ static size_t bytes(int nkl) { return bar_off(nkl) + 2 * kPipeNC * kPipeNS * 8; }
+};
+
+struct RingPipeHeader {
+  long long row, pos;
+  int nvis, b, head, pad;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(32 * (kPipeNC + kPipeNP), 1) ring_attn_frame_pipe_kernel(const RingArgs a) {
+  using SM = RingPipeSmem<HD>;
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int RB = SM::kRB, RS = SM::kRS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int RING = a.ring;
+  const int NV = a.past < RING ? a.past : RING;              // ring rows any frame can see (launch-wide)
+  const int nkl = NV + 1;
+  const size_t SB = SM::stage_bytes(nkl);
+  uint8_t* sZero = smem + SM::zero_off(nkl);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SM::bar_off(nkl));   // [consumer * kPipeNS + stage]
+  uint64_t* empty = full + kPipeNC * kPipeNS;
+  volatile int* abort_flag = reinterpret_cast<int*>(smem + SM::flag_off(nkl));
+  const long long items = static_cast<long long>(a.B) * a.H;
+  const long long nloc = (items - blockIdx.x + gridDim.x - 1) / gridDim.x;   // this CTA's items (grid <= items)
+
+  if (tid == 0) {
+    for (int i = 0; i < kPipeNC * kPipeNS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    fence_mbar_init();
   }
-  float s[NT][4];
-#pragma unroll
-  for (int j = 0; j < NT; ++j) {
-    s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-    if (j < nt) {
-      const int key = 8 * j + (lane & 7);
-      const uint32_t ra = k_base + key * RS + (lane >> 3) * 16;
-#pragma unroll
-      for (int kp = 0; kp < HD / 32; ++kp) {                 // 32 dims (two k-steps) per ldmatrix.x4
-        uint32_t bf[4];
-        ldsm_x4(key < nk ? ra + kp * 64 : zero_addr, bf);
-        mma_f16(s[j], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, bf[0], bf[1]);
-        mma_f16(s[j], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, bf[2], bf[3]);
+  if (tid < 4) reinterpret_cast<uint32_t*>(sZero)[tid] = 0u;
+  if (tid == 4) *abort_flag = 0;
+  __syncthreads();
+
+  if (warp < kPipeNP) {
+    // ---- producers: all kPipeNP warps walk the same items; warp 0 lane 0 writes the header and the expected bytes,
+    //      the copies of an item are spread over every producer lane. The ring row and position of the next item are
+    //      loaded while the current one is issued.
+    long long k = 0;
+    long long nrow = 0, npos = 0;
+    if (nloc > 0) {
+      const int b0 = static_cast<int>(static_cast<long long>(blockIdx.x) / a.H);
+      nrow = a.ring_rows[b0];
+      npos = a.pos[b0];
+    }
+    for (; k < nloc; ++k) {
+      const long long item = blockIdx.x + k * gridDim.x;
+      const int b = static_cast<int>(item / a.H), head = static_cast<int>(item % a.H);
+      const long long row = nrow, pos = npos;
+      if (k + 1 < nloc) {
+        const int bn = static_cast<int>((item + gridDim.x) / a.H);
+        nrow = a.ring_rows[bn];
+        npos = a.pos[bn];
+      }
+      const int cw = static_cast<int>(k % kPipeNC);
+      const long long j = k / kPipeNC;
+      const int st = static_cast<int>(j % kPipeNS);
+      const int bi = cw * kPipeNS + st;
+      if (j >= kPipeNS && !mbar_wait_bounded(&empty[bi], static_cast<uint32_t>((j / kPipeNS - 1) & 1))) {
+        if (lane == 0) {
+          atomicOr(a.status, kStatusWaitTimeout);
+          *abort_flag = 1;
+        }
+      }
+      __syncwarp();
+      if (*abort_flag) break;
+      const long long pm1 = pos - 1;
+      const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+      int nvis = NV;
+      if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
+      const int nk = nvis + 1;
+      uint8_t* S = smem + bi * SB;
+      if (warp == 0 && lane == 0) {
+        RingPipeHeader* hd = reinterpret_cast<RingPipeHeader*>(S + SM::hdr_off(nkl));
+        hd->row = row;
+        hd->pos = pos;
+        hd->nvis = nvis;
+        hd->b = b;
+        hd->head = head;
+        mbar_arrive_expect_tx(&full[bi], static_cast<uint32_t>(2 * nk + 1) * RB);   // release: the header is seen
+      }
+      __syncwarp();
+      const long long fo = b * a.qkv_batch_stride + head * HD;
+      const __half* kr = a.k_ring + row * a.ring_stream_stride + head * HD;
+      const __half* vr = a.v_ring + row * a.ring_stream_stride + head * HD;
+      for (int i = warp * 32 + lane; i < 2 * nk + 1; i += 32 * kPipeNP) {
+        if (i == 0) {
+          bulk_g2s(S + SM::q_off(nkl), a.q + fo, RB, &full[bi]);
+        } else {
+          const bool v = i > nk;
+          const int r = v ? i - 1 - nk : i - 1;
+          const __half* src;
+          if (r < nvis) {
+            int jj = pm1_mod - r;
+            if (jj < 0) jj += RING;
+            src = (v ? vr : kr) + jj * a.ring_slot_stride;
+          } else {
+            src = (v ? a.v_new : a.k_new) + fo;
+          }
+          bulk_g2s(S + (v ? SM::v_off(nkl) : 0) + r * RS, src, RB, &full[bi]);
+        }
       }
     }
-  }
-
-  // ---- softmax over row 0 (lanes 0-3 hold keys 8j + 2t4, +1 of every tile j); P rounded to fp16
-  float m = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int key = 8 * j + 2 * t4 + e;
-      const float x = (j < nt && key < nk) ? round_fp16(s[j][e]) * a.scale : -INFINITY;
-      s[j][e] = x;
-      m = fmaxf(m, x);
-    }
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-  float sum = 0.f;
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float x = (j < nt) ? expf(s[j][e] - m) : 0.f;   // masked keys: exp(-inf) = 0
-      s[j][e] = x;
-      sum += x;
-    }
-  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-  const float inv = 1.f / sum;                               // the frame always sees itself: sum > 0 (lanes 0-3)
-  float pmine = 0.f;
-#pragma unroll
-  for (int j = 0; j < NT; ++j)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int key = 8 * j + 2 * t4 + e;
-      float p = round_fp16(s[j][e] * inv);
-      if (key == nvis) {                                     // the frame's own key: kept apart from the ring sum
-        pmine = p;
-        p = 0.f;
+    if (k < nloc && lane == 0) {
+      // gave up (each producer warp, for the items it issued copies of): the stages issued last may still be landing; wait for them (bounded) before the CTA can exit
+      for (long long kk = k > kPipeNC * kPipeNS ? k - kPipeNC * kPipeNS : 0; kk < k; ++kk) {
+        const int bi = static_cast<int>(kk % kPipeNC) * kPipeNS + static_cast<int>((kk / kPipeNC) % kPipeNS);
+        mbar_wait_bounded(&full[bi], static_cast<uint32_t>((kk / kPipeNC / kPipeNS) & 1), 100000000ull);
       }
-      s[j][e] = lane < 4 ? p : 0.f;                          // rows 1-15 of the P operand are zero
     }
-  const float pself = __shfl_sync(0xffffffffu, pmine, (nvis & 7) >> 1);
-
-  if (!mbar_wait_bounded(&bar[1], 0)) {
-    give_up();
     return;
   }
-  // ---- O_ring = P_ring.V_ring: 16-key steps; ldmatrix.x4.trans gives the V fragments of two 8-dim tiles
-  float o[NTO][4];
-#pragma unroll
-  for (int jn = 0; jn < NTO; ++jn) o[jn][0] = o[jn][1] = o[jn][2] = o[jn][3] = 0.f;
-  const int ksteps = (nk + 15) >> 4;
-#pragma unroll
-  for (int kk = 0; kk < NT / 2; ++kk) {
-    if (kk < ksteps) {
-      const uint32_t pa0 = pack_half2(s[2 * kk][0], s[2 * kk][1]);        // keys 16kk + 2t4, +1
-      const uint32_t pa2 = pack_half2(s[2 * kk + 1][0], s[2 * kk + 1][1]);  // keys 16kk + 8 + 2t4, +1
-      const int key = 16 * kk + ((lane >> 3) & 1) * 8 + (lane & 7);
-      const uint32_t ra = v_base + key * RS + (lane >> 4) * 16;
-#pragma unroll
-      for (int np = 0; np < NTO / 2; ++np) {
-        uint32_t bf[4];
-        ldsm_x4_trans(key < nk ? ra + np * 32 : zero_addr, bf);
-        mma_f16(o[2 * np], pa0, 0u, pa2, 0u, bf[0], bf[1]);
-        mma_f16(o[2 * np + 1], pa0, 0u, pa2, 0u, bf[2], bf[3]);
+
+  // ---- consumer cw: items cw, cw + kPipeNC, ... of this CTA, stage j % kPipeNS of its own ring
+  const int cw = warp - kPipeNP;
+  const uint32_t zero_addr = smem_addr(sZero);
+  long long j = 0;
+  for (long long k = cw; k < nloc; k += kPipeNC, ++j) {
+    const int bi = cw * kPipeNS + static_cast<int>(j % kPipeNS);
+    if (!mbar_wait_bounded(&full[bi], static_cast<uint32_t>((j / kPipeNS) & 1))) {
+      if (lane == 0) {
+        atomicOr(a.status, kStatusWaitTimeout);
+        *abort_flag = 1;
       }
+      break;
     }
-  }
-
-  // ---- o = fp16(fp16(ring) + fp16(p_self v_self)): lanes 0-3 hold dims 8jn + 2t4, +1
-  if (lane < 4) {
-    const __half* vself = reinterpret_cast<const __half*>(sV + nvis * RS) + w * HD;
-    __half* op = a.out + b * a.out_batch_stride + (hg * G + w) * HD;
-#pragma unroll
-    for (int jn = 0; jn < NTO; ++jn) {
-      const int d = 8 * jn + 2 * t4;
-      const float2 vs = __half22float2(*reinterpret_cast<const __half2*>(vself + d));
-      *reinterpret_cast<__half2*>(op + d) = __floats2half2_rn(round_fp16(o[jn][0]) + round_fp16(pself * vs.x),
-                                                              round_fp16(o[jn][1]) + round_fp16(pself * vs.y));
-    }
-  }
-
-  // ---- the frame's columns into the ring (a slot outside every window of this launch, never staged)
-  if (a.write_new) {
-    constexpr int DPL = HD / 32;
-    const long long slot = ((pos % RING) + RING) % RING;
-    const long long off = row * a.ring_stream_stride + slot * a.ring_slot_stride + (hg * G + w) * HD + lane * DPL;
-    const __half* ks = reinterpret_cast<const __half*>(sK + nvis * RS) + w * HD + lane * DPL;
-    const __half* vs = reinterpret_cast<const __half*>(sV + nvis * RS) + w * HD + lane * DPL;
-#pragma unroll
-    for (int j = 0; j < DPL; j += 2) {
-      *reinterpret_cast<__half2*>(a.k_ring + off + j) = *reinterpret_cast<const __half2*>(ks + j);
-      *reinterpret_cast<__half2*>(a.v_ring + off + j) = *reinterpret_cast<const __half2*>(vs + j);
-    }
+    if (*abort_flag) break;
+    const uint8_t* S = smem + bi * SB;
+    const RingPipeHeader hd = *reinterpret_cast<const RingPipeHeader*>(S + SM::hdr_off(nkl));
+    const uint32_t sa = smem_addr(S);
+    ring_frame_head_mma<HD>(a, sa, sa + static_cast<uint32_t>(SM::v_off(nkl)), S + SM::q_off(nkl), S + hd.nvis * RS,
+                            S + SM::v_off(nkl) + hd.nvis * RS, RS, zero_addr, hd.nvis, hd.b, hd.head, hd.row,
+                            hd.pos, lane, []() -> bool { return true; });
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[bi]);
   }
 }
 
@@ -1074,6 +1255,26 @@ size_t ring_smem_bytes(int ring, int past, int hd, int n) { return RingGeom(ring
 int g_ring_frame_kernel = 2;
 int g_ring_chunk_kernel = 1;
 
+// The pipelined one-frame kernel: head_dim 64 and stage rings that fit the SM's shared memory (up to 88 visible rows).
+static bool pipe_fits(const RingArgs& a, int nv) {
+  return a.hd == 64 && RingPipeSmem<64>::bytes(nv + 1) <= 227u * 1024u;
+}
+
+static cudaError_t launch_frame_pipe(int nv, const RingArgs& a, cudaStream_t stream) {
+  static thread_local int sm_dev = -1, sms = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (sm_dev != dev) {
+    cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    sm_dev = dev;
+  }
+  const long long items = static_cast<long long>(a.B) * a.H;
+  const int grid = static_cast<int>(items < sms ? items : sms);
+  ring_attn_frame_pipe_kernel<64><<<grid, 32 * (kPipeNC + kPipeNP), RingPipeSmem<64>::bytes(nv + 1), stream>>>(a);
+  return cudaGetLastError();
+}
+
 template <int HD, int G>
 static cudaError_t set_mma_frame_smem() {
   return cudaFuncSetAttribute(ring_attn_frame_mma_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1127,6 +1328,9 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
     if (e == cudaSuccess) e = set_mma_frame_smem<64, 1>();
     if (e == cudaSuccess) e = set_mma_frame_smem<128, 2>();
     if (e == cudaSuccess) e = set_mma_frame_smem<128, 1>();
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ring_attn_frame_pipe_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(227u * 1024u));
     if (e == cudaSuccess) e = set_chunk_smem<64, 4>();
     if (e == cudaSuccess) e = set_chunk_smem<64, 2>();
     if (e == cudaSuccess) e = set_chunk_smem<64, 1>();
@@ -1137,6 +1341,7 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
   }
   if (a.B == 0 || a.n == 0) return cudaSuccess;
   const int nv = a.past < a.ring ? a.past : a.ring;
+  if (a.n == 1 && g_ring_frame_kernel == 5 && pipe_fits(a, nv)) return launch_frame_pipe(nv, a, stream);
   if (a.n == 1 && nv < kRingMmaMaxKeys) {
     // one frame on the tensor cores, G heads per CTA: 4 x 64 or 2 x 128 halves per staged row (selection 0; 3 and 4
     // take fewer heads per CTA); under 75 KB of shared memory per CTA at 71 visible rows, so three CTAs per SM

@@ -623,7 +623,8 @@ def _(q, k, v, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, prefi
 
 def set_ring_frame_kernel(kernel: int) -> int:
     """Select the one-frame ring attention kernel. 0: tensor cores, one warp per head, 4 x 64 or 2 x 128 heads per
-    CTA; 3: the same with 2 x 64 or 1 x 128; 4: one head per CTA; 2: scalar math, one warp per head, 4 x 64 or
+    CTA; 3: the same with 2 x 64 or 1 x 128; 4: one head per CTA; 5: persistent pipeline, one CTA per SM with a
+    producer warp and three tensor-core consumer warps (head_dim 64, past <= 88); 2: scalar math, one warp per head, 4 x 64 or
     2 x 128 heads per CTA; 1: scalar math, one CTA per (stream, head), always. Where the heads do not divide, 1 is
     used. Returns the previous selection."""
     return int(_lib.load().q3_set_ring_frame_kernel(int(kernel)))
@@ -645,6 +646,6 @@ def set_prefill_kernel(kernel: int) -> int:
 def set_decode_variant(variant: int) -> int:
     """Select the decode kernel variant (0: 8-token chunks x 3 stages, two CTAs/SM; 1: 16-token x 3, one CTA/SM;
     2: 8-token x 2, two CTAs/SM; 3 / 4: warp-MMA scoring with early stage release, 8-token x 3 / 2, two CTAs/SM;
-    5: dedicated producer warps, one CTA/SM running two 8-token x 3 chunk streams)."""
+    5 (default): dedicated producer warps, one CTA/SM running two 8-token x 3 chunk streams)."""
     _ws.clear()
     return int(_lib.load().q3_set_decode_variant(int(variant)))
