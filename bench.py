@@ -53,11 +53,11 @@ def parse():
     p.add_argument("--num-splits", type=int, default=0)
     p.add_argument("--prefill-kernel", type=int, default=0, help="prefill kernel (q3_set_prefill_kernel): 0 TMA, 1 single")
     p.add_argument("--ring-frame-kernel", type=int, default=2,
-                   help="one-frame ring kernel (q3_set_ring_frame_kernel): 0 tensor cores 4x64 heads per CTA, "
-                        "3 / 4 the same with 2 / 1 heads, 2 scalar heads per CTA, 1 scalar CTA per head")
+                   help="one-frame ring kernel (q3_set_ring_frame_kernel): 2 scalar heads per CTA (default), "
+                        "1 scalar CTA per head, 0 / 3 / 4 tensor cores 4 / 2 / 1 heads per CTA, 5 TMA pipeline")
     p.add_argument("--ring-chunk-kernel", type=int, default=1,
-                   help="multi-frame ring kernel (q3_set_ring_chunk_kernel): 0 tensor cores 2x64 heads per CTA, "
-                        "2 / 3 the same with 4 / 1 heads, 1 one CTA per head")
+                   help="multi-frame ring kernel (q3_set_ring_chunk_kernel): 1 one CTA per head (default), "
+                        "0 / 2 / 3 tensor cores 2 / 4 / 1 heads per CTA")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)

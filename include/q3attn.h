@@ -221,18 +221,18 @@ int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
  * reference's fp16 rounding points (scores, P and each P.V half rounded to fp16). write_new != 0 also stores the
  * chunk's K/V into ring slots (pos + j) % ring (the caller's index_copy_, decoder_stream.py:330-333).
  * head_dim 64 or 128, ring <= 128, n <= min(17, ring - past). out: [B, n, heads * head_dim] fp16. */
-/* One-frame ring kernel used by q3_ring_window_attn for n == 1 (and past < 96): 0 = tensor cores, one warp per head,
- * G heads per CTA (4 for head_dim 64, 2 for 128; default), 3 = the same with G = 2 / 1, 4 = G = 1; 5 = a persistent
- * pipeline, one CTA per SM with a producer warp staging (stream, head) items for three tensor-core consumer warps
- * (head_dim 64 and past <= 88; other calls use kernel 1); 2 = scalar math,
- * one warp per head, G = 4 / 2; 1 = scalar math, one CTA per (stream, head), always. Where G does not divide the head
- * count, kernel 1 runs. Other values leave the selection unchanged. Returns the previous value. No reference
- * counterpart (a tuning knob of this library). */
+/* One-frame ring kernel used by q3_ring_window_attn for n == 1: 2 = scalar math, one warp per head, G heads per CTA
+ * (4 for head_dim 64, 2 for 128; the default, the fastest measured); 1 = scalar math, one CTA per (stream, head);
+ * 0 = tensor cores, one warp per head, G = 4 / 2, 3 = G = 2 / 1, 4 = G = 1 (past < 96); 5 = a persistent TMA
+ * pipeline, quads of four warps per (stream, head) fed by producer warps (head_dim 64, past <= 97). Calls a selection
+ * does not fit (G not dividing the head count, sizes) run kernel 1. Other values leave the selection unchanged.
+ * Returns the previous value. No reference counterpart (a tuning knob of this library). */
 int q3_set_ring_frame_kernel(int kernel);
-/* Kernel used by q3_ring_window_attn for chunks of 2 .. 16 frames (past + n <= 112): 0 = tensor cores, one warp per
- * head, G heads per CTA (2 for head_dim 64, 1 for 128; default), 2 = G = 4 / 2, 3 = G = 1; 1 = one CTA per (stream,
- * head), always (also for 17 frames and where G does not divide the head count). Other values leave the selection
- * unchanged. Returns the previous value. No reference counterpart (a tuning knob of this library). */
+/* Kernel used by q3_ring_window_attn for chunks of 2 .. 17 frames: 1 = one CTA per (stream, head), tensor cores
+ * (the default, the fastest measured; also every call another selection does not fit); 0 = tensor cores, one warp per
+ * head, G heads per CTA (2 for head_dim 64, 1 for 128), 2 = G = 4 / 2, 3 = G = 1 (up to 16 frames, past + n <= 112).
+ * Other values leave the selection unchanged. Returns the previous value. No reference counterpart (a tuning knob of
+ * this library). */
 int q3_set_ring_chunk_kernel(int kernel);
 int q3_ring_window_attn(const void* q, const void* k_new, const void* v_new, int64_t qkv_batch_stride,
                         int64_t qkv_frame_stride, void* k_ring, void* v_ring, int64_t ring_stream_stride,

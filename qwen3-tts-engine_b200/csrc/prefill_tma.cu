@@ -32,6 +32,7 @@
 #include <cstring>
 
 #include "prefill_common.cuh"
+#include "tensor_map.cuh"
 
 namespace q3 {
 
@@ -574,26 +575,10 @@ __global__ void __launch_bounds__(kTwThreads, 2) prefill_tma_kernel(const __grid
 }
 
 // ---------------------------------------------------------------- host side
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_fn() {
-  static const EncodeTiled fn = []() -> EncodeTiled {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return nullptr;
-    return reinterpret_cast<EncodeTiled>(f);
-  }();
-  return fn;
-}
-
 // 3-D map over rows of `heads` x 128 bf16 (heads 256 bytes apart, rows row_bytes apart); box = 64 dims x 1 head x
 // box_rows rows, 128-byte swizzle, zero fill past the last row.
 bool make_rows_map(CUtensorMap* m, const void* base, long long rows, int heads, long long row_bytes, int box_rows) {
-  const EncodeTiled enc = encode_fn();
+  const EncodeTiled enc = tensor_map_encoder();
   if (!enc || rows <= 0 || rows > (1ll << 31) - 1) return false;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(heads),
                               static_cast<cuuint64_t>(rows)};

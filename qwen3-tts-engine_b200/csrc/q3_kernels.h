@@ -203,15 +203,12 @@ struct RingArgs {
 };
 size_t ring_smem_bytes(int ring, int past, int hd, int n);
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);
-// Which one-frame ring kernel launch_ring_attn uses: 0 = tensor cores, one warp per head, 4 x 64 / 2 x 128 heads per
-// CTA (default); 3 = the same with 2 x 64 / 1 x 128 and 4 = one head per CTA; 5 = the persistent pipeline (one CTA per
-// SM, producer warp + three tensor-core consumer warps; head_dim 64, past <= 88); 2 = scalar math, one warp per head,
-// 4 x 64 / 2 x 128 heads per CTA; 1 = scalar math, one CTA per (stream, head), always (also where the heads do not
-// divide).
+// Which one-frame ring kernel launch_ring_attn uses: 2 = scalar math, one warp per head, 4 x 64 / 2 x 128 heads per
+// CTA (default); 1 = scalar math, one CTA per (stream, head) (also every call another selection does not fit);
+// 0 / 3 / 4 = tensor cores, one warp per head, 4 / 2 / 1 heads of 64 per CTA; 5 = the persistent TMA pipeline.
 extern int g_ring_frame_kernel;
-// Which kernel runs chunks of 2 .. 16 frames: 0 = tensor cores, one warp per head, 2 x 64 / 1 x 128 heads per CTA
-// (default); 2 = 4 x 64 / 2 x 128; 3 = one head per CTA; 1 = one CTA per (stream, head) (also for 17 frames and where
-// the heads do not divide).
+// Which kernel runs chunks of 2 .. 17 frames: 1 = one CTA per (stream, head) (default, also every call another
+// selection does not fit); 0 / 2 / 3 = tensor cores, one warp per head, 2 / 4 / 1 heads of 64 per CTA.
 extern int g_ring_chunk_kernel;
 
 struct PrefillArgs {

@@ -13,16 +13,19 @@
 // so no query of this launch can see them, and each CTA writes only its own head after reading it.
 //
 // The ring rows that some query of the chunk sees form one contiguous range of distances d = 0 .. nvis-1 back from the
-// newest frame (the union over the chunk is query 0's window); every kernel stages them in shared memory in that order
-// (row d), followed by the chunk's rows. Ring rows no query sees are never read. The kernels (launch_ring_attn picks
-// one by chunk size and the q3_set_ring_frame_kernel / q3_set_ring_chunk_kernel selections):
-//   * ring_attn_frame_mma_kernel (one frame, default) and ring_attn_chunk_mma_kernel (2..16 frames, default): one warp
-//     per head, G heads per CTA, each staged row (the G heads of one slot) by one bulk copy into rows padded by 16
-//     bytes, both contractions on the tensor cores with P handed from the score fragments to the P.V fragments in
-//     registers; described where they are defined;
-//   * ring_attn_frame_heads_kernel (one frame): the same staging, scalar math, one warp per head;
-// and, one CTA per (stream, head) with 4 warps (used also where the heads do not divide G, and for 17 frames):
-//   * ring_attn_mma_kernel (2..17 frames): rows staged by 16-byte asynchronous copies; the two ring contractions run
+// newest frame (the union over the chunk is query 0's window); the kernels stage them in shared memory in that order
+// (row d), followed by the chunk's rows (the TMA pipeline in slot order). Ring rows no query sees are never used. The
+// kernels (launch_ring_attn picks one by chunk size and the q3_set_ring_frame_kernel / q3_set_ring_chunk_kernel
+// selections; the defaults are the fastest measured):
+//   * ring_attn_frame_heads_kernel (one frame, default): one warp per head, G heads per CTA, each staged row (the G
+//     heads of one slot) by one bulk copy, scalar math;
+//   * ring_attn_frame_mma_kernel (one frame) and ring_attn_chunk_mma_kernel (2..16 frames): the same staging into rows
+//     padded by 16 bytes, both contractions on the tensor cores with P handed from the score fragments to the P.V
+//     fragments in registers;
+//   * ring_attn_frame_tma_kernel (one frame): a persistent pipeline staging (stream, head) items by 2-D tensor boxes;
+// each described where it is defined; and, one CTA per (stream, head) with 4 warps (used also for every call another
+// selection does not fit):
+//   * ring_attn_mma_kernel (2..17 frames, default): rows staged by 16-byte asynchronous copies; the two ring contractions run
 //     on the tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulation): S = Q.K^T over 8-key column tiles (the
 //     chunk's keys included) and O_ring = P_ring.V_ring over 16-key steps with V fragments by ldmatrix.trans (V rows
 //     past nvis zeroed, so a zero probability never meets stale data); O_new = P_new.V_new (n <= 17 keys) is a few
@@ -31,8 +34,11 @@
 //   * ring_attn_frame_kernel (one frame): rows staged by one bulk copy each, scalar math.
 #include "q3_common.cuh"
 #include "q3_kernels.h"
+#include "tensor_map.cuh"
 
 #include <cuda_fp16.h>
+
+#include <cstring>
 
 namespace q3 {
 
@@ -850,87 +856,258 @@ __global__ void __launch_bounds__(32 * G) ring_attn_frame_mma_kernel(const RingA
                           });
 }
 
-// One query frame as a persistent pipeline: one CTA per SM walks the (stream, head) items c, c + grid, c + 2 grid, ...
-// of the launch. Warps 0 .. kPipeNP-1 are producers: for item k they wait until stage (k / kPipeNC) % kPipeNS of consumer
-// warp k % kPipeNC's ring is free; warp 0 writes the item's header (ring row, position, visible rows) there, and all
-// producer lanes stage the item's rows by bulk copies (q, then the visible ring rows of K and V by distance, then the
-// frame's k / v; rows padded by 16 bytes). The next kPipeNC warps are consumers, each running ring_frame_head_mma on its own items
-// in order, so one consumer's stages form a plain single-reader ring (no phase can be overtaken). While consumers
-// compute, later items stream in, so DRAM sees no gaps between waves of CTAs; the per-(stream, head) kernels wait for
-// all their rows before any math and then leave DRAM idle while they compute.
-constexpr int kPipeNC = 3, kPipeNS = 3, kPipeNP = 4;   // consumer warps, stages per consumer, producer warps
+// One query frame as a persistent TMA pipeline (head_dim 64). Each CTA walks (stream, head) items
+// c, c + grid, c + 2 grid, ... with kTqQuads quads of four consumer warps, each quad fed by its own producer warp
+// through a ring of kTqStages stages (full / empty mbarriers, one writer and one reader group per stage, so no phase
+// can be overtaken). Quad q takes items q, q + kTqQuads, ... of the CTA in order.
+//   * The producer stages an item with 2-D tensor boxes. The visible ring slots form one slot range, or two when the
+//     window wraps the ring. Each range goes in as boxes of 8 slots x 64 dims (1 KB, 128-byte swizzle) for K and V,
+//     so about 20 TMA operations instead of one bulk copy per row. q and the frame's own k / v come by 1-D bulk copies.
+//     A box may run up to 7 slots past its range (other frames' slots, or zero fill past the ring's end); those rows
+//     are masked out of the scores and read as the zero row by P.V, like every row outside the window.
+//   * The four consumer warps split the item's keys by 16-key steps (warp w takes steps w, w + 4). They exchange the
+//     row maximum, then the row sum, through shared memory, so P = fp16(exp(s - max) / sum) is rounded after the
+//     whole row is normalised, as the reference's softmax-then-cast does (decoder_stream.py:172-173). Each warp's P.V
+//     partial (fp32) is summed over the four warps before the fp16 rounding of the ring half (:173-175).
+// One warp per item is latency-bound (a dependent chain of ldmatrix, mma and shuffles per key tile). Splitting the
+// keys over a quad cuts that chain four-fold, and two CTAs per SM keep 20 warps resident. Loads of later items stream
+// while earlier ones are computed, so DRAM sees no wave-wide gaps.
+constexpr int kTqMaxKeys = 112;                              // staged rows + the frame's own key: 7 steps of 16
 
-template <int HD>
-struct RingPipeSmem {
-  static constexpr int kRB = HD * 2, kRS = kRB + 16;
-  __host__ __device__ static size_t v_off(int nkl) { return static_cast<size_t>(nkl) * kRS; }
-  __host__ __device__ static size_t q_off(int nkl) { return 2 * static_cast<size_t>(nkl) * kRS; }
-  __host__ __device__ static size_t hdr_off(int nkl) { return q_off(nkl) + kRS; }
-  __host__ __device__ static size_t stage_bytes(int nkl) { return hdr_off(nkl) + 32; }
-  __host__ __device__ static size_t zero_off(int nkl) { return kPipeNC * kPipeNS * stage_bytes(nkl); }
-  __host__ __device__ static size_t flag_off(int nkl) { return zero_off(nkl) + 16; }  // the 16-byte zero row, then
-  __host__ __device__ static size_t bar_off(int nkl) { return flag_off(nkl) + 16; }   // a give-up flag; full, empty
-  __host__ __device__ static size_t bytes(int nkl) { return bar_off(nkl) + 2 * kPipeNC * kPipeNS * 8; }
-};
-
-struct RingPipeHeader {
+struct RingTmaHeader {
   long long row, pos;
-  int nvis, b, head, pad;
+  int b, head;
+  int n1, r2, n2;                                            // rows [0, n1) and [r2, r2 + n2) hold visible slots
+  int pad;
 };
 
-template <int HD>
-__global__ void __launch_bounds__(32 * (kPipeNC + kPipeNP), 1) ring_attn_frame_pipe_kernel(const RingArgs a) {
-  using SM = RingPipeSmem<HD>;
-  extern __shared__ __align__(16) uint8_t smem[];
-  constexpr int RB = SM::kRB, RS = SM::kRS;
+// Rows per range are rounded up to 8 (one box), so two ranges of nvis <= NV rows together need floor8(NV + 14) rows.
+__host__ __device__ inline int tma_stage_rows(int nv) { return ((nv + 14) / 8) * 8; }
+
+template <int NQ, int NS>
+struct RingTmaSmem {
+  static constexpr int kRowBytes = 128;                      // 64 fp16 dims
+  __host__ __device__ static size_t v_off(int kr) { return static_cast<size_t>(kr) * kRowBytes; }
+  __host__ __device__ static size_t self_off(int kr) { return 2 * static_cast<size_t>(kr) * kRowBytes; }  // q, k, v
+  __host__ __device__ static size_t hdr_off(int kr) { return self_off(kr) + 3 * kRowBytes; }
+  __host__ __device__ static size_t stage_bytes(int kr) {
+    return (hdr_off(kr) + sizeof(RingTmaHeader) + 1023) & ~static_cast<size_t>(1023);
+  }
+  // per quad: row maxima [4], row sums [4], p_self, a give-up snapshot, then the four warps' P.V partials [4][64]
+  static constexpr size_t kXBytes = 64 + 4 * 64 * 4;
+  __host__ __device__ static size_t x_off(int kr) { return NQ * NS * stage_bytes(kr); }
+  __host__ __device__ static size_t zero_off(int kr) { return x_off(kr) + NQ * kXBytes; }
+  __host__ __device__ static size_t flag_off(int kr) { return zero_off(kr) + 16; }
+  __host__ __device__ static size_t bar_off(int kr) { return flag_off(kr) + 16; }   // full[quads][stages], then empty
+  __host__ __device__ static size_t bytes(int kr) { return bar_off(kr) + 2 * NQ * NS * 8 + 1024; }
+  static constexpr int kThreads = 32 * NQ * 5;               // a producer warp and four consumers per quad
+};
+
+struct RingTmaParams {
+  RingArgs a;
+  CUtensorMap km, vm;                                        // {64 dims, heads, slots, stream rows} of the K / V rings
+};
+
+__device__ __forceinline__ void quad_sync(int quad) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + quad) : "memory");
+}
+
+// One consumer warp's share of an item: 16-key steps wq and wq + 4 of the staged rows (K / V regions at k_reg / v_reg,
+// 1024-aligned, 128-byte rows swizzled by row & 7; the frame's own key is key kr, its k / v unswizzled in `self`).
+// The quad's four warps meet at three barriers per item: row maximum, row sum, P.V partials. `ok` is false after a
+// give-up: the warp still takes part in every barrier, but writes nothing outside shared memory.
+__device__ __forceinline__ void ring_tma_quad_math(const RingArgs& a, uint32_t k_reg, uint32_t v_reg,
+                                                   const uint8_t* self, int kr, uint32_t zero_addr,
+                                                   const RingTmaHeader& hd, float* xch, int quad, int wq, int lane,
+                                                   bool ok) {
+  constexpr int HD = 64;
+  constexpr int NTO = HD / 8;
+  const int t4 = lane & 3;
+  const int nsteps = (kr + 1 + 15) >> 4;                     // 16-key steps over the staged rows and the own key
+  const uint32_t self_addr = smem_addr(self);
+  auto visible_row = [&](int key) -> bool {
+    return key < kr && (key < hd.n1 || (key >= hd.r2 && key < hd.r2 + hd.n2));
+  };
+
+  uint32_t qa[HD / 16][2];
+#pragma unroll
+  for (int ks = 0; ks < HD / 16; ++ks) {
+    const uint32_t* qw = reinterpret_cast<const uint32_t*>(self + ks * 32);
+    qa[ks][0] = lane < 4 ? qw[t4] : 0u;
+    qa[ks][1] = lane < 4 ? qw[4 + t4] : 0u;
+  }
+  // ---- scores of this warp's steps (two 8-key tiles each), masked, fp16-rounded and scaled
+  float s[2][2][4];
+  float m = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int kk = wq + 4 * u;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      s[u][t][0] = s[u][t][1] = s[u][t][2] = s[u][t][3] = 0.f;
+      if (kk < nsteps) {
+        const int key = 16 * kk + 8 * t + (lane & 7);
+#pragma unroll
+        for (int kp = 0; kp < HD / 32; ++kp) {
+          const int c = kp * 4 + (lane >> 3);
+          const uint32_t addr = key < kr ? k_reg + key * 128 + ((c ^ (key & 7)) << 4)
+                                         : (key == kr ? self_addr + 128 + c * 16 : zero_addr);
+          uint32_t bf[4];
+          ldsm_x4(addr, bf);
+          mma_f16(s[u][t], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, bf[0], bf[1]);
+          mma_f16(s[u][t], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, bf[2], bf[3]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = 16 * kk + 8 * t + 2 * t4 + e;
+        const bool vis = kk < nsteps && (key == kr || visible_row(key));
+        const float x = vis ? round_fp16(s[u][t][e]) * a.scale : -INFINITY;
+        s[u][t][e] = x;
+        m = fmaxf(m, x);
+      }
+    }
+  }
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  if (lane == 0) xch[wq] = m;
+  quad_sync(quad);                                           // (1) row maxima
+  const float M = fmaxf(fmaxf(xch[0], xch[1]), fmaxf(xch[2], xch[3]));   // the own key is always visible: finite
+  float sum = 0.f;
+#pragma unroll
+  for (int u = 0; u < 2; ++u)
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float x = s[u][t][e] == -INFINITY ? 0.f : expf(s[u][t][e] - M);
+        s[u][t][e] = x;
+        sum += x;
+      }
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  if (lane == 0) xch[4 + wq] = sum;
+  quad_sync(quad);                                           // (2) row sums
+  const float inv = 1.f / (((xch[4] + xch[5]) + xch[6]) + xch[7]);
+  // ---- P = fp16(e / sum); the own key's probability kept apart from the ring sum
+#pragma unroll
+  for (int u = 0; u < 2; ++u)
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = 16 * (wq + 4 * u) + 8 * t + 2 * t4 + e;
+        float p = round_fp16(s[u][t][e] * inv);
+        if (key == kr) {
+          if (lane < 4) xch[8] = p;                          // one lane of one warp holds it
+          p = 0.f;
+        }
+        s[u][t][e] = lane < 4 ? p : 0.f;
+      }
+  // ---- this warp's P.V partial over its steps; rows without a visible slot read the zero row
+  float o[NTO][4];
+#pragma unroll
+  for (int jn = 0; jn < NTO; ++jn) o[jn][0] = o[jn][1] = o[jn][2] = o[jn][3] = 0.f;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int kk = wq + 4 * u;
+    if (kk < nsteps) {
+      const uint32_t pa0 = pack_half2(s[u][0][0], s[u][0][1]);
+      const uint32_t pa2 = pack_half2(s[u][1][0], s[u][1][1]);
+      const int key = 16 * kk + ((lane >> 3) & 1) * 8 + (lane & 7);
+      const bool vis = visible_row(key);
+#pragma unroll
+      for (int np = 0; np < NTO / 2; ++np) {
+        const int c = np * 2 + (lane >> 4);
+        uint32_t bf[4];
+        ldsm_x4_trans(vis ? v_reg + key * 128 + ((c ^ (key & 7)) << 4) : zero_addr, bf);
+        mma_f16(o[2 * np], pa0, 0u, pa2, 0u, bf[0], bf[1]);
+        mma_f16(o[2 * np + 1], pa0, 0u, pa2, 0u, bf[2], bf[3]);
+      }
+    }
+  }
+  float* part = xch + 16;                                    // [warp][64]
+  if (lane < 4) {
+#pragma unroll
+    for (int jn = 0; jn < NTO; ++jn) {
+      part[wq * 64 + 8 * jn + 2 * t4] = o[jn][0];
+      part[wq * 64 + 8 * jn + 2 * t4 + 1] = o[jn][1];
+    }
+  }
+  quad_sync(quad);                                           // (3) partials
+  // ---- warp wq writes dims 16 wq .. 16 wq + 15: o = fp16(fp16(sum of partials) + fp16(p_self v_self))
+  if (lane < 16 && ok) {
+    const int d = 16 * wq + lane;
+    const float ring = ((part[d] + part[64 + d]) + part[128 + d]) + part[192 + d];
+    const float vs = __half2float(reinterpret_cast<const __half*>(self + 256)[d]);
+    a.out[hd.b * a.out_batch_stride + hd.head * HD + d] = __float2half_rn(round_fp16(ring) + round_fp16(xch[8] * vs));
+  }
+  if (wq == 0 && ok && a.write_new) {
+    const int RING = a.ring;
+    const long long slot = ((hd.pos % RING) + RING) % RING;
+    const long long off = hd.row * a.ring_stream_stride + slot * a.ring_slot_stride + hd.head * HD + lane * 2;
+    *reinterpret_cast<__half2*>(a.k_ring + off) = *reinterpret_cast<const __half2*>(self + 128 + lane * 4);
+    *reinterpret_cast<__half2*>(a.v_ring + off) = *reinterpret_cast<const __half2*>(self + 256 + lane * 4);
+  }
+}
+
+template <int NQ, int NS, int MINB>
+__global__ void __launch_bounds__(32 * NQ * 5, MINB) ring_attn_frame_tma_kernel(const __grid_constant__ RingTmaParams P) {
+  using SMEM = RingTmaSmem<NQ, NS>;
+  constexpr int kTqQuads = NQ, kTqStages = NS;
+  const RingArgs& a = P.a;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  // 128-byte swizzled boxes need 1024-byte aligned destinations: align the dynamic shared memory base at run time
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int RING = a.ring;
   const int NV = a.past < RING ? a.past : RING;              // ring rows any frame can see (launch-wide)
-  const int nkl = NV + 1;
-  const size_t SB = SM::stage_bytes(nkl);
-  uint8_t* sZero = smem + SM::zero_off(nkl);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SM::bar_off(nkl));   // [consumer * kPipeNS + stage]
-  uint64_t* empty = full + kPipeNC * kPipeNS;
-  volatile int* abort_flag = reinterpret_cast<int*>(smem + SM::flag_off(nkl));
+  const int kr = tma_stage_rows(NV);
+  const size_t SB = SMEM::stage_bytes(kr);
+  uint8_t* sZero = smem + SMEM::zero_off(kr);
+  volatile int* abort_flag = reinterpret_cast<int*>(smem + SMEM::flag_off(kr));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SMEM::bar_off(kr));   // [quad * kTqStages + stage]
+  uint64_t* empty = full + NQ * NS;
   const long long items = static_cast<long long>(a.B) * a.H;
   const long long nloc = (items - blockIdx.x + gridDim.x - 1) / gridDim.x;   // this CTA's items (grid <= items)
 
   if (tid == 0) {
-    for (int i = 0; i < kPipeNC * kPipeNS; ++i) {
+    for (int i = 0; i < NQ * NS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], 4);
     }
+    *abort_flag = 0;
     fence_mbar_init();
   }
   if (tid < 4) reinterpret_cast<uint32_t*>(sZero)[tid] = 0u;
-  if (tid == 4) *abort_flag = 0;
   __syncthreads();
 
-  if (warp < kPipeNP) {
-    // ---- producers: all kPipeNP warps walk the same items; warp 0 lane 0 writes the header and the expected bytes,
-    //      the copies of an item are spread over every producer lane. The ring row and position of the next item are
-    //      loaded while the current one is issued.
-    long long k = 0;
+  if (warp < kTqQuads) {
+    // ---- producer of quad `warp`: items warp, warp + kTqQuads, ... of this CTA
+    const int quad = warp;
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&P.km)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&P.vm)) : "memory");
+    }
+    long long j = 0;
     long long nrow = 0, npos = 0;
-    if (nloc > 0) {
-      const int b0 = static_cast<int>(static_cast<long long>(blockIdx.x) / a.H);
+    if (quad < nloc) {
+      const int b0 = static_cast<int>((blockIdx.x + static_cast<long long>(quad) * gridDim.x) / a.H);
       nrow = a.ring_rows[b0];
       npos = a.pos[b0];
     }
-    for (; k < nloc; ++k) {
+    for (long long k = quad; k < nloc; k += kTqQuads, ++j) {
       const long long item = blockIdx.x + k * gridDim.x;
       const int b = static_cast<int>(item / a.H), head = static_cast<int>(item % a.H);
       const long long row = nrow, pos = npos;
-      if (k + 1 < nloc) {
-        const int bn = static_cast<int>((item + gridDim.x) / a.H);
+      if (k + kTqQuads < nloc) {                             // the next item's ring row and position, loaded early
+        const int bn = static_cast<int>((item + static_cast<long long>(kTqQuads) * gridDim.x) / a.H);
         nrow = a.ring_rows[bn];
         npos = a.pos[bn];
       }
-      const int cw = static_cast<int>(k % kPipeNC);
-      const long long j = k / kPipeNC;
-      const int st = static_cast<int>(j % kPipeNS);
-      const int bi = cw * kPipeNS + st;
-      if (j >= kPipeNS && !mbar_wait_bounded(&empty[bi], static_cast<uint32_t>((j / kPipeNS - 1) & 1))) {
+      const int bi = quad * kTqStages + static_cast<int>(j % kTqStages);
+      if (j >= kTqStages && !mbar_wait_bounded(&empty[bi], static_cast<uint32_t>((j / kTqStages - 1) & 1))) {
         if (lane == 0) {
           atomicOr(a.status, kStatusWaitTimeout);
           *abort_flag = 1;
@@ -938,75 +1115,89 @@ __global__ void __launch_bounds__(32 * (kPipeNC + kPipeNP), 1) ring_attn_frame_p
       }
       __syncwarp();
       if (*abort_flag) break;
+      // visible slots: distances 0 .. nvis-1 back from slot pm1 = (pos - 1) mod RING, i.e. slots
+      // [pm1 - nvis + 1, pm1], or [0, pm1] and [RING - (nvis - pm1 - 1), RING) when that wraps
       const long long pm1 = pos - 1;
       const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
       int nvis = NV;
       if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
-      const int nk = nvis + 1;
+      const int s_lo = pm1_mod - nvis + 1;
+      int seg1 = 0, n1 = nvis, seg2 = 0, n2 = 0;
+      if (s_lo >= 0) {
+        seg1 = s_lo;
+      } else {
+        n1 = pm1_mod + 1;
+        seg2 = RING + s_lo;
+        n2 = -s_lo;
+      }
+      const int r2 = (n1 + 7) & ~7;
+      const int nb1 = (n1 + 7) >> 3, nb2 = (n2 + 7) >> 3, nb = nb1 + nb2;
       uint8_t* S = smem + bi * SB;
-      if (warp == 0 && lane == 0) {
-        RingPipeHeader* hd = reinterpret_cast<RingPipeHeader*>(S + SM::hdr_off(nkl));
-        hd->row = row;
-        hd->pos = pos;
-        hd->nvis = nvis;
-        hd->b = b;
-        hd->head = head;
-        mbar_arrive_expect_tx(&full[bi], static_cast<uint32_t>(2 * nk + 1) * RB);   // release: the header is seen
+      if (lane == 0) {
+        RingTmaHeader* h = reinterpret_cast<RingTmaHeader*>(S + SMEM::hdr_off(kr));
+        h->row = row;
+        h->pos = pos;
+        h->b = b;
+        h->head = head;
+        h->n1 = n1;
+        h->r2 = r2;
+        h->n2 = n2;
+        mbar_arrive_expect_tx(&full[bi], static_cast<uint32_t>(2 * nb) * 1024u + 3u * 128u);   // release: header seen
       }
       __syncwarp();
-      const long long fo = b * a.qkv_batch_stride + head * HD;
-      const __half* kr = a.k_ring + row * a.ring_stream_stride + head * HD;
-      const __half* vr = a.v_ring + row * a.ring_stream_stride + head * HD;
-      for (int i = warp * 32 + lane; i < 2 * nk + 1; i += 32 * kPipeNP) {
-        if (i == 0) {
-          bulk_g2s(S + SM::q_off(nkl), a.q + fo, RB, &full[bi]);
+      const uint32_t sa = smem_addr(S), bar = smem_addr(&full[bi]);
+      const long long fo = b * a.qkv_batch_stride + head * 64;
+      for (int i = lane; i < 3 + 2 * nb; i += 32) {
+        if (i < 3) {
+          const __half* src = i == 0 ? a.q + fo : (i == 1 ? a.k_new + fo : a.v_new + fo);
+          bulk_g2s(S + SMEM::self_off(kr) + i * 128, src, 128, &full[bi]);
         } else {
-          const bool v = i > nk;
-          const int r = v ? i - 1 - nk : i - 1;
-          const __half* src;
-          if (r < nvis) {
-            int jj = pm1_mod - r;
-            if (jj < 0) jj += RING;
-            src = (v ? vr : kr) + jj * a.ring_slot_stride;
-          } else {
-            src = (v ? a.v_new : a.k_new) + fo;
-          }
-          bulk_g2s(S + (v ? SM::v_off(nkl) : 0) + r * RS, src, RB, &full[bi]);
+          const int t = i - 3, kv = t >= nb ? 1 : 0, bx = t - kv * nb;
+          const int slot = bx < nb1 ? seg1 + 8 * bx : seg2 + 8 * (bx - nb1);
+          const int r = bx < nb1 ? 8 * bx : r2 + 8 * (bx - nb1);
+          tma_load_4d(sa + static_cast<uint32_t>(kv ? SMEM::v_off(kr) : 0) + r * 128, kv ? &P.vm : &P.km, 0,
+                      head, slot, static_cast<int>(row), bar);
         }
       }
     }
-    if (k < nloc && lane == 0) {
-      // gave up (each producer warp, for the items it issued copies of): the stages issued last may still be landing; wait for them (bounded) before the CTA can exit
-      for (long long kk = k > kPipeNC * kPipeNS ? k - kPipeNC * kPipeNS : 0; kk < k; ++kk) {
-        const int bi = static_cast<int>(kk % kPipeNC) * kPipeNS + static_cast<int>((kk / kPipeNC) % kPipeNS);
-        mbar_wait_bounded(&full[bi], static_cast<uint32_t>((kk / kPipeNC / kPipeNS) & 1), 100000000ull);
-      }
+    const long long mine = (nloc - quad + kTqQuads - 1) / kTqQuads;
+    if (j < mine && lane == 0) {
+      // gave up: the stages issued last may still be landing; wait for them (bounded) before the CTA can exit
+      for (long long jj = j > kTqStages ? j - kTqStages : 0; jj < j; ++jj)
+        mbar_wait_bounded(&full[quad * kTqStages + static_cast<int>(jj % kTqStages)],
+                          static_cast<uint32_t>((jj / kTqStages) & 1), 100000000ull);
     }
     return;
   }
 
-  // ---- consumer cw: items cw, cw + kPipeNC, ... of this CTA, stage j % kPipeNS of its own ring
-  const int cw = warp - kPipeNP;
+  // ---- consumer warp wq of quad `quad`; every warp of a quad takes the same barriers, item after item, even after
+  //      a give-up (then writing nothing outside shared memory), and the quad leaves together
+  const int quad = (warp - kTqQuads) >> 2, wq = (warp - kTqQuads) & 3;
+  float* xch = reinterpret_cast<float*>(smem + SMEM::x_off(kr) + quad * SMEM::kXBytes);
   const uint32_t zero_addr = smem_addr(sZero);
   long long j = 0;
-  for (long long k = cw; k < nloc; k += kPipeNC, ++j) {
-    const int bi = cw * kPipeNS + static_cast<int>(j % kPipeNS);
-    if (!mbar_wait_bounded(&full[bi], static_cast<uint32_t>((j / kPipeNS) & 1))) {
+  for (long long k = quad; k < nloc; k += kTqQuads, ++j) {
+    const int bi = quad * kTqStages + static_cast<int>(j % kTqStages);
+    if (!mbar_wait_bounded(&full[bi], static_cast<uint32_t>((j / kTqStages) & 1))) {
       if (lane == 0) {
         atomicOr(a.status, kStatusWaitTimeout);
         *abort_flag = 1;
       }
-      break;
     }
-    if (*abort_flag) break;
+    __syncwarp();
+    const bool ok = *abort_flag == 0;
     const uint8_t* S = smem + bi * SB;
-    const RingPipeHeader hd = *reinterpret_cast<const RingPipeHeader*>(S + SM::hdr_off(nkl));
+    const RingTmaHeader hd = *reinterpret_cast<const RingTmaHeader*>(S + SMEM::hdr_off(kr));
     const uint32_t sa = smem_addr(S);
-    ring_frame_head_mma<HD>(a, sa, sa + static_cast<uint32_t>(SM::v_off(nkl)), S + SM::q_off(nkl), S + hd.nvis * RS,
-                            S + SM::v_off(nkl) + hd.nvis * RS, RS, zero_addr, hd.nvis, hd.b, hd.head, hd.row,
-                            hd.pos, lane, []() -> bool { return true; });
+    ring_tma_quad_math(a, sa, sa + static_cast<uint32_t>(SMEM::v_off(kr)), S + SMEM::self_off(kr), kr,
+                       zero_addr, hd, xch, quad, wq, lane, ok);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[bi]);
+    // one snapshot of the give-up flag per item, taken by warp 0 before the barrier, so all four warps of the quad
+    // break after the same item (the flag itself may change at any time)
+    if (wq == 0 && lane == 0) xch[9] = *abort_flag ? 1.f : 0.f;
+    quad_sync(quad);
+    if (xch[9] != 0.f) break;
   }
 }
 
@@ -1255,24 +1446,57 @@ size_t ring_smem_bytes(int ring, int past, int hd, int n) { return RingGeom(ring
 int g_ring_frame_kernel = 2;
 int g_ring_chunk_kernel = 1;
 
-// The pipelined one-frame kernel: head_dim 64 and stage rings that fit the SM's shared memory (up to 88 visible rows).
-static bool pipe_fits(const RingArgs& a, int nv) {
-  return a.hd == 64 && RingPipeSmem<64>::bytes(nv + 1) <= 227u * 1024u;
+// The pipelined TMA one-frame kernel: head_dim 64, stage rings that fit the SM's shared memory, row strides in whole
+// 16-byte units (tensor maps), and a driver that offers the tensor-map encoder. Otherwise *launched stays false.
+static bool make_ring_map(CUtensorMap* m, const void* base, const RingArgs& a) {
+  const EncodeTiled enc = tensor_map_encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || (a.ring_slot_stride * 2) % 16 ||
+      (a.ring_stream_stride * 2) % 16 || a.ring_slot_stride <= 0 || a.ring_stream_stride <= 0)
+    return false;
+  // the stream-row extent is not part of the call: the largest row coordinate a map can take, never reached
+  const cuuint64_t dims[4] = {64u, static_cast<cuuint64_t>(a.H), static_cast<cuuint64_t>(a.ring), 0x7fffffffu};
+  const cuuint64_t strides[3] = {128u, static_cast<cuuint64_t>(a.ring_slot_stride) * 2,
+                                 static_cast<cuuint64_t>(a.ring_stream_stride) * 2};
+  const cuuint32_t box[4] = {64u, 1u, 8u, 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static cudaError_t launch_frame_pipe(int nv, const RingArgs& a, cudaStream_t stream) {
+template <int NQ, int NS, int MINB>
+static cudaError_t launch_frame_tma_cfg(int nv, const RingArgs& a, cudaStream_t stream, bool* launched) {
+  using SMEM = RingTmaSmem<NQ, NS>;
+  *launched = false;
+  const int kr = tma_stage_rows(nv);
+  if (a.hd != 64 || kr + 1 > kTqMaxKeys || SMEM::bytes(kr) * MINB > 227u * 1024u) return cudaSuccess;
+  RingTmaParams p;
+  memset(&p, 0, sizeof(p));
+  p.a = a;
+  if (!make_ring_map(&p.km, a.k_ring, a) || !make_ring_map(&p.vm, a.v_ring, a)) return cudaSuccess;
   static thread_local int sm_dev = -1, sms = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (sm_dev != dev) {
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ring_attn_frame_tma_kernel<NQ, NS, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(227u * 1024u / MINB));
     if (e != cudaSuccess) return e;
     sm_dev = dev;
   }
   const long long items = static_cast<long long>(a.B) * a.H;
-  const int grid = static_cast<int>(items < sms ? items : sms);
-  ring_attn_frame_pipe_kernel<64><<<grid, 32 * (kPipeNC + kPipeNP), RingPipeSmem<64>::bytes(nv + 1), stream>>>(a);
+  const long long slots = static_cast<long long>(MINB) * sms;
+  const int grid = static_cast<int>(items < slots ? items : slots);
+  ring_attn_frame_tma_kernel<NQ, NS, MINB><<<grid, 32 * NQ * 5, SMEM::bytes(kr), stream>>>(p);
+  *launched = true;
   return cudaGetLastError();
+}
+
+// Two quads of two stages, two CTAs per SM: measured against three quads of three stages and two quads of four
+// stages at one CTA per SM (24.2-24.6 against 27.6-27.9 and 32.6 us per layer at 256 streams x 16 heads).
+static cudaError_t launch_frame_tma(int nv, const RingArgs& a, cudaStream_t stream, bool* launched) {
+  return launch_frame_tma_cfg<2, 2, 2>(nv, a, stream, launched);
 }
 
 template <int HD, int G>
@@ -1328,9 +1552,6 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
     if (e == cudaSuccess) e = set_mma_frame_smem<64, 1>();
     if (e == cudaSuccess) e = set_mma_frame_smem<128, 2>();
     if (e == cudaSuccess) e = set_mma_frame_smem<128, 1>();
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(ring_attn_frame_pipe_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(227u * 1024u));
     if (e == cudaSuccess) e = set_chunk_smem<64, 4>();
     if (e == cudaSuccess) e = set_chunk_smem<64, 2>();
     if (e == cudaSuccess) e = set_chunk_smem<64, 1>();
@@ -1341,7 +1562,11 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
   }
   if (a.B == 0 || a.n == 0) return cudaSuccess;
   const int nv = a.past < a.ring ? a.past : a.ring;
-  if (a.n == 1 && g_ring_frame_kernel == 5 && pipe_fits(a, nv)) return launch_frame_pipe(nv, a, stream);
+  if (a.n == 1 && g_ring_frame_kernel == 5) {
+    bool launched = false;
+    const cudaError_t e = launch_frame_tma(nv, a, stream, &launched);
+    if (e != cudaSuccess || launched) return e;
+  }
   if (a.n == 1 && nv < kRingMmaMaxKeys) {
     // one frame on the tensor cores, G heads per CTA: 4 x 64 or 2 x 128 halves per staged row (selection 0; 3 and 4
     // take fewer heads per CTA); under 75 KB of shared memory per CTA at 71 visible rows, so three CTAs per SM

@@ -622,18 +622,17 @@ def _(q, k, v, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, prefi
 
 
 def set_ring_frame_kernel(kernel: int) -> int:
-    """Select the one-frame ring attention kernel. 0: tensor cores, one warp per head, 4 x 64 or 2 x 128 heads per
-    CTA; 3: the same with 2 x 64 or 1 x 128; 4: one head per CTA; 5: persistent pipeline, one CTA per SM with a
-    producer warp and three tensor-core consumer warps (head_dim 64, past <= 88); 2: scalar math, one warp per head, 4 x 64 or
-    2 x 128 heads per CTA; 1: scalar math, one CTA per (stream, head), always. Where the heads do not divide, 1 is
-    used. Returns the previous selection."""
+    """Select the one-frame ring attention kernel. 2 (default): scalar math, one warp per head, 4 x 64 or 2 x 128
+    heads per CTA; 1: scalar math, one CTA per (stream, head); 0 / 3 / 4: tensor cores, one warp per head, 4 / 2 / 1
+    heads of 64 (2 / 1 / 1 of 128) per CTA; 5: persistent TMA pipeline, quads of four warps per (stream, head) fed by
+    producer warps (head_dim 64). Calls a selection does not fit run 1. Returns the previous selection."""
     return int(_lib.load().q3_set_ring_frame_kernel(int(kernel)))
 
 
 def set_ring_chunk_kernel(kernel: int) -> int:
-    """Select the ring attention kernel for chunks of 2 .. 16 frames. 0: tensor cores, one warp per head, 2 x 64 or
-    1 x 128 heads per CTA; 2: 4 x 64 or 2 x 128; 3: one head per CTA; 1: one CTA per (stream, head), always (also for
-    17 frames and where the heads do not divide). Returns the previous selection."""
+    """Select the ring attention kernel for chunks of 2 .. 17 frames. 1 (default): one CTA per (stream, head), tensor
+    cores, also for every call another selection does not fit; 0 / 2 / 3: tensor cores, one warp per head, 2 / 4 / 1
+    heads of 64 (1 / 2 / 1 of 128) per CTA, up to 16 frames. Returns the previous selection."""
     return int(_lib.load().q3_set_ring_chunk_kernel(int(kernel)))
 
 

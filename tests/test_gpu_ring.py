@@ -31,17 +31,17 @@ def q3():
 
 
 # (one-frame kernel, multi-frame kernel) pairs; together they cover every selection of both
-RING_KERNELS = [(0, 0), (1, 1), (2, 2), (3, 3), (4, 0), (5, 0)]
+RING_KERNELS = [(2, 1), (1, 1), (0, 0), (3, 2), (4, 3), (5, 0)]
 
 
-@pytest.fixture(params=RING_KERNELS, ids=["mma_default", "cta_per_head", "heads_wide", "heads_narrow", "mma_one", "pipe"],
+@pytest.fixture(params=RING_KERNELS, ids=["default", "cta_per_head", "mma_heads", "mma_narrow", "mma_one", "tma_pipe"],
                 autouse=True)
 def ring_kernels(q3, request):
-    """Every test runs on each kernel selection. One frame: 0 = tensor cores with 4 x 64 / 2 x 128 heads per CTA
-    (default), 3 = 2 x 64 / 1 x 128, 4 = one head per CTA, 5 = the persistent pipeline (head_dim 64), 2 = scalar math
-    with one warp per head, 1 = one CTA per (stream, head). Chunks of 2 .. 16 frames: 0 = tensor cores with 2 x 64 / 1 x 128 heads per CTA (default),
-    2 = 4 x 64 / 2 x 128, 3 = one head per CTA, 1 = one CTA per (stream, head). Heads that do not divide fall back
-    to one CTA per (stream, head), and 17 frames always do."""
+    """Every test runs on each kernel selection (one-frame kernel, multi-frame kernel). One frame: 2 = scalar math,
+    one warp per head, 4 x 64 / 2 x 128 heads per CTA (default); 1 = one CTA per (stream, head); 0 / 3 / 4 = tensor
+    cores with 4 / 2 / 1 heads of 64 per CTA; 5 = the persistent TMA pipeline (head_dim 64). Chunks of 2 .. 16 frames:
+    1 = one CTA per (stream, head) (default, also for 17 frames); 0 / 2 / 3 = tensor cores, one warp per head, with
+    2 / 4 / 1 heads of 64 per CTA. Heads that do not divide fall back to one CTA per (stream, head)."""
     frame, chunk = request.param
     prev_f = q3.set_ring_frame_kernel(frame)
     prev_c = q3.set_ring_chunk_kernel(chunk)
