@@ -45,6 +45,11 @@ const char* q3_last_cuda_error(void);
 int q3_device_sm_count(void);
 /* Read (and optionally clear) the device status word of the current device. Synchronous; not for the hot loop. */
 int q3_read_status(uint32_t* status_out, int clear);
+/* Self-test of the failure reporting every pipeline kernel shares: launches one kernel whose bounded wait (on an
+ * mbarrier nothing arrives on) expires after limit_ns (1 .. 100,000,000 ns), which raises Q3_STATUS_WAIT_TIMEOUT and
+ * returns; the context stays usable. Asynchronous on `stream`. No reference counterpart (the reference has no
+ * device-side waits). */
+int q3_selftest_bounded_wait(uint64_t limit_ns, void* stream);
 
 /* ---------------------------------------------------------------- paged decode attention
  * Replaces flash_attn_with_kvcache(q, k_cache, v_cache, k=, v=, cache_seqlens=, block_table=, softmax_scale=,

@@ -123,6 +123,15 @@ int q3_device_sm_count(void) {
   return sm_count(dev);
 }
 
+int q3_selftest_bounded_wait(uint64_t limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 100000000ull) return Q3_ERR_INVALID;
+  int dev = 0, rc = current_device(&dev);
+  if (rc != Q3_OK) return rc;
+  uint32_t* p = nullptr;
+  if ((rc = status_ptr(dev, &p)) != Q3_OK) return rc;
+  return record(q3::launch_bounded_wait_selftest(p, limit_ns, static_cast<cudaStream_t>(stream)));
+}
+
 int q3_read_status(uint32_t* status_out, int clear) {
   int dev = 0, rc = current_device(&dev);
   if (rc != Q3_OK) return rc;

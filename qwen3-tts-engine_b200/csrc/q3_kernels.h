@@ -41,6 +41,9 @@ struct DecodeArgs {
   float eps = 1e-6f;
 };
 
+// One CTA whose bounded mbarrier wait expires after limit_ns and raises the wait-timeout bit in *status.
+cudaError_t launch_bounded_wait_selftest(uint32_t* status, unsigned long long limit_ns, cudaStream_t stream);
+
 int decode_rows_per_chunk(int variant);
 int decode_ctas_per_sm(int variant);
 int decode_occupancy(int variant);   // resident CTAs per SM measured by the runtime (-1 on error)

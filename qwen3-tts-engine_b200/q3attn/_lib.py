@@ -63,6 +63,7 @@ SIGNATURES = {
     "q3_qk_norm_rope_rows": (ctypes.c_int, [_P, _I64, _NR, _I64, _P]),
     "q3_set_ring_frame_kernel": (ctypes.c_int, [ctypes.c_int]),
     "q3_set_ring_chunk_kernel": (ctypes.c_int, [ctypes.c_int]),
+    "q3_selftest_bounded_wait": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_void_p]),
     "q3_ring_window_attn": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _I32, _I32, _I32,
                                            _I32, _I32, _I32, _F32, _I32, _P, _I64, _I64, _P]),
     "q3_kv_copy_prefix": (ctypes.c_int, [_P, _P, _I64, _I64, _P, _P, _I32, _I64, _I32, _I32, _I32, _P, _P, _I32, _I32,
