@@ -57,7 +57,7 @@ def parse():
                         "1 scalar CTA per head, 0 / 3 / 4 tensor cores 4 / 2 / 1 heads per CTA, 5 TMA pipeline")
     p.add_argument("--ring-chunk-kernel", type=int, default=1,
                    help="multi-frame ring kernel (q3_set_ring_chunk_kernel): 1 one CTA per head (default), "
-                        "0 / 2 / 3 tensor cores 2 / 4 / 1 heads per CTA")
+                        "0 / 2 / 3 tensor cores 2 / 4 / 1 heads per CTA, 4 TMA pipeline")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)

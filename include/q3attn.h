@@ -235,7 +235,8 @@ int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
 int q3_set_ring_frame_kernel(int kernel);
 /* Kernel used by q3_ring_window_attn for chunks of 2 .. 17 frames: 1 = one CTA per (stream, head), tensor cores
  * (the default, the fastest measured; also every call another selection does not fit); 0 = tensor cores, one warp per
- * head, G heads per CTA (2 for head_dim 64, 1 for 128), 2 = G = 4 / 2, 3 = G = 1 (up to 16 frames, past + n <= 112).
+ * head, G heads per CTA (2 for head_dim 64, 1 for 128), 2 = G = 4 / 2, 3 = G = 1 (up to 16 frames, past + n <= 112);
+ * 4 = the persistent TMA pipeline of selection 5 above for 2 .. 8 frames (head_dim 64, 66 <= past <= 97).
  * Other values leave the selection unchanged. Returns the previous value. No reference counterpart (a tuning knob of
  * this library). */
 int q3_set_ring_chunk_kernel(int kernel);

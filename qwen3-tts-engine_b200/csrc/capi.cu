@@ -632,7 +632,7 @@ int q3_set_ring_frame_kernel(int kernel) {
 
 int q3_set_ring_chunk_kernel(int kernel) {
   const int prev = q3::g_ring_chunk_kernel;
-  if (kernel >= 0 && kernel <= 3) q3::g_ring_chunk_kernel = kernel;
+  if (kernel >= 0 && kernel <= 4) q3::g_ring_chunk_kernel = kernel;
   return prev;
 }
 

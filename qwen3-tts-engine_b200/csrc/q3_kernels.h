@@ -211,7 +211,8 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);
 // 0 / 3 / 4 = tensor cores, one warp per head, 4 / 2 / 1 heads of 64 per CTA; 5 = the persistent TMA pipeline.
 extern int g_ring_frame_kernel;
 // Which kernel runs chunks of 2 .. 17 frames: 1 = one CTA per (stream, head) (default, also every call another
-// selection does not fit); 0 / 2 / 3 = tensor cores, one warp per head, 2 / 4 / 1 heads of 64 per CTA.
+// selection does not fit); 0 / 2 / 3 = tensor cores, one warp per head, 2 / 4 / 1 heads of 64 per CTA; 4 = the
+// persistent TMA pipeline (2 .. 8 frames).
 extern int g_ring_chunk_kernel;
 
 struct PrefillArgs {

@@ -878,23 +878,28 @@ struct RingTmaHeader {
   long long row, pos;
   int b, head;
   int n1, r2, n2;                                            // rows [0, n1) and [r2, r2 + n2) hold visible slots
-  int pad;
+  int seg1, seg2;                                            // ... slots [seg1, seg1 + n1) and [seg2, seg2 + n2)
+  int pm1;                                                   // (pos - 1) mod RING: the newest frame's slot
 };
 
 // Rows per range are rounded up to 8 (one box), so two ranges of nvis <= NV rows together need floor8(NV + 14) rows.
 __host__ __device__ inline int tma_stage_rows(int nv) { return ((nv + 14) / 8) * 8; }
 
-template <int NQ, int NS>
+template <int NQ, int NS, int NF = 1>
 struct RingTmaSmem {
   static constexpr int kRowBytes = 128;                      // 64 fp16 dims
   __host__ __device__ static size_t v_off(int kr) { return static_cast<size_t>(kr) * kRowBytes; }
-  __host__ __device__ static size_t self_off(int kr) { return 2 * static_cast<size_t>(kr) * kRowBytes; }  // q, k, v
-  __host__ __device__ static size_t hdr_off(int kr) { return self_off(kr) + 3 * kRowBytes; }
+  // q rows [0, NF), the chunk's k rows [NF, 2 NF), its v rows [2 NF, 3 NF)
+  __host__ __device__ static size_t self_off(int kr) { return 2 * static_cast<size_t>(kr) * kRowBytes; }
+  __host__ __device__ static size_t hdr_off(int kr) { return self_off(kr) + 3 * NF * kRowBytes; }
   __host__ __device__ static size_t stage_bytes(int kr) {
     return (hdr_off(kr) + sizeof(RingTmaHeader) + 1023) & ~static_cast<size_t>(1023);
   }
-  // per quad: row maxima [4], row sums [4], p_self, a give-up snapshot, then the four warps' P.V partials [4][64]
-  static constexpr size_t kXBytes = 64 + 4 * 64 * 4;
+  // per quad, one frame: row maxima [4], row sums [4], p_self, a give-up snapshot (index 9), then the four warps' P.V
+  // partials [4][64]; a chunk: row maxima [4][8], row sums [4][8], the snapshot (index 64) (its P.V partials go to the
+  // stage's K region)
+  static constexpr size_t kXBytes = NF == 1 ? 64 + 4 * 64 * 4 : 512;
+  static constexpr int kFlag = NF == 1 ? 9 : 64;
   __host__ __device__ static size_t x_off(int kr) { return NQ * NS * stage_bytes(kr); }
   __host__ __device__ static size_t zero_off(int kr) { return x_off(kr) + NQ * kXBytes; }
   __host__ __device__ static size_t flag_off(int kr) { return zero_off(kr) + 16; }
@@ -1051,9 +1056,209 @@ __device__ __forceinline__ void ring_tma_quad_math(const RingArgs& a, uint32_t k
   }
 }
 
-template <int NQ, int NS, int MINB>
+// One consumer warp's share of a chunk of n = 2 .. NF frames (rows 0 .. n-1 of the A operand; q, the chunk's k and
+// v rows unswizzled in `self` at rows [0, NF), [NF, 2 NF), [2 NF, 3 NF)). Ring steps wq and wq + 4 as in
+// ring_tma_quad_math; warp 3 also takes the chunk's own keys as one extra 8-key tile. Per row i: a ring row at
+// distance d is visible when it holds a window slot and d <= past - 1 - i (decoder_stream.py:152-155), the chunk's key
+// jj when jj <= i (:156). Row maxima and sums are exchanged through xch ([4][8] each); the P.V partials (ring:
+// [4 warps][NF rows][64], chunk: [NF][64] fp32) go to `part`, the stage's K region, free once the scores are read.
+// o = fp16(fp16(sum of ring partials) + fp16(chunk partial)) (:173-175).
+template <int NF>
+__device__ __forceinline__ void ring_tma_chunk_math(const RingArgs& a, uint32_t k_reg, uint32_t v_reg,
+                                                    const uint8_t* self, float* part, int kr, uint32_t zero_addr,
+                                                    const RingTmaHeader& hd, float* xch, int quad, int wq, int lane,
+                                                    bool ok) {
+  constexpr int HD = 64;
+  constexpr int NTO = HD / 8;
+  const int n = a.n, g = lane >> 2, t4 = lane & 3;
+  const int RING = a.ring, PAST = a.past;
+  const int nrs = (kr + 15) >> 4;                            // 16-key steps over the staged ring rows
+  const uint32_t self_addr = smem_addr(self);
+  auto visible_row = [&](int key) -> bool {
+    return key < kr && (key < hd.n1 || (key >= hd.r2 && key < hd.r2 + hd.n2));
+  };
+  auto dist = [&](int key) -> int {                          // distance back from the newest frame of a visible row
+    const int slot = key < hd.n1 ? hd.seg1 + key : hd.seg2 + (key - hd.r2);
+    const int d = hd.pm1 - slot;
+    return d < 0 ? d + RING : d;
+  };
+
+  // ---- Q fragments: rows 0 .. n-1 of the A operand
+  uint32_t qa[HD / 16][4];
+  {
+    const int qr = ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks)
+      ldsm_x4(qr < n ? self_addr + qr * 128 + (ks * 2 + (lane >> 4)) * 16 : zero_addr, qa[ks]);
+  }
+  // ---- scores: ring steps wq, wq + 4, and (warp 3) the chunk's keys; only row g (< n <= 8) is real in each lane
+  float s[2][2][4], sn[4] = {0.f, 0.f, 0.f, 0.f};
+  float m = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int kk = wq + 4 * u;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      s[u][t][0] = s[u][t][1] = s[u][t][2] = s[u][t][3] = 0.f;
+      if (kk < nrs) {
+        const int key = 16 * kk + 8 * t + (lane & 7);
+#pragma unroll
+        for (int kp = 0; kp < HD / 32; ++kp) {
+          const int c = kp * 4 + (lane >> 3);
+          uint32_t bf[4];
+          ldsm_x4(key < kr ? k_reg + key * 128 + ((c ^ (key & 7)) << 4) : zero_addr, bf);
+          mma_f16(s[u][t], qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], bf[0], bf[1]);
+          mma_f16(s[u][t], qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2], qa[2 * kp + 1][3], bf[2], bf[3]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = 16 * kk + 8 * t + 2 * t4 + e;
+        const bool vis = kk < nrs && g < n && visible_row(key) && dist(key) <= PAST - 1 - g;
+        const float x = vis ? round_fp16(s[u][t][e]) * a.scale : -INFINITY;
+        s[u][t][e] = x;
+        m = fmaxf(m, x);
+      }
+    }
+  }
+  if (wq == 3) {
+    const int jj = lane & 7;                                 // the chunk's key this lane addresses
+#pragma unroll
+    for (int kp = 0; kp < HD / 32; ++kp) {
+      const int c = kp * 4 + (lane >> 3);
+      uint32_t bf[4];
+      ldsm_x4(jj < n ? self_addr + (NF + jj) * 128 + c * 16 : zero_addr, bf);
+      mma_f16(sn, qa[2 * kp][0], qa[2 * kp][1], qa[2 * kp][2], qa[2 * kp][3], bf[0], bf[1]);
+      mma_f16(sn, qa[2 * kp + 1][0], qa[2 * kp + 1][1], qa[2 * kp + 1][2], qa[2 * kp + 1][3], bf[2], bf[3]);
+    }
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int key = 2 * t4 + e;
+      const bool vis = g < n && key < n && key <= g;
+      const float x = vis ? round_fp16(sn[e]) * a.scale : -INFINITY;
+      sn[e] = x;
+      m = fmaxf(m, x);
+    }
+  }
+  // ---- row maxima and sums across the quad (lanes 4g .. 4g+3 hold row g)
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  if (t4 == 0) xch[wq * 8 + g] = m;
+  quad_sync(quad);                                           // (1) row maxima
+  const float M = fmaxf(fmaxf(xch[g], xch[8 + g]), fmaxf(xch[16 + g], xch[24 + g]));
+  float sum = 0.f;
+#pragma unroll
+  for (int u = 0; u < 2; ++u)
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float x = s[u][t][e] == -INFINITY ? 0.f : expf(s[u][t][e] - M);
+        s[u][t][e] = x;
+        sum += x;
+      }
+  if (wq == 3) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float x = sn[e] == -INFINITY ? 0.f : expf(sn[e] - M);
+      sn[e] = x;
+      sum += x;
+    }
+  }
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  if (t4 == 0) xch[32 + wq * 8 + g] = sum;
+  quad_sync(quad);                                           // (2) row sums
+  const float L = ((xch[32 + g] + xch[40 + g]) + xch[48 + g]) + xch[56 + g];
+  const float inv = L > 0.f ? 1.f / L : 0.f;                 // rows past n have no key
+#pragma unroll
+  for (int u = 0; u < 2; ++u)
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) s[u][t][e] = round_fp16(s[u][t][e] * inv);
+  sn[0] = round_fp16(sn[0] * inv);
+  sn[1] = round_fp16(sn[1] * inv);
+
+  // ---- ring P.V partial over this warp's steps (rows without a visible slot read the zero row)
+  float o[NTO][4];
+#pragma unroll
+  for (int jn = 0; jn < NTO; ++jn) o[jn][0] = o[jn][1] = o[jn][2] = o[jn][3] = 0.f;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int kk = wq + 4 * u;
+    if (kk < nrs) {
+      const uint32_t pa0 = pack_half2(s[u][0][0], s[u][0][1]);
+      const uint32_t pa2 = pack_half2(s[u][1][0], s[u][1][1]);
+      const int key = 16 * kk + ((lane >> 3) & 1) * 8 + (lane & 7);
+      const bool vis = visible_row(key);
+#pragma unroll
+      for (int np = 0; np < NTO / 2; ++np) {
+        const int c = np * 2 + (lane >> 4);
+        uint32_t bf[4];
+        ldsm_x4_trans(vis ? v_reg + key * 128 + ((c ^ (key & 7)) << 4) : zero_addr, bf);
+        mma_f16(o[2 * np], pa0, 0u, pa2, 0u, bf[0], bf[1]);
+        mma_f16(o[2 * np + 1], pa0, 0u, pa2, 0u, bf[2], bf[3]);
+      }
+    }
+  }
+  if (g < n) {
+#pragma unroll
+    for (int jn = 0; jn < NTO; ++jn) {
+      part[(wq * NF + g) * 64 + 8 * jn + 2 * t4] = o[jn][0];
+      part[(wq * NF + g) * 64 + 8 * jn + 2 * t4 + 1] = o[jn][1];
+    }
+  }
+  // ---- the chunk's P.V (warp 3): one 16-key step over its v rows, keys past n read the zero row
+  if (wq == 3) {
+#pragma unroll
+    for (int jn = 0; jn < NTO; ++jn) o[jn][0] = o[jn][1] = o[jn][2] = o[jn][3] = 0.f;
+    const uint32_t pa0 = pack_half2(sn[0], sn[1]);
+    const int key = ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+    for (int np = 0; np < NTO / 2; ++np) {
+      const int c = np * 2 + (lane >> 4);
+      uint32_t bf[4];
+      ldsm_x4_trans(key < n ? self_addr + (2 * NF + key) * 128 + c * 16 : zero_addr, bf);
+      mma_f16(o[2 * np], pa0, 0u, 0u, 0u, bf[0], bf[1]);
+      mma_f16(o[2 * np + 1], pa0, 0u, 0u, 0u, bf[2], bf[3]);
+    }
+    if (g < n) {
+#pragma unroll
+      for (int jn = 0; jn < NTO; ++jn) {
+        part[(4 * NF + g) * 64 + 8 * jn + 2 * t4] = o[jn][0];
+        part[(4 * NF + g) * 64 + 8 * jn + 2 * t4 + 1] = o[jn][1];
+      }
+    }
+  }
+  quad_sync(quad);                                           // (3) partials
+  // ---- warp wq writes dims 16 wq .. 16 wq + 15 of every row
+  if (lane < 16 && ok) {
+    const int d = 16 * wq + lane;
+    for (int i = 0; i < n; ++i) {
+      const float ring = ((part[i * 64 + d] + part[(NF + i) * 64 + d]) + part[(2 * NF + i) * 64 + d]) +
+                         part[(3 * NF + i) * 64 + d];
+      const float own = part[(4 * NF + i) * 64 + d];
+      a.out[hd.b * a.out_batch_stride + i * a.out_frame_stride + hd.head * HD + d] =
+          __float2half_rn(round_fp16(ring) + round_fp16(own));
+    }
+  }
+  // ---- the chunk's k / v into ring slots (pos + jj) % RING
+  if (ok && a.write_new) {
+    for (int jj = wq; jj < n; jj += 4) {
+      const long long slot = (((hd.pos + jj) % RING) + RING) % RING;
+      const long long off = hd.row * a.ring_stream_stride + slot * a.ring_slot_stride + hd.head * HD + lane * 2;
+      *reinterpret_cast<__half2*>(a.k_ring + off) = *reinterpret_cast<const __half2*>(self + (NF + jj) * 128 + lane * 4);
+      *reinterpret_cast<__half2*>(a.v_ring + off) =
+          *reinterpret_cast<const __half2*>(self + (2 * NF + jj) * 128 + lane * 4);
+    }
+  }
+  fence_proxy_async_smem();                                  // `part` (generic stores) is the next item's TMA target
+}
+
+template <int NQ, int NS, int MINB, int NF>
 __global__ void __launch_bounds__(32 * NQ * 5, MINB) ring_attn_frame_tma_kernel(const __grid_constant__ RingTmaParams P) {
-  using SMEM = RingTmaSmem<NQ, NS>;
+  using SMEM = RingTmaSmem<NQ, NS, NF>;
   constexpr int kTqQuads = NQ, kTqStages = NS;
   const RingArgs& a = P.a;
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -1071,6 +1276,7 @@ __global__ void __launch_bounds__(32 * NQ * 5, MINB) ring_attn_frame_tma_kernel(
   uint64_t* empty = full + NQ * NS;
   const long long items = static_cast<long long>(a.B) * a.H;
   const long long nloc = (items - blockIdx.x + gridDim.x - 1) / gridDim.x;   // this CTA's items (grid <= items)
+  const int nf = NF == 1 ? 1 : a.n;                          // frames of the chunk (1 .. NF)
 
   if (tid == 0) {
     for (int i = 0; i < NQ * NS; ++i) {
@@ -1142,17 +1348,21 @@ __global__ void __launch_bounds__(32 * NQ * 5, MINB) ring_attn_frame_tma_kernel(
         h->n1 = n1;
         h->r2 = r2;
         h->n2 = n2;
-        mbar_arrive_expect_tx(&full[bi], static_cast<uint32_t>(2 * nb) * 1024u + 3u * 128u);   // release: header seen
+        h->seg1 = seg1;
+        h->seg2 = seg2;
+        h->pm1 = pm1_mod;
+        mbar_arrive_expect_tx(&full[bi], static_cast<uint32_t>(2 * nb) * 1024u + static_cast<uint32_t>(3 * nf) * 128u);
       }
       __syncwarp();
       const uint32_t sa = smem_addr(S), bar = smem_addr(&full[bi]);
       const long long fo = b * a.qkv_batch_stride + head * 64;
-      for (int i = lane; i < 3 + 2 * nb; i += 32) {
-        if (i < 3) {
-          const __half* src = i == 0 ? a.q + fo : (i == 1 ? a.k_new + fo : a.v_new + fo);
-          bulk_g2s(S + SMEM::self_off(kr) + i * 128, src, 128, &full[bi]);
+      for (int i = lane; i < 3 * nf + 2 * nb; i += 32) {
+        if (i < 3 * nf) {                                    // q, then the chunk's k, then its v rows
+          const int kind = i / nf, f = i - kind * nf;
+          const __half* src = (kind == 0 ? a.q : (kind == 1 ? a.k_new : a.v_new)) + fo + f * a.qkv_frame_stride;
+          bulk_g2s(S + SMEM::self_off(kr) + (kind * NF + f) * 128, src, 128, &full[bi]);
         } else {
-          const int t = i - 3, kv = t >= nb ? 1 : 0, bx = t - kv * nb;
+          const int t = i - 3 * nf, kv = t >= nb ? 1 : 0, bx = t - kv * nb;
           const int slot = bx < nb1 ? seg1 + 8 * bx : seg2 + 8 * (bx - nb1);
           const int r = bx < nb1 ? 8 * bx : r2 + 8 * (bx - nb1);
           tma_load_4d(sa + static_cast<uint32_t>(kv ? SMEM::v_off(kr) : 0) + r * 128, kv ? &P.vm : &P.km, 0,
@@ -1189,15 +1399,19 @@ __global__ void __launch_bounds__(32 * NQ * 5, MINB) ring_attn_frame_tma_kernel(
     const uint8_t* S = smem + bi * SB;
     const RingTmaHeader hd = *reinterpret_cast<const RingTmaHeader*>(S + SMEM::hdr_off(kr));
     const uint32_t sa = smem_addr(S);
-    ring_tma_quad_math(a, sa, sa + static_cast<uint32_t>(SMEM::v_off(kr)), S + SMEM::self_off(kr), kr,
-                       zero_addr, hd, xch, quad, wq, lane, ok);
+    if constexpr (NF == 1)
+      ring_tma_quad_math(a, sa, sa + static_cast<uint32_t>(SMEM::v_off(kr)), S + SMEM::self_off(kr), kr, zero_addr,
+                         hd, xch, quad, wq, lane, ok);
+    else
+      ring_tma_chunk_math<NF>(a, sa, sa + static_cast<uint32_t>(SMEM::v_off(kr)), S + SMEM::self_off(kr),
+                              reinterpret_cast<float*>(smem + bi * SB), kr, zero_addr, hd, xch, quad, wq, lane, ok);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[bi]);
     // one snapshot of the give-up flag per item, taken by warp 0 before the barrier, so all four warps of the quad
     // break after the same item (the flag itself may change at any time)
-    if (wq == 0 && lane == 0) xch[9] = *abort_flag ? 1.f : 0.f;
+    if (wq == 0 && lane == 0) xch[SMEM::kFlag] = *abort_flag ? 1.f : 0.f;
     quad_sync(quad);
-    if (xch[9] != 0.f) break;
+    if (xch[SMEM::kFlag] != 0.f) break;
   }
 }
 
@@ -1464,12 +1678,15 @@ static bool make_ring_map(CUtensorMap* m, const void* base, const RingArgs& a) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NQ, int NS, int MINB>
+template <int NQ, int NS, int MINB, int NF>
 static cudaError_t launch_frame_tma_cfg(int nv, const RingArgs& a, cudaStream_t stream, bool* launched) {
-  using SMEM = RingTmaSmem<NQ, NS>;
+  using SMEM = RingTmaSmem<NQ, NS, NF>;
   *launched = false;
   const int kr = tma_stage_rows(nv);
   if (a.hd != 64 || kr + 1 > kTqMaxKeys || SMEM::bytes(kr) * MINB > 227u * 1024u) return cudaSuccess;
+  // a chunk: 2 .. NF frames, and the stage's K region must hold the P.V partials ([5 NF][64] fp32)
+  if (NF > 1 && (a.n < 2 || a.n > NF || static_cast<size_t>(kr) * 128 < static_cast<size_t>(5 * NF) * 64 * 4))
+    return cudaSuccess;
   RingTmaParams p;
   memset(&p, 0, sizeof(p));
   p.a = a;
@@ -1480,7 +1697,7 @@ static cudaError_t launch_frame_tma_cfg(int nv, const RingArgs& a, cudaStream_t 
   if (sm_dev != dev) {
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(ring_attn_frame_tma_kernel<NQ, NS, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(ring_attn_frame_tma_kernel<NQ, NS, MINB, NF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(227u * 1024u / MINB));
     if (e != cudaSuccess) return e;
     sm_dev = dev;
@@ -1488,7 +1705,7 @@ static cudaError_t launch_frame_tma_cfg(int nv, const RingArgs& a, cudaStream_t 
   const long long items = static_cast<long long>(a.B) * a.H;
   const long long slots = static_cast<long long>(MINB) * sms;
   const int grid = static_cast<int>(items < slots ? items : slots);
-  ring_attn_frame_tma_kernel<NQ, NS, MINB><<<grid, 32 * NQ * 5, SMEM::bytes(kr), stream>>>(p);
+  ring_attn_frame_tma_kernel<NQ, NS, MINB, NF><<<grid, 32 * NQ * 5, SMEM::bytes(kr), stream>>>(p);
   *launched = true;
   return cudaGetLastError();
 }
@@ -1496,7 +1713,11 @@ static cudaError_t launch_frame_tma_cfg(int nv, const RingArgs& a, cudaStream_t 
 // Two quads of two stages, two CTAs per SM: measured against three quads of three stages and two quads of four
 // stages at one CTA per SM (24.2-24.6 against 27.6-27.9 and 32.6 us per layer at 256 streams x 16 heads).
 static cudaError_t launch_frame_tma(int nv, const RingArgs& a, cudaStream_t stream, bool* launched) {
-  return launch_frame_tma_cfg<2, 2, 2>(nv, a, stream, launched);
+  return launch_frame_tma_cfg<2, 2, 2, 1>(nv, a, stream, launched);
+}
+
+static cudaError_t launch_chunk_tma(int nv, const RingArgs& a, cudaStream_t stream, bool* launched) {
+  return launch_frame_tma_cfg<2, 2, 2, 8>(nv, a, stream, launched);
 }
 
 template <int HD, int G>
@@ -1585,7 +1806,13 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
       }
     }
   }
-  if (a.n >= 2 && a.n <= kRingChunkMaxFrames && nv + a.n <= kRingChunkMaxKeys && g_ring_chunk_kernel != 1) {
+  if (a.n >= 2 && g_ring_chunk_kernel == 4) {
+    bool launched = false;
+    const cudaError_t e = launch_chunk_tma(nv, a, stream, &launched);
+    if (e != cudaSuccess || launched) return e;
+  }
+  if (a.n >= 2 && a.n <= kRingChunkMaxFrames && nv + a.n <= kRingChunkMaxKeys && g_ring_chunk_kernel != 1 &&
+      g_ring_chunk_kernel != 4) {
     // 2 .. 16 frames on the tensor cores, G heads per CTA: 2 x 64 / 1 x 128 (selection 0), 4 x 64 / 2 x 128 (2),
     // one head (3)
     const int sel = g_ring_chunk_kernel;

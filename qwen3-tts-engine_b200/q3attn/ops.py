@@ -632,7 +632,8 @@ def set_ring_frame_kernel(kernel: int) -> int:
 def set_ring_chunk_kernel(kernel: int) -> int:
     """Select the ring attention kernel for chunks of 2 .. 17 frames. 1 (default): one CTA per (stream, head), tensor
     cores, also for every call another selection does not fit; 0 / 2 / 3: tensor cores, one warp per head, 2 / 4 / 1
-    heads of 64 (1 / 2 / 1 of 128) per CTA, up to 16 frames. Returns the previous selection."""
+    heads of 64 (1 / 2 / 1 of 128) per CTA, up to 16 frames; 4: the persistent TMA pipeline (2 .. 8 frames, head_dim
+    64). Returns the previous selection."""
     return int(_lib.load().q3_set_ring_chunk_kernel(int(kernel)))
 
 

@@ -31,7 +31,7 @@ def q3():
 
 
 # (one-frame kernel, multi-frame kernel) pairs; together they cover every selection of both
-RING_KERNELS = [(2, 1), (1, 1), (0, 0), (3, 2), (4, 3), (5, 0)]
+RING_KERNELS = [(2, 1), (1, 1), (0, 0), (3, 2), (4, 3), (5, 4)]
 
 
 @pytest.fixture(params=RING_KERNELS, ids=["default", "cta_per_head", "mma_heads", "mma_narrow", "mma_one", "tma_pipe"],
@@ -41,7 +41,8 @@ def ring_kernels(q3, request):
     one warp per head, 4 x 64 / 2 x 128 heads per CTA (default); 1 = one CTA per (stream, head); 0 / 3 / 4 = tensor
     cores with 4 / 2 / 1 heads of 64 per CTA; 5 = the persistent TMA pipeline (head_dim 64). Chunks of 2 .. 16 frames:
     1 = one CTA per (stream, head) (default, also for 17 frames); 0 / 2 / 3 = tensor cores, one warp per head, with
-    2 / 4 / 1 heads of 64 per CTA. Heads that do not divide fall back to one CTA per (stream, head)."""
+    2 / 4 / 1 heads of 64 per CTA; 4 = the persistent TMA pipeline (2 .. 8 frames, head_dim 64). Calls a selection
+    does not fit fall back to one CTA per (stream, head)."""
     frame, chunk = request.param
     prev_f = q3.set_ring_frame_kernel(frame)
     prev_c = q3.set_ring_chunk_kernel(chunk)
