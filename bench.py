@@ -60,6 +60,9 @@ def parse():
                         "0 / 2 / 3 tensor cores 2 / 4 / 1 heads per CTA, 4 TMA pipeline")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--no-aux", action="store_true",
+                   help="skip the short timing of configs 3 / 4, the prefill and the ring attention that a 1-GPU "
+                        "config-2 run adds to its line under other_configs")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--cpu-seats", type=int, default=64)
     p.add_argument("--kernel-breakdown", action="store_true",
@@ -437,8 +440,9 @@ def bench_admit(a):
 
 
 def bench_aux(a):
-    """Configs 3 and 4 (reported in DESIGN, not the headline): device time per layer on one GPU, CUDA events over
-    graph replays, inputs resident; L2 is not flushed for c4 (its 38 MB per-layer scratch is L2-resident by design)."""
+    """Configs 3 and 4, the prefill part of 3 and the codec ring attention (not the headline), returned as a dict:
+    device time per layer on one GPU, CUDA events over graph replays, inputs resident; L2 is not flushed for c4 (its
+    38 MB per-layer scratch is L2-resident by design)."""
     import q3attn
     from q3attn import synth
     dev = torch.device("cuda", 0)
@@ -489,10 +493,9 @@ def bench_aux(a):
             q3attn.prefill_paged(qp, kpn, vpn, kp, vp, cu, cu, plen, zeros, sid, bt, SCALE, True, True)
         t_pre = timed(pre, a.steps)
         flops = 4 * 128 * 16 * np_ * (plen * (plen + 1) // 2)
-        print(json.dumps({"metric": "chunked prefill 10 x 320 tokens into fresh pages (C3 prefill part)",
-                          "workload": "prefill", "value": t_pre * 1e3, "unit": "us", "tflops": flops / t_pre / 1e9,
-                          "flops": flops}), flush=True)
-        return
+        return {"metric": "chunked prefill 10 x 320 tokens into fresh pages (C3 prefill part)",
+                "workload": "prefill", "value": t_pre * 1e3, "unit": "us", "tflops": flops / t_pre / 1e9,
+                "flops": flops}
     if a.workload == "ring":
         # the codec decoder's windowed ring attention, one layer per launch: 256 streams, an 88-slot ring, 72-frame
         # window, fp16; heads x head_dim 16 x 64 assumed (the codec's config is not part of the checkout)
@@ -514,12 +517,10 @@ def bench_aux(a):
             vis = int(torch.clamp(pos, max=71).sum())
             byt = (2 * vis + Bs * 4 * n) * H * hd * 2
             res[n] = {"us_per_layer": ms * 1e3 / L, "gbs": byt * L / ms / 1e6}
-        print(json.dumps({"metric": "codec decoder ring attention us per layer @256 streams (fp16, 16 x 64 heads)",
-                          "workload": "ring", "value": res[1]["us_per_layer"], "unit": "us per layer (1-frame chunk)",
-                          "chunk1": res[1], "chunk4": res[4], "layers_per_call": L,
-                          "reference_a100": "whole decoder call 14.1 / 44.5 ms at 256 streams x 1 / 4 frames"}),
-              flush=True)
-        return
+        return {"metric": "codec decoder ring attention us per layer @256 streams (fp16, 16 x 64 heads)",
+                "workload": "ring", "value": res[1]["us_per_layer"], "unit": "us per layer (1-frame chunk)",
+                "chunk1": res[1], "chunk4": res[4], "layers_per_call": L,
+                "reference_a100": "whole decoder call 14.1 / 44.5 ms at 256 streams x 1 / 4 frames"}
     if a.workload == "c4":
         B, L = a.seats, 5
         K = torch.randn((L, B, 8, 16, 128), generator=gen, device=dev, dtype=torch.bfloat16)
@@ -534,11 +535,10 @@ def bench_aux(a):
         ms = timed(frame, a.steps)
         launches = 16 * L
         byt = sum(B * (4096 * (p + 1) + 12288) for p in range(16)) * L
-        print(json.dumps({"metric": "code-predictor attention us per (step, layer) @576 seats", "workload": "c4",
-                          "value": ms * 1e3 / launches, "unit": "us", "frame_ms": ms, "launches_per_frame": launches,
-                          "bytes_per_frame": byt, "achieved_gbs": byt / ms / 1e6, "bound": "latency / L2 (not HBM)",
-                          "peak_hbm_gbs": peak}), flush=True)
-        return
+        return {"metric": "code-predictor attention us per (step, layer) @576 seats", "workload": "c4",
+                "value": ms * 1e3 / launches, "unit": "us", "frame_ms": ms, "launches_per_frame": launches,
+                "bytes_per_frame": byt, "achieved_gbs": byt / ms / 1e6, "bound": "latency / L2 (not HBM)",
+                "peak_hbm_gbs": peak}
     # c3: 470 decoding seats (ctx U[100,1500]) + 10 seats prefilling 320-token chunks into fresh pages, per layer
     lay, pseats, plen = synth.c3_layout(a.seed)
     nd = 470
@@ -571,11 +571,11 @@ def bench_aux(a):
     t_dec, t_pre, t_both = timed(dec, a.steps), timed(pre, a.steps), timed(both, a.steps)
     flops = 4 * 128 * 16 * np_ * (plen * (plen + 1) // 2)
     byt = synth.decode_bytes(lay.ctx[:nd] + 1)
-    print(json.dumps({"metric": "1.7B talker layer: decode (470 seats) + chunked prefill (10 x 320)", "workload": "c3",
-                      "value": t_both * 1e3, "unit": "us per layer", "decode_us": t_dec * 1e3,
-                      "decode_gbs": byt / t_dec / 1e6, "decode_frac_of_hbm": byt / t_dec / 1e6 / peak,
-                      "prefill_us": t_pre * 1e3, "prefill_tflops": flops / t_pre / 1e9, "prefill_flops": flops,
-                      "peak_hbm_gbs": peak, "peak_source": peak_kind}), flush=True)
+    return {"metric": "1.7B talker layer: decode (470 seats) + chunked prefill (10 x 320)", "workload": "c3",
+            "value": t_both * 1e3, "unit": "us per layer", "decode_us": t_dec * 1e3,
+            "decode_gbs": byt / t_dec / 1e6, "decode_frac_of_hbm": byt / t_dec / 1e6 / peak,
+            "prefill_us": t_pre * 1e3, "prefill_tflops": flops / t_pre / 1e9, "prefill_flops": flops,
+            "peak_hbm_gbs": peak, "peak_source": peak_kind}
 
 
 def main():
@@ -585,7 +585,8 @@ def main():
     if a.workload == "admit" and a.impl == "ours":
         return bench_admit(a)
     if a.workload != "c2" and a.impl == "ours":
-        return bench_aux(a)
+        print(json.dumps(bench_aux(a)), flush=True)
+        return
     if a.impl == "reference":
         return run_reference(a)
     import q3attn
@@ -759,13 +760,24 @@ def main():
     for g in graphs:
         del g
     graphs.clear()
+    # ---------------- the other configurations, timed briefly in the same run (1 GPU), outside the timed region
+    other = None
+    if rank == 0 and world == 1 and not a.no_aux:
+        import copy
+        other = {}
+        for w in ("c3", "c4", "prefill", "ring"):
+            b = copy.copy(a)
+            b.workload, b.steps, b.warmup = w, 20, 3
+            r = bench_aux(b)
+            other[w] = {k: v for k, v in r.items() if k not in ("workload", "reference_a100", "peak_hbm_gbs",
+                                                                "peak_source")}
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
                 "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic (seeded, BASELINE config 2 shapes; K/V N(0,1)*0.5)",
                 "config": config_dict(a, world), "gpu_launches": a.steps * L, "roofline": roof,
                 "e2e": e2e, "cpu_baseline": cpu, "clocks": clk,
-                "hbm_gbs_per_gpu": achieved, "hbm_frac_of_peak": achieved / peak}
+                "hbm_gbs_per_gpu": achieved, "hbm_frac_of_peak": achieved / peak, "other_configs": other}
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
