@@ -52,7 +52,7 @@ def ring_kernels(q3, request):
 
 
 @pytest.mark.parametrize("hd,H", [(64, 8), (128, 4), (64, 6), (128, 3)])
-@pytest.mark.parametrize("n", [1, 2, 4, 16, 17])
+@pytest.mark.parametrize("n", [1, 2, 4, 8, 16, 17])
 def test_ring_attention_matches_oracle(q3, hd, H, n):
     g = synth.cpu_gen(hd + n)
     pos = torch.tensor([0, 1, 5, 70, 71, 72, 87, 88, 150, 1000], dtype=torch.int64)
@@ -120,7 +120,7 @@ def test_decoder_transformer_matches_reference_stream(q3, golden_dir):
 
 
 @pytest.mark.parametrize("hd,H", [(64, 8), (128, 4)])
-@pytest.mark.parametrize("n", [1, 4, 16])
+@pytest.mark.parametrize("n", [1, 4, 8, 16])
 def test_ring_slots_no_query_sees_are_never_used(q3, hd, H, n):
     """Ring slots outside every query's window (never written yet, or older than the window) may hold anything, NaN
     included: the outputs equal those computed with the same slots zeroed."""
