@@ -11,12 +11,16 @@
 // per CTA; the last CTA to finish a (seat, KV head) -- decided by an atomic ticket, never by waiting -- merges them.
 // A seat inside one CTA is written directly.
 //
-// Inside a CTA there are 8 warps, one per KV head, and no dedicated producer: K and V of a chunk (ROWS token rows of
-// 2 KB, all 8 heads) are brought into a ring of NSTAGES shared-memory stages by one-dimensional TMA bulk copies
-// (cp.async.bulk) whose completion is counted on an mbarrier per stage. Warp 0 issues the first NSTAGES chunks; after
-// that, the warp that is LAST to finish reading a stage (a shared-memory ticket per stage) refills it with the chunk
-// NSTAGES further on. Keeping the CTA at 8 warps lets two CTAs share an SM at 128 registers per thread (the register
-// file is split over the SM's four sub-partitions, 16K registers each).
+// A chunk stream is read by 8 consumer warps, one per KV head: K and V of a chunk (ROWS token rows of 2 KB, all 8
+// heads) are brought into a ring of NSTAGES shared-memory stages by one-dimensional TMA bulk copies (cp.async.bulk)
+// whose completion is counted on an mbarrier per stage. Two ways to refill the stages:
+//   * paged_decode_kernel (variants 0-2): 8-warp CTAs, no dedicated producer. Warp 0 issues the first NSTAGES chunks;
+//     after that, the warp that is LAST to finish reading a stage (a shared-memory ticket per stage) refills it with
+//     the chunk NSTAGES further on. Keeping the CTA at 8 warps lets two CTAs share an SM at 128 registers per thread
+//     (the register file is split over the SM's four sub-partitions, 16K registers each).
+//   * paged_decode_ws_kernel (variant 5, the default): one CTA per SM with two streams, each refilled by a producer
+//     warp of its own (described where it is defined).
+// Both run the same consumer code (decode_consume).
 //
 // Scores: lane l of warp h scores row l / LPR of the chunk over DPL of the 128 dims, for both q heads of the group,
 // with packed fp32 FMAs (FFMA2); LPR lanes per row combine with shuffles. Online softmax in the exp2 domain.
