@@ -52,9 +52,10 @@ def parse():
     p.add_argument("--variant", type=int, default=5, help="decode kernel variant (q3_set_decode_variant)")
     p.add_argument("--num-splits", type=int, default=0)
     p.add_argument("--prefill-kernel", type=int, default=0, help="prefill kernel (q3_set_prefill_kernel): 0 TMA, 1 single")
-    p.add_argument("--ring-frame-kernel", type=int, default=2,
-                   help="one-frame ring kernel (q3_set_ring_frame_kernel): 2 scalar heads per CTA (default), "
-                        "1 scalar CTA per head, 0 / 3 / 4 tensor cores 4 / 2 / 1 heads per CTA, 5 TMA pipeline")
+    p.add_argument("--ring-frame-kernel", type=int, default=6,
+                   help="one-frame ring kernel (q3_set_ring_frame_kernel): 6 rows straight into registers (default), "
+                        "2 scalar heads per CTA, 1 scalar CTA per head, 0 / 3 / 4 tensor cores 4 / 2 / 1 heads per "
+                        "CTA, 5 TMA pipeline")
     p.add_argument("--ring-chunk-kernel", type=int, default=1,
                    help="multi-frame ring kernel (q3_set_ring_chunk_kernel): 1 one CTA per head (default), "
                         "0 / 2 / 3 tensor cores 2 / 4 / 1 heads per CTA, 4 TMA pipeline")

@@ -626,7 +626,7 @@ int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
 
 int q3_set_ring_frame_kernel(int kernel) {
   const int prev = q3::g_ring_frame_kernel;
-  if (kernel >= 0 && kernel <= 5) q3::g_ring_frame_kernel = kernel;
+  if (kernel >= 0 && kernel <= 6) q3::g_ring_frame_kernel = kernel;
   return prev;
 }
 

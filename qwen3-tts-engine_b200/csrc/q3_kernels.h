@@ -203,11 +203,16 @@ struct RingArgs {
   __half* out;                     // [B, n, H * hd]
   long long out_batch_stride, out_frame_stride;
   uint32_t* status;                // error bits (a staging wait that gave up)
+  // set by launch_ring_attn: the multiply-high reciprocal of ring (ceil(2^(63 + l) / ring), l = ceil(log2 ring)) and
+  // l - 1, through which the streaming kernel takes positions modulo the ring
+  unsigned long long ring_magic;
+  int ring_shift;
 };
 size_t ring_smem_bytes(int ring, int past, int hd, int n);
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);
-// Which one-frame ring kernel launch_ring_attn uses: 2 = scalar math, one warp per head, 4 x 64 / 2 x 128 heads per
-// CTA (default); 1 = scalar math, one CTA per (stream, head) (also every call another selection does not fit);
+// Which one-frame ring kernel launch_ring_attn uses: 6 = nothing staged, four warps per (stream, head) loading straight
+// into registers (default; head_dim 128 and wider windows go to 2); 2 = scalar math, one warp per head, 4 x 64 / 2 x 128
+// heads per CTA; 1 = scalar math, one CTA per (stream, head) (also every call another selection does not fit);
 // 0 / 3 / 4 = tensor cores, one warp per head, 4 / 2 / 1 heads of 64 per CTA; 5 = the persistent TMA pipeline.
 extern int g_ring_frame_kernel;
 // Which kernel runs chunks of 2 .. 17 frames: 1 = one CTA per (stream, head) (default, also every call another

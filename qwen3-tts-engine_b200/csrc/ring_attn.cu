@@ -13,12 +13,14 @@
 // so no query of this launch can see them, and each CTA writes only its own head after reading it.
 //
 // The ring rows that some query of the chunk sees form one contiguous range of distances d = 0 .. nvis-1 back from the
-// newest frame (the union over the chunk is query 0's window); the kernels stage them in shared memory in that order
-// (row d), followed by the chunk's rows (the TMA pipeline in slot order). Ring rows no query sees are never used. The
-// kernels (launch_ring_attn picks one by chunk size and the q3_set_ring_frame_kernel / q3_set_ring_chunk_kernel
-// selections; the defaults are the fastest measured):
-//   * ring_attn_frame_heads_kernel (one frame, default): one warp per head, G heads per CTA, each staged row (the G
-//     heads of one slot) by one bulk copy, scalar math;
+// newest frame (the union over the chunk is query 0's window); the kernels read them in that order (row d), followed
+// by the chunk's rows (the TMA pipeline in slot order). Ring rows no query sees are never used. The kernels
+// (launch_ring_attn picks one by chunk size and the q3_set_ring_frame_kernel / q3_set_ring_chunk_kernel selections;
+// the defaults are the fastest measured):
+//   * ring_attn_frame_stream_kernel (one frame, head_dim 64, default): four warps per (stream, head), every row
+//     loaded straight into registers, nothing staged;
+//   * ring_attn_frame_heads_kernel (one frame; head_dim 128 under the default): one warp per head, G heads per CTA,
+//     each staged row (the G heads of one slot) by one bulk copy into shared memory, scalar math;
 //   * ring_attn_frame_mma_kernel (one frame) and ring_attn_chunk_mma_kernel (2..16 frames): the same staging into rows
 //     padded by 16 bytes, both contractions on the tensor cores with P handed from the score fragments to the P.V
 //     fragments in registers;
@@ -1649,6 +1651,241 @@ __global__ void __launch_bounds__(32 * G) ring_attn_chunk_mma_kernel(const RingA
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------------
+// One query frame with nothing staged (selection 6, head_dim 64): each (stream, head) is one CTA of W = 4 warps, and
+// every K and V row the frame sees goes straight from HBM into registers, all loads issued before the first is used.
+// Warp w holds key rows r = 4 (W i + w) + g, i < P + R (distance order; the frame's own key is row nvis), lane
+// l = 8 g + c the 16-byte piece c (dims 8c .. 8c+7) of them: one load instruction of a warp reads four whole 128-byte
+// rows, and a lane keeps (P + R) x 2 pieces in flight.
+//   scores   per-lane partial dot products over 8 dims (fp32), completed over the 8 lanes of a row group by a
+//            transposing butterfly in a batch of P rows and one of R (afterwards lane c holds the score of batch index
+//            c / (8 / P), resp. P + c / (8 / R)); fp16-rounded, scaled in fp32 (decoder_stream.py:172);
+//   softmax  each warp's (max, sum of exp) pair meets the others' in shared memory, so every warp normalises with the
+//            whole row's max and sum before P is rounded to fp16 (:173);
+//   P.V      each lane takes its rows' probabilities by shuffles and accumulates its 8 dims; the four row groups meet by
+//            a second transposing butterfly (lane (g, c) ends with dims 8c + 2g, 8c + 2g + 1), warps 1 .. W-1 hand
+//            their partial sums (and p_self) to warp 0 through shared memory; o = fp16(fp16(ring) + fp16(p_self
+//            v_self)) (:174).
+// Measured against one warp per (stream, head) (18 rows per lane group, 168 registers), 2, 6 and 8 warps per item, and
+// a resident grid walking the items: four warps per item, one item per CTA, at nine CTAs per SM gave the shortest
+// layer (the number of items in flight per SM is what counts).
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 r;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t ld_nc_u1(const void* p) {
+  uint32_t r;
+  asm("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+
+// Sum the N per-lane values v (N a power of two, at most 8) over the 8 lanes of a lane group (xor offsets 4, 2, 1);
+// the result is the complete sum of value index c >> (3 - log2 N), c = lane & 7.
+template <int N>
+__device__ __forceinline__ float group8_transpose_sum(float (&v)[N], int c) {
+  static_assert(N >= 1 && N <= 8 && (N & (N - 1)) == 0, "N must be a power of two <= 8");
+  int off = 4;
+#pragma unroll
+  for (int n = N; n > 1; n >>= 1, off >>= 1) {
+    const bool up = (c & off) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = up ? v[i] : v[i + n / 2];
+      const float keep = up ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  float s = v[0];
+#pragma unroll
+  for (; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  return s;
+}
+
+// 8 fp16 of a 16-byte piece dotted with 8 fp32 (two chains of packed FMAs)
+__device__ __forceinline__ float dot8_h(const uint4 w, const float2 (&q)[4]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&w);
+  float2 a0 = __fmul2_rn(__half22float2(h[0]), q[0]);
+  float2 a1 = __fmul2_rn(__half22float2(h[1]), q[1]);
+  a0 = __ffma2_rn(__half22float2(h[2]), q[2], a0);
+  a1 = __ffma2_rn(__half22float2(h[3]), q[3], a1);
+  return (a0.x + a0.y) + (a1.x + a1.y);
+}
+
+// (pos - 1) mod RING, non-negative, for every int64 position, RING >= 2: division by the launch-invariant RING as a
+// multiply-high by magic = ceil(2^(63 + l) / RING), l = ceil(log2 RING), and a shift by l - 1, exact for dividends up to
+// 2^63 (Granlund and Montgomery, "Division by invariant integers using multiplication", 1994). pos - 1 >= 0 is divided
+// as it is; below that, (pos - 1) mod RING = RING - 1 - ((-pos) mod RING).
+__device__ __forceinline__ int ring_pm1_mod(long long pos, int ring, unsigned long long magic, int shift) {
+  const unsigned long long up = static_cast<unsigned long long>(pos);
+  const bool ge1 = pos >= 1;
+  const unsigned long long z = ge1 ? up - 1ull : 0ull - up;  // pos - 1, or -pos: both in [0, 2^63]
+  const unsigned long long q = __umul64hi(z, magic) >> shift;
+  const int r = static_cast<int>(z - q * static_cast<unsigned long long>(ring));
+  return ge1 ? r : ring - 1 - r;
+}
+
+constexpr int kRingStreamWarps = 4;
+constexpr int kRingStreamRows = 5;                           // rows per lane group and warp: P + R = 4 + 1
+constexpr int kRingStreamMaxKeys = 4 * kRingStreamWarps * kRingStreamRows;   // ring rows + the frame's own key: 80
+
+__global__ void __launch_bounds__(32 * kRingStreamWarps) ring_attn_frame_stream_kernel(const RingArgs a) {
+  constexpr int HD = 64, W = kRingStreamWarps, P = 4, R = 1, RPL = P + R;
+  static_assert(RPL == kRingStreamRows, "row batches");
+  constexpr int SP = 8 / P, SR = 8 / R;                      // lanes holding one completed score of a batch
+  __shared__ float2 s_ml[W];                                 // (max, sum of exp(s - max)) per warp
+  __shared__ float3 s_acc[W - 1][32];                        // warps 1 .. W-1: two output dims and p_self per lane
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, c = lane & 7;
+  const int b = static_cast<int>(blockIdx.x / a.H), head = static_cast<int>(blockIdx.x % a.H);   // grid = B * H
+  const int RING = a.ring;
+  const int NV = a.past < RING ? a.past : RING;              // ring rows any frame can see (launch-wide)
+  const long long row = a.ring_rows[b];
+  const long long pos = a.pos[b];
+  const int pm1_mod = ring_pm1_mod(pos, RING, a.ring_magic, a.ring_shift);   // distance d: slot (pos-1-d) mod RING
+  int nvis = NV;
+  if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
+  const int nk = nvis + 1;                                   // <= kRingStreamMaxKeys (checked by the launcher)
+
+  // ---- every load, K first: ring rows by distance and the frame's own key; V of the ring rows only (the frame's own
+  //      value enters through p_self)
+  const long long fo = b * a.qkv_batch_stride + head * HD;   // the frame's q / k / v row of this head
+  const long long ro = row * a.ring_stream_stride + head * HD + c * 8;
+  const int d0 = 8 * c + 2 * g;                              // the two output dims of this lane
+  const uint4 qw = ld_stream_v4(a.q + fo + c * 8);
+  uint32_t vself_w = 0u, kself_w = 0u;
+  if (w == 0) {
+    vself_w = ld_nc_u1(a.v_new + fo + d0);
+    if (a.write_new) kself_w = ld_nc_u1(a.k_new + fo + d0);
+  }
+  uint4 kw[RPL], vw[RPL];
+#pragma unroll
+  for (int i = 0; i < RPL; ++i) {
+    const int r = 4 * (W * i + w) + g;
+    kw[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (r < nvis) {
+      int j = pm1_mod - r;
+      if (j < 0) j += RING;
+      kw[i] = ld_stream_v4(a.k_ring + ro + j * a.ring_slot_stride);
+    } else if (r == nvis) {
+      kw[i] = ld_stream_v4(a.k_new + fo + c * 8);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < RPL; ++i) {
+    const int r = 4 * (W * i + w) + g;
+    vw[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (r < nvis) {
+      int j = pm1_mod - r;
+      if (j < 0) j += RING;
+      vw[i] = ld_stream_v4(a.v_ring + ro + j * a.ring_slot_stride);
+    }
+  }
+
+  // ---- scores
+  float2 q2[4];
+  {
+    const __half2* qh = reinterpret_cast<const __half2*>(&qw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) q2[j] = __half22float2(qh[j]);
+  }
+  float s[2];
+  {
+    float part[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) part[i] = dot8_h(kw[i], q2);
+    s[0] = group8_transpose_sum<P>(part, c);
+    float rest[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) rest[i] = dot8_h(kw[P + i], q2);
+    s[1] = group8_transpose_sum<R>(rest, c);
+  }
+  const int rr[2] = {4 * (W * (c / SP) + w) + g, 4 * (W * (P + c / SR) + w) + g};
+  const bool first[2] = {(c % SP) == 0, (c % SR) == 0};      // the lane that counts a duplicated score once
+  float mw = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    s[u] = rr[u] < nk ? round_fp16(s[u]) * a.scale : -INFINITY;
+    mw = fmaxf(mw, s[u]);
+  }
+  mw = warp_max(mw);
+  float lw = 0.f;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) lw += (rr[u] < nk && first[u]) ? expf(s[u] - mw) : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+  // ---- the row's max and sum over the W warps (a warp with no visible key reports (-inf, 0))
+  if (lane == 0) s_ml[w] = make_float2(mw, lw);
+  __syncthreads();
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < W; ++j) m = fmaxf(m, s_ml[j].x);       // finite: the frame's own key is in some warp
+  float l = 0.f;
+#pragma unroll
+  for (int j = 0; j < W; ++j) l += s_ml[j].y > 0.f ? s_ml[j].y * expf(s_ml[j].x - m) : 0.f;
+  const float inv = 1.f / l;
+  float p[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) p[u] = rr[u] < nk ? round_fp16(expf(s[u] - m) * inv) : 0.f;
+  // p_self, on the warp holding row nvis = 4 (W i_s + w_s) + g_s
+  const int qd = nvis >> 2, w_s = qd % W, i_s = qd / W, g_s = nvis & 3;
+  float pself = 0.f;
+  if (w == w_s)
+    pself = __shfl_sync(0xffffffffu, i_s < P ? p[0] : p[1], 8 * g_s + (i_s < P ? i_s * SP : (i_s - P) * SR));
+
+  // ---- P_ring.V_ring over this lane's rows (V of rows >= nvis is zero), then over the row groups and the warps
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+  for (int i = 0; i < RPL; ++i) {
+    const float pi = i < P ? __shfl_sync(0xffffffffu, p[0], 8 * g + i * SP)
+                           : __shfl_sync(0xffffffffu, p[1], 8 * g + (i - P) * SR);
+    const float2 pp = make_float2(pi, pi);
+    const __half2* vh = reinterpret_cast<const __half2*>(&vw[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 t = make_float2(acc[2 * j], acc[2 * j + 1]);
+      t = __ffma2_rn(__half22float2(vh[j]), pp, t);
+      acc[2 * j] = t.x;
+      acc[2 * j + 1] = t.y;
+    }
+  }
+#pragma unroll
+  for (int n = 8, off = 16; n > 2; n >>= 1, off >>= 1) {
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = up ? acc[i] : acc[i + n / 2];
+      const float keep = up ? acc[i + n / 2] : acc[i];
+      acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  if (w > 0) s_acc[w > 0 ? w - 1 : 0][lane] = make_float3(acc[0], acc[1], pself);
+  __syncthreads();
+  if (w > 0) return;
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) {
+    const float3 t = s_acc[j][lane];
+    acc[0] += t.x;
+    acc[1] += t.y;
+    pself += t.z;
+  }
+  const float2 vs = __half22float2(*reinterpret_cast<const __half2*>(&vself_w));
+  __half* op = a.out + b * a.out_batch_stride + head * HD + d0;
+  *reinterpret_cast<__half2*>(op) = __floats2half2_rn(round_fp16(acc[0]) + round_fp16(pself * vs.x),
+                                                      round_fp16(acc[1]) + round_fp16(pself * vs.y));
+  // ---- the frame's columns into the ring (a slot outside every window of this launch, never loaded)
+  if (a.write_new) {
+    const int pos_mod = pm1_mod + 1 == RING ? 0 : pm1_mod + 1;
+    const long long off = row * a.ring_stream_stride + pos_mod * a.ring_slot_stride + head * HD + d0;
+    *reinterpret_cast<uint32_t*>(a.k_ring + off) = kself_w;
+    *reinterpret_cast<uint32_t*>(a.v_ring + off) = vself_w;
+  }
+}
+
 static size_t frame_smem_bytes(int ring, int past, int hd) {
   const int nv = past < ring ? past : ring;
   return static_cast<size_t>(2 * (nv + 1) + 1) * hd * sizeof(__half) + static_cast<size_t>((nv + 1 + 3) & ~3) * 4 +
@@ -1657,7 +1894,16 @@ static size_t frame_smem_bytes(int ring, int past, int hd) {
 
 size_t ring_smem_bytes(int ring, int past, int hd, int n) { return RingGeom(ring, past, n).bytes(hd, n); }
 
-int g_ring_frame_kernel = 2;
+int g_ring_frame_kernel = 6;
+
+// ceil(2^(63 + l) / d) and l - 1, l = ceil(log2 d), for ring_pm1_mod (2 <= d <= kRingMaxSlots)
+static void ring_reciprocal(int d, unsigned long long* magic, int* shift) {
+  int l = 1;
+  while ((1 << l) < d) ++l;
+  const unsigned __int128 num = static_cast<unsigned __int128>(1) << (63 + l);
+  *magic = static_cast<unsigned long long>((num + static_cast<unsigned>(d) - 1u) / static_cast<unsigned>(d));
+  *shift = l - 1;
+}
 int g_ring_chunk_kernel = 1;
 
 // The pipelined TMA one-frame kernel: head_dim 64, stage rings that fit the SM's shared memory, row strides in whole
@@ -1828,8 +2074,18 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
       return launch_chunk<128, 1>(cgrid, nv, a, stream);
     }
   }
-  if (a.n == 1 && g_ring_frame_kernel == 2 && nv <= 95) {
-    // one frame, scalar math, G heads per CTA (4 x 64 or 2 x 128 halves per staged row)
+  if (a.n == 1 && g_ring_frame_kernel == 6 && a.hd == 64 && a.ring >= 2 && nv + 1 <= kRingStreamMaxKeys &&
+      static_cast<long long>(a.B) * a.H <= 2147483647ll) {
+    // one frame, nothing staged: a CTA of four warps per (stream, head)
+    RingArgs s = a;
+    ring_reciprocal(a.ring, &s.ring_magic, &s.ring_shift);
+    ring_attn_frame_stream_kernel<<<static_cast<unsigned>(static_cast<long long>(a.B) * a.H), 32 * kRingStreamWarps, 0,
+                                    stream>>>(s);
+    return cudaGetLastError();
+  }
+  if (a.n == 1 && (g_ring_frame_kernel == 2 || g_ring_frame_kernel == 6) && nv <= 95) {
+    // one frame, scalar math, G heads per CTA (4 x 64 or 2 x 128 halves per staged row); also the calls selection 6
+    // does not fit (head_dim 128, wider windows)
     const int G = a.hd == 64 ? 4 : 2;
     if (a.H % G == 0) {
       const dim3 hgrid(a.H / G, a.B);

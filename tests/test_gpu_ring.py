@@ -31,18 +31,19 @@ def q3():
 
 
 # (one-frame kernel, multi-frame kernel) pairs; together they cover every selection of both
-RING_KERNELS = [(2, 1), (1, 1), (0, 0), (3, 2), (4, 3), (5, 4)]
+RING_KERNELS = [(6, 1), (2, 1), (1, 1), (0, 0), (3, 2), (4, 3), (5, 4)]
 
 
-@pytest.fixture(params=RING_KERNELS, ids=["default", "cta_per_head", "mma_heads", "mma_narrow", "mma_one", "tma_pipe"],
-                autouse=True)
+@pytest.fixture(params=RING_KERNELS, autouse=True,
+                ids=["default", "heads", "cta_per_head", "mma_heads", "mma_narrow", "mma_one", "tma_pipe"])
 def ring_kernels(q3, request):
-    """Every test runs on each kernel selection (one-frame kernel, multi-frame kernel). One frame: 2 = scalar math,
-    one warp per head, 4 x 64 / 2 x 128 heads per CTA (default); 1 = one CTA per (stream, head); 0 / 3 / 4 = tensor
-    cores with 4 / 2 / 1 heads of 64 per CTA; 5 = the persistent TMA pipeline (head_dim 64). Chunks of 2 .. 16 frames:
-    1 = one CTA per (stream, head) (default, also for 17 frames); 0 / 2 / 3 = tensor cores, one warp per head, with
-    2 / 4 / 1 heads of 64 per CTA; 4 = the persistent TMA pipeline (2 .. 8 frames, head_dim 64). Calls a selection
-    does not fit fall back to one CTA per (stream, head)."""
+    """Every test runs on each kernel selection (one-frame kernel, multi-frame kernel). One frame: 6 = nothing staged,
+    four warps per (stream, head) loading straight into registers (default; head_dim 128 runs 2); 2 = scalar math, one
+    warp per head, 4 x 64 / 2 x 128 heads per CTA; 1 = one CTA per (stream, head); 0 / 3 / 4 = tensor cores with
+    4 / 2 / 1 heads of 64 per CTA; 5 = the persistent TMA pipeline (head_dim 64). Chunks of 2 .. 16 frames: 1 = one
+    CTA per (stream, head) (default, also for 17 frames); 0 / 2 / 3 = tensor cores, one warp per head, with 2 / 4 / 1
+    heads of 64 per CTA; 4 = the persistent TMA pipeline (2 .. 8 frames, head_dim 64). Calls a selection does not fit
+    fall back to one CTA per (stream, head)."""
     frame, chunk = request.param
     prev_f = q3.set_ring_frame_kernel(frame)
     prev_c = q3.set_ring_chunk_kernel(chunk)
@@ -76,6 +77,35 @@ def test_ring_attention_matches_oracle(q3, hd, H, n):
         for j in range(n):
             K2[rows[b], (pos[b] + j) % RING, li] = k[b, j]
             V2[rows[b], (pos[b] + j) % RING, li] = v[b, j]
+    assert bits_equal(Kg, K2) and bits_equal(Vg, V2)
+
+
+@pytest.mark.parametrize("n", [1, 4])
+def test_ring_attention_far_positions(q3, n):
+    """Positions far past 2^31 (a stream's frame counter is int64): the slot arithmetic stays exact."""
+    hd, H = 64, 8
+    g = synth.cpu_gen(900 + n)
+    pos = torch.tensor([2**31 - 2, 2**31 - 1, 2**31, 2**31 + 87, 2**32 + 5, 2**40 + 13, 2**62 + 71, 2**63 - 64],
+                       dtype=torch.int64)
+    B, S = len(pos), 10
+    rows = torch.randperm(S, generator=g)[:B]
+    K = synth.randn((S, RING, H, hd), g, 1.0, torch.float16)
+    V = synth.randn((S, RING, H, hd), g, 1.0, torch.float16)
+    q = synth.randn((B, n, H, hd), g, 1.0, torch.float16)
+    k = synth.randn((B, n, H, hd), g, 1.0, torch.float16)
+    v = synth.randn((B, n, H, hd), g, 1.0, torch.float16)
+    Kg, Vg = K.to(DEV), V.to(DEV)
+    out = q3.ring_window_attn(q.to(DEV), k.to(DEV), v.to(DEV), Kg, Vg, rows.to(DEV), pos.to(DEV), PAST, hd ** -0.5,
+                              True)
+    torch.cuda.synchronize()
+    ref = OR.ring_attention(q, k, v, K[rows], V[rows], pos, PAST, hd ** -0.5, emulate_fp16=True)
+    err = (out.float().cpu() - ref).abs()
+    assert float(err.max()) <= 1e-2 + 2e-2 * float(ref.abs().max()), f"max err {float(err.max()):.3e}"
+    K2, V2 = K.clone(), V.clone()
+    for b in range(B):
+        for j in range(n):
+            K2[rows[b], (int(pos[b]) + j) % RING] = k[b, j]
+            V2[rows[b], (int(pos[b]) + j) % RING] = v[b, j]
     assert bits_equal(Kg, K2) and bits_equal(Vg, V2)
 
 
