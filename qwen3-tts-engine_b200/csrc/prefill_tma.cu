@@ -109,8 +109,6 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // This thread's bulk stores have finished reading shared memory (the slot may be refilled).
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-// This thread's bulk stores are complete.
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Number of new-key tiles the query tile q of a sequence visits (the key tiles past the prefix).
 __device__ __forceinline__ int new_tiles_of(const PfSeq& s, int q, int causal) {

@@ -48,6 +48,28 @@ constexpr int kRingThreads = 128;
 
 __device__ __forceinline__ float round_fp16(float x) { return __half2float(__float2half_rn(x)); }
 
+// (pos - 1) mod RING, non-negative, for every int64 position, RING >= 2: division by the launch-invariant RING as a
+// multiply-high by magic = ceil(2^(63 + l) / RING), l = ceil(log2 RING), and a shift by l - 1, exact for dividends up to
+// 2^63 (Granlund and Montgomery, "Division by invariant integers using multiplication", 1994). pos - 1 >= 0 is divided
+// as it is; below that, (pos - 1) mod RING = RING - 1 - ((-pos) mod RING).
+__device__ __forceinline__ int ring_pm1_mod(long long pos, int ring, unsigned long long magic, int shift) {
+  const unsigned long long up = static_cast<unsigned long long>(pos);
+  const bool ge1 = pos >= 1;
+  const unsigned long long z = ge1 ? up - 1ull : 0ull - up;  // pos - 1, or -pos: both in [0, 2^63]
+  const unsigned long long q = __umul64hi(z, magic) >> shift;
+  const int r = static_cast<int>(z - q * static_cast<unsigned long long>(ring));
+  return ge1 ? r : ring - 1 - r;
+}
+
+// (pos - 1) mod RING for any ring size (the staged kernels; ring_magic / ring_shift are set for RING >= 2)
+__device__ __forceinline__ int ring_pm1(long long pos, const RingArgs& a) {
+  return a.ring == 1 ? 0 : ring_pm1_mod(pos, a.ring, a.ring_magic, a.ring_shift);
+}
+
+// Slot of frame pos + f given (pos - 1) mod RING (0 <= f <= the largest chunk)
+__device__ __forceinline__ int ring_slot_after(int pm1_mod, int f, int ring) { return (pm1_mod + 1 + f) % ring; }
+
+
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                         uint32_t b1) {
   asm volatile(
@@ -102,8 +124,7 @@ __global__ void __launch_bounds__(kRingThreads, HD == 64 ? 9 : 4) ring_attn_mma_
   const long long pos = a.pos[b];
   // Distance d back from the newest frame (pos-1) lives in slot (pos-1-d) mod RING; query i sees it when
   // d <= min(pos-1, PAST-1-i) (decoder_stream.py:152-155), so rows d < nvis = min(pos, PAST, RING) cover every query.
-  const long long pm1 = pos - 1;
-  const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+  const int pm1_mod = ring_pm1(pos, a);
   int nvis = a.past < RING ? a.past : RING;
   if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
 
@@ -272,7 +293,7 @@ __global__ void __launch_bounds__(kRingThreads, HD == 64 ? 9 : 4) ring_attn_mma_
     __half* vw = a.v_ring + row * a.ring_stream_stride + hh * HD;
     for (int i = tid; i < n * CH; i += kRingThreads) {
       const int f = i / CH, c = i - f * CH;
-      const long long slot = (((pos + f) % RING) + RING) % RING;
+      const int slot = ring_slot_after(pm1_mod, f, RING);
       reinterpret_cast<uint4*>(kw + slot * a.ring_slot_stride)[c] =
           *reinterpret_cast<const uint4*>(swz<HD>(sK, G.RP + f, c));
       reinterpret_cast<uint4*>(vw + slot * a.ring_slot_stride)[c] =
@@ -306,8 +327,7 @@ __global__ void __launch_bounds__(kRingThreads) ring_attn_frame_kernel(const Rin
 
   const long long row = a.ring_rows[b];
   const long long pos = a.pos[b];
-  const long long pm1 = pos - 1;
-  const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+  const int pm1_mod = ring_pm1(pos, a);
   int nvis = NV;                                             // distance d lives in slot (pos-1-d) mod RING
   if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
   const int nk = nvis + 1;                                   // keys: nvis ring rows, then the frame itself
@@ -427,7 +447,7 @@ __global__ void __launch_bounds__(kRingThreads) ring_attn_frame_kernel(const Rin
 
   // ---- the frame's columns into the ring (a slot outside every window of this launch, never staged)
   if (a.write_new) {
-    const long long slot = ((pos % RING) + RING) % RING;
+    const int slot = ring_slot_after(pm1_mod, 0, RING);
     __half* kw = a.k_ring + row * a.ring_stream_stride + hh * HD + slot * a.ring_slot_stride;
     __half* vw = a.v_ring + row * a.ring_stream_stride + hh * HD + slot * a.ring_slot_stride;
     for (int i = tid; i < 2 * CH; i += kRingThreads) {
@@ -474,8 +494,7 @@ __global__ void __launch_bounds__(32 * G) ring_attn_frame_heads_kernel(const Rin
 
   const long long row = a.ring_rows[b];
   const long long pos = a.pos[b];
-  const long long pm1 = pos - 1;
-  const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+  const int pm1_mod = ring_pm1(pos, a);
   int nvis = NV;                                             // distance d lives in slot (pos-1-d) mod RING
   if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
   const int nk = nvis + 1;                                   // keys: nvis ring rows, then the frame itself
@@ -597,7 +616,7 @@ __global__ void __launch_bounds__(32 * G) ring_attn_frame_heads_kernel(const Rin
 
   // ---- the frame's columns into the ring (a slot outside every window of this launch, never staged)
   if (a.write_new) {
-    const long long slot = ((pos % RING) + RING) % RING;
+    const int slot = ring_slot_after(pm1_mod, 0, RING);
     const long long off = row * a.ring_stream_stride + slot * a.ring_slot_stride + (hg * G + w) * HD + d0;
     const __half* ks = sK + nvis * SM::kRowHalves + w * HD + d0;
 #pragma unroll
@@ -772,7 +791,7 @@ __device__ __forceinline__ void ring_frame_head_mma(const RingArgs& a, uint32_t 
   // ---- the frame's columns into the ring (a slot outside every window of this launch, never staged)
   if (a.write_new) {
     constexpr int DPL = HD / 32;
-    const long long slot = ((pos % RING) + RING) % RING;
+    const int slot = ring_slot_after(ring_pm1(pos, a), 0, RING);
     const long long off = row * a.ring_stream_stride + slot * a.ring_slot_stride + head * HD + lane * DPL;
     const __half* ks = reinterpret_cast<const __half*>(k_self) + lane * DPL;
     const __half* vs = reinterpret_cast<const __half*>(v_self) + lane * DPL;
@@ -800,8 +819,7 @@ __global__ void __launch_bounds__(32 * G) ring_attn_frame_mma_kernel(const RingA
 
   const long long row = a.ring_rows[b];
   const long long pos = a.pos[b];
-  const long long pm1 = pos - 1;
-  const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+  const int pm1_mod = ring_pm1(pos, a);
   int nvis = NV;                                             // distance d lives in slot (pos-1-d) mod RING
   if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
   const int nk = nvis + 1;                                   // keys: nvis ring rows, then the frame itself
@@ -1051,7 +1069,7 @@ __device__ __forceinline__ void ring_tma_quad_math(const RingArgs& a, uint32_t k
   }
   if (wq == 0 && ok && a.write_new) {
     const int RING = a.ring;
-    const long long slot = ((hd.pos % RING) + RING) % RING;
+    const int slot = ring_slot_after(hd.pm1, 0, RING);
     const long long off = hd.row * a.ring_stream_stride + slot * a.ring_slot_stride + hd.head * HD + lane * 2;
     *reinterpret_cast<__half2*>(a.k_ring + off) = *reinterpret_cast<const __half2*>(self + 128 + lane * 4);
     *reinterpret_cast<__half2*>(a.v_ring + off) = *reinterpret_cast<const __half2*>(self + 256 + lane * 4);
@@ -1248,7 +1266,7 @@ __device__ __forceinline__ void ring_tma_chunk_math(const RingArgs& a, uint32_t 
   // ---- the chunk's k / v into ring slots (pos + jj) % RING
   if (ok && a.write_new) {
     for (int jj = wq; jj < n; jj += 4) {
-      const long long slot = (((hd.pos + jj) % RING) + RING) % RING;
+      const int slot = ring_slot_after(hd.pm1, jj, RING);
       const long long off = hd.row * a.ring_stream_stride + slot * a.ring_slot_stride + hd.head * HD + lane * 2;
       *reinterpret_cast<__half2*>(a.k_ring + off) = *reinterpret_cast<const __half2*>(self + (NF + jj) * 128 + lane * 4);
       *reinterpret_cast<__half2*>(a.v_ring + off) =
@@ -1325,8 +1343,7 @@ __global__ void __launch_bounds__(32 * NQ * 5, MINB) ring_attn_frame_tma_kernel(
       if (*abort_flag) break;
       // visible slots: distances 0 .. nvis-1 back from slot pm1 = (pos - 1) mod RING, i.e. slots
       // [pm1 - nvis + 1, pm1], or [0, pm1] and [RING - (nvis - pm1 - 1), RING) when that wraps
-      const long long pm1 = pos - 1;
-      const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+      const int pm1_mod = ring_pm1(pos, a);
       int nvis = NV;
       if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
       const int s_lo = pm1_mod - nvis + 1;
@@ -1458,8 +1475,7 @@ __global__ void __launch_bounds__(32 * G) ring_attn_chunk_mma_kernel(const RingA
 
   const long long row = a.ring_rows[b];
   const long long pos = a.pos[b];
-  const long long pm1 = pos - 1;
-  const int pm1_mod = static_cast<int>(((pm1 % RING) + RING) % RING);
+  const int pm1_mod = ring_pm1(pos, a);
   int nvis = NV;                                             // distance d lives in slot (pos-1-d) mod RING
   if (pos < nvis) nvis = pos < 0 ? 0 : static_cast<int>(pos);
   const int nk = nvis + n;                                   // keys: nvis ring rows, then the chunk's n frames
@@ -1638,7 +1654,7 @@ __global__ void __launch_bounds__(32 * G) ring_attn_chunk_mma_kernel(const RingA
   if (a.write_new) {
     constexpr int DPL = HD / 32;
     for (int jj = 0; jj < n; ++jj) {
-      const long long slot = (((pos + jj) % RING) + RING) % RING;
+      const int slot = ring_slot_after(pm1_mod, jj, RING);
       const long long off = row * a.ring_stream_stride + slot * a.ring_slot_stride + (hg * G + w) * HD + lane * DPL;
       const __half* ks = reinterpret_cast<const __half*>(sK + (nvis + jj) * RS) + w * HD + lane * DPL;
       const __half* vs = reinterpret_cast<const __half*>(sV + (nvis + jj) * RS) + w * HD + lane * DPL;
@@ -1713,19 +1729,6 @@ __device__ __forceinline__ float dot8_h(const uint4 w, const float2 (&q)[4]) {
   a0 = __ffma2_rn(__half22float2(h[2]), q[2], a0);
   a1 = __ffma2_rn(__half22float2(h[3]), q[3], a1);
   return (a0.x + a0.y) + (a1.x + a1.y);
-}
-
-// (pos - 1) mod RING, non-negative, for every int64 position, RING >= 2: division by the launch-invariant RING as a
-// multiply-high by magic = ceil(2^(63 + l) / RING), l = ceil(log2 RING), and a shift by l - 1, exact for dividends up to
-// 2^63 (Granlund and Montgomery, "Division by invariant integers using multiplication", 1994). pos - 1 >= 0 is divided
-// as it is; below that, (pos - 1) mod RING = RING - 1 - ((-pos) mod RING).
-__device__ __forceinline__ int ring_pm1_mod(long long pos, int ring, unsigned long long magic, int shift) {
-  const unsigned long long up = static_cast<unsigned long long>(pos);
-  const bool ge1 = pos >= 1;
-  const unsigned long long z = ge1 ? up - 1ull : 0ull - up;  // pos - 1, or -pos: both in [0, 2^63]
-  const unsigned long long q = __umul64hi(z, magic) >> shift;
-  const int r = static_cast<int>(z - q * static_cast<unsigned long long>(ring));
-  return ge1 ? r : ring - 1 - r;
 }
 
 constexpr int kRingStreamWarps = 4;
@@ -1990,7 +1993,9 @@ static cudaError_t launch_chunk(dim3 grid, int nv, const RingArgs& a, cudaStream
   return cudaGetLastError();
 }
 
-cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
+cudaError_t launch_ring_attn(const RingArgs& args, cudaStream_t stream) {
+  RingArgs a = args;                                         // + the ring's reciprocal for the kernels' slot arithmetic
+  if (a.ring >= 2) ring_reciprocal(a.ring, &a.ring_magic, &a.ring_shift);
   // the shared-memory limits are raised once per device, for the largest ring and chunk supported, so a call made
   // during stream capture sets no attribute
   static thread_local int configured_device = -1;
@@ -2077,10 +2082,8 @@ cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream) {
   if (a.n == 1 && g_ring_frame_kernel == 6 && a.hd == 64 && a.ring >= 2 && nv + 1 <= kRingStreamMaxKeys &&
       static_cast<long long>(a.B) * a.H <= 2147483647ll) {
     // one frame, nothing staged: a CTA of four warps per (stream, head)
-    RingArgs s = a;
-    ring_reciprocal(a.ring, &s.ring_magic, &s.ring_shift);
     ring_attn_frame_stream_kernel<<<static_cast<unsigned>(static_cast<long long>(a.B) * a.H), 32 * kRingStreamWarps, 0,
-                                    stream>>>(s);
+                                    stream>>>(a);
     return cudaGetLastError();
   }
   if (a.n == 1 && (g_ring_frame_kernel == 2 || g_ring_frame_kernel == 6) && nv <= 95) {
