@@ -79,6 +79,12 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
 __device__ __forceinline__ void ldsm_x2_trans(const void* p, uint32_t& r0, uint32_t& r1) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_addr(p)));
 }
@@ -151,65 +157,40 @@ __global__ void __launch_bounds__(kRingThreads, HD == 64 ? 9 : 4) ring_attn_mma_
   cp_async_wait_all();
   __syncthreads();
 
-  // ---- S = Q.K^T: warp w takes key tiles w, w+4, ..., two at a time (independent accumulator chains); each score is
-  //      an fp16-rounded dot product (the reference's fp16 matmul), scaled and masked in fp32. Query rows >= n enter
-  //      the MMA as zeros; with n <= 16 (one query tile) the Q fragments are loaded once for all key tiles.
-  const int MT = (n + 15) / 16;
-  auto q_frag = [&](int q0, int ks, uint32_t (&f)[4]) {
-    f[0] = q0 < n ? *reinterpret_cast<const uint32_t*>(swz<HD>(sQ, q0, 2 * ks) + 2 * t) : 0u;
-    f[1] = q0 + 8 < n ? *reinterpret_cast<const uint32_t*>(swz<HD>(sQ, q0 + 8, 2 * ks) + 2 * t) : 0u;
-    f[2] = q0 < n ? *reinterpret_cast<const uint32_t*>(swz<HD>(sQ, q0, 2 * ks + 1) + 2 * t) : 0u;
-    f[3] = q0 + 8 < n ? *reinterpret_cast<const uint32_t*>(swz<HD>(sQ, q0 + 8, 2 * ks + 1) + 2 * t) : 0u;
-  };
-  auto store_scores = [&](const float (&acc)[4], int q0, int nt) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int i = q0 + (e >> 1) * 8;                       // query row of accumulator element e
-      const int c = nt * 8 + 2 * t + (e & 1);                // key column
-      if (i < n) {
-        const bool ok = c < G.RP ? (c < nvis && c <= a.past - 1 - i)   // ring row at distance c
-                                 : (c - G.RP <= i);                    // the chunk's own keys, causally
-        sS[i * G.KA + c] = ok ? round_fp16(acc[e]) * a.scale : -INFINITY;
-      }
-    }
-  };
-  const int NT = G.KA / 8;
+  // ---- S^T = K.Q^T on the tensor cores, keys as the 16-row A operand (one ldmatrix.x4 per 16 dims from the swizzled K
+  //      rows) and the chunk's queries as the 8-column B operand (loaded once per query tile): warp w takes key tiles
+  //      w, w+4, ... Each score is an fp16-rounded dot product (the reference's fp16 matmul), scaled and masked in fp32.
+  //      The last key tile may run up to 8 rows past KA (into V's first rows): those keys are never stored, and a
+  //      non-finite value there stays in its own accumulator element.
   constexpr int NW = kRingThreads / 32;
-  if (MT == 1) {
-    uint32_t qf[HD / 16][4];
+  const int QT = (n + 7) / 8;                                // query tiles of 8
+  const int KT = (G.KA + 15) / 16;                           // key tiles of 16
+  for (int qt = 0; qt < QT; ++qt) {
+    const int qi = qt * 8 + g;                               // the query whose B column this lane supplies
+    uint32_t qf[HD / 16][2];
 #pragma unroll
-    for (int ks = 0; ks < HD / 16; ++ks) q_frag(g, ks, qf[ks]);
-    for (int nt = warp; nt < NT; nt += 2 * NW) {
-      const int nt2 = nt + NW;                               // second tile of the pair (may be past the end)
-      const bool two = nt2 < NT;
-      const int k1 = nt * 8 + g, k2 = (two ? nt2 : nt) * 8 + g;
-      float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      qf[ks][0] = qi < n ? *reinterpret_cast<const uint32_t*>(swz<HD>(sQ, qi, 2 * ks) + 2 * t) : 0u;
+      qf[ks][1] = qi < n ? *reinterpret_cast<const uint32_t*>(swz<HD>(sQ, qi, 2 * ks + 1) + 2 * t) : 0u;
+    }
+    for (int kt = warp; kt < KT; kt += NW) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int arow = kt * 16 + (lane & 15);                // lanes 0-15: dims 16ks..+7, lanes 16-31: 16ks+8..+15
 #pragma unroll
       for (int ks = 0; ks < HD / 16; ++ks) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, k1, 2 * ks) + 2 * t);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, k1, 2 * ks + 1) + 2 * t);
-        const uint32_t c0 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, k2, 2 * ks) + 2 * t);
-        const uint32_t c1 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, k2, 2 * ks + 1) + 2 * t);
-        mma_f16(acc1, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b0, b1);
-        mma_f16(acc2, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], c0, c1);
+        uint32_t af[4];
+        ldsm_x4(smem_addr(swz<HD>(sK, arow, 2 * ks + (lane >> 4))), af);
+        mma_f16(acc, af[0], af[1], af[2], af[3], qf[ks][0], qf[ks][1]);
       }
-      store_scores(acc1, g, nt);
-      if (two) store_scores(acc2, g, nt2);
-    }
-  } else {
-    for (int nt = warp; nt < NT; nt += NW) {
-      const int key = nt * 8 + g;
-      for (int mt = 0; mt < MT; ++mt) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-          uint32_t qf[4];
-          q_frag(mt * 16 + g, ks, qf);
-          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, key, 2 * ks) + 2 * t);
-          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(swz<HD>(sK, key, 2 * ks + 1) + 2 * t);
-          mma_f16(acc, qf[0], qf[1], qf[2], qf[3], b0, b1);
+      for (int e = 0; e < 4; ++e) {
+        const int c = kt * 16 + g + (e >> 1) * 8;            // key (accumulator row)
+        const int i = qt * 8 + 2 * t + (e & 1);              // query (accumulator column)
+        if (i < n && c < G.KA) {
+          const bool ok = c < G.RP ? (c < nvis && c <= a.past - 1 - i)   // ring row at distance c
+                                   : (c - G.RP <= i);                    // the chunk's own keys, causally
+          sS[i * G.KA + c] = ok ? round_fp16(acc[e]) * a.scale : -INFINITY;
         }
-        store_scores(acc, mt * 16 + g, nt);
       }
     }
   }
@@ -245,6 +226,7 @@ __global__ void __launch_bounds__(kRingThreads, HD == 64 ? 9 : 4) ring_attn_mma_
   // ---- O = fp16(fp16(P_ring.V_ring) + fp16(P_new.V_new)): warp w takes dim tiles w, w+4, ... (HD / 32 of them), all
   //      in one pass over the 16-key steps so the P fragment of a step is loaded once
   constexpr int DT = HD / 8 / NW;                            // dim tiles per warp
+  const int MT = (n + 15) / 16;                              // query tiles of 16 rows
   const int vrow = lane & 15;                                // the ldmatrix row this lane supplies (lanes 0-15)
   for (int mt = 0; mt < MT; ++mt) {
     const int q0 = mt * 16 + g;
@@ -651,11 +633,6 @@ struct RingMmaSmem {
   __host__ __device__ static size_t bytes(int nk) { return bar_off(nk) + 16; }
 };
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
 
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
