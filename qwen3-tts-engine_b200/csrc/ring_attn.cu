@@ -28,11 +28,12 @@
 // each described where it is defined; and, one CTA per (stream, head) with 4 warps (used also for every call another
 // selection does not fit):
 //   * ring_attn_mma_kernel (2..17 frames, default): rows staged by 16-byte asynchronous copies; the two ring contractions run
-//     on the tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulation): S = Q.K^T over 8-key column tiles (the
-//     chunk's keys included) and O_ring = P_ring.V_ring over 16-key steps with V fragments by ldmatrix.trans (V rows
-//     past nvis zeroed, so a zero probability never meets stale data); O_new = P_new.V_new (n <= 17 keys) is a few
-//     scalar FMAs per output. Rows of K, V and Q are 16-byte chunks XOR-swizzled by (row & 7), which keeps every
-//     fragment load free of bank conflicts. About 23 KB of shared memory at 88 slots, head_dim 64: nine CTAs per SM.
+//     on the tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulation): S^T = K.Q^T over 16-key row tiles (the
+//     chunk's keys included; queries as the 8-column operand) and O_ring = P_ring.V_ring over 16-key steps with V
+//     fragments by ldmatrix.trans (V rows past nvis zeroed, so a zero probability never meets stale data);
+//     O_new = P_new.V_new (n <= 17 keys) is a few scalar FMAs per output. Rows of K, V and Q are 16-byte chunks
+//     XOR-swizzled by (row & 7), which keeps every fragment load free of bank conflicts. About 25 KB of shared memory
+//     at 88 slots, 4 frames, head_dim 64: eight CTAs per SM.
 //   * ring_attn_frame_kernel (one frame): rows staged by one bulk copy each, scalar math.
 #include "q3_common.cuh"
 #include "q3_kernels.h"
