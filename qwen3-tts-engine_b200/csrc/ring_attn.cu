@@ -29,8 +29,9 @@
 // selection does not fit):
 //   * ring_attn_mma_kernel (2..17 frames, default): rows staged by 16-byte asynchronous copies; the two ring contractions run
 //     on the tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulation): S^T = K.Q^T over 16-key row tiles (the
-//     chunk's keys included; queries as the 8-column operand) and O_ring = P_ring.V_ring over 16-key steps with V
-//     fragments by ldmatrix.trans (V rows past nvis zeroed, so a zero probability never meets stale data);
+//     chunk's keys included; queries as the 8-column operand) and O_ring^T = V_ring^T.P_ring^T over 16-key steps
+//     (16 dims as the A operand by ldmatrix.x4.trans; V rows past nvis zeroed, so a zero probability never meets stale
+//     data);
 //     O_new = P_new.V_new (n <= 17 keys) is a few scalar FMAs per output. Rows of K, V and Q are 16-byte chunks
 //     XOR-swizzled by (row & 7), which keeps every fragment load free of bank conflicts. About 25 KB of shared memory
 //     at 88 slots, 4 frames, head_dim 64: eight CTAs per SM.
@@ -82,6 +83,12 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
@@ -224,47 +231,39 @@ __global__ void __launch_bounds__(kRingThreads, HD == 64 ? 9 : 4) ring_attn_mma_
   }
   __syncthreads();
 
-  // ---- O = fp16(fp16(P_ring.V_ring) + fp16(P_new.V_new)): warp w takes dim tiles w, w+4, ... (HD / 32 of them), all
-  //      in one pass over the 16-key steps so the P fragment of a step is loaded once
-  constexpr int DT = HD / 8 / NW;                            // dim tiles per warp
-  const int MT = (n + 15) / 16;                              // query tiles of 16 rows
-  const int vrow = lane & 15;                                // the ldmatrix row this lane supplies (lanes 0-15)
-  for (int mt = 0; mt < MT; ++mt) {
-    const int q0 = mt * 16 + g;
-    float acc[DT][4];
+  // ---- O^T = V_ring^T.P_ring^T on the tensor cores: 16 dims as the A operand (ldmatrix.x4.trans of the V rows), the
+  //      queries as the 8-column B operand (two 32-bit loads of P per 16 keys); warp w takes 16-dim tiles w, w+4, ...
+  //      o = fp16(fp16(ring) + fp16(P_new.V_new)), the chunk's part a few scalar FMAs per output
+  constexpr int DT16 = HD / 16 / NW;                         // 16-dim tiles per warp
+  for (int qt = 0; qt < QT; ++qt) {
+    const int qi = qt * 8 + g;                               // the query whose B column this lane supplies
+    float acc[DT16][4];
 #pragma unroll
-    for (int u = 0; u < DT; ++u) acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
+    for (int u = 0; u < DT16; ++u) acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
+    const int lkey = (lane & 7) + ((lane >> 4) << 3), lch = (lane >> 3) & 1;   // this lane's ldmatrix row
     for (int ks = 0; ks < G.RP / 16; ++ks) {
-      const __half* pr = sPr + ks * 16 + 2 * t;
-      const uint32_t a0 = q0 < n ? *reinterpret_cast<const uint32_t*>(pr + q0 * G.LPR) : 0u;
-      const uint32_t a1 = q0 + 8 < n ? *reinterpret_cast<const uint32_t*>(pr + (q0 + 8) * G.LPR) : 0u;
-      const uint32_t a2 = q0 < n ? *reinterpret_cast<const uint32_t*>(pr + q0 * G.LPR + 8) : 0u;
-      const uint32_t a3 = q0 + 8 < n ? *reinterpret_cast<const uint32_t*>(pr + (q0 + 8) * G.LPR + 8) : 0u;
+      const __half* pr = sPr + qi * G.LPR + ks * 16 + 2 * t;
+      const uint32_t b0 = qi < n ? *reinterpret_cast<const uint32_t*>(pr) : 0u;
+      const uint32_t b1 = qi < n ? *reinterpret_cast<const uint32_t*>(pr + 8) : 0u;
 #pragma unroll
-      for (int u = 0; u < DT; ++u) {
-        uint32_t b0, b1;
-        ldsm_x2_trans(swz<HD>(sV, ks * 16 + vrow, warp + u * NW), b0, b1);
-        mma_f16(acc[u], a0, a1, a2, a3, b0, b1);
+      for (int u = 0; u < DT16; ++u) {
+        uint32_t af[4];
+        ldsm_x4_trans(smem_addr(swz<HD>(sV, ks * 16 + lkey, 2 * (warp + u * NW) + lch)), af);
+        mma_f16(acc[u], af[0], af[1], af[2], af[3], b0, b1);
       }
     }
 #pragma unroll
-    for (int u = 0; u < DT; ++u) {
-      const int dt = warp + u * NW;
+    for (int u = 0; u < DT16; ++u) {
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {                        // rows g and g + 8 of the tile
-        const int i = q0 + 8 * h2;
+      for (int e = 0; e < 4; ++e) {
+        const int d = 16 * (warp + u * NW) + g + (e >> 1) * 8;   // dim (accumulator row)
+        const int i = qt * 8 + 2 * t + (e & 1);                  // query (accumulator column)
         if (i < n) {
-          float n0 = 0.f, n1 = 0.f;                           // the chunk's keys jj <= i
-          for (int jj = 0; jj <= i; ++jj) {
-            const float p = sPn[i * n + jj];
-            const float2 v = __half22float2(*reinterpret_cast<const __half2*>(swz<HD>(sV, G.RP + jj, dt) + 2 * t));
-            n0 = fmaf(p, v.x, n0);
-            n1 = fmaf(p, v.y, n1);
-          }
-          const __half2 o = __floats2half2_rn(round_fp16(acc[u][2 * h2]) + round_fp16(n0),
-                                              round_fp16(acc[u][2 * h2 + 1]) + round_fp16(n1));
-          *reinterpret_cast<__half2*>(a.out + b * a.out_batch_stride + i * a.out_frame_stride + hh * HD + dt * 8 +
-                                      2 * t) = o;
+          float ns = 0.f;                                        // the chunk's keys jj <= i
+          for (int jj = 0; jj <= i; ++jj)
+            ns = fmaf(sPn[i * n + jj], __half2float(swz<HD>(sV, G.RP + jj, d >> 3)[d & 7]), ns);
+          a.out[b * a.out_batch_stride + i * a.out_frame_stride + hh * HD + d] =
+              __float2half_rn(round_fp16(acc[u][e]) + round_fp16(ns));
         }
       }
     }
@@ -635,11 +634,6 @@ struct RingMmaSmem {
 };
 
 
-__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
