@@ -43,6 +43,7 @@
 #include <cuda_fp16.h>
 
 #include <cstring>
+#include <type_traits>
 
 namespace q3 {
 
@@ -1671,12 +1672,12 @@ __device__ __forceinline__ uint32_t ld_nc_u1(const void* p) {
   return r;
 }
 
-// Sum the N per-lane values v (N a power of two, at most 8) over the 8 lanes of a lane group (xor offsets 4, 2, 1);
-// the result is the complete sum of value index c >> (3 - log2 N), c = lane & 7.
-template <int N>
-__device__ __forceinline__ float group8_transpose_sum(float (&v)[N], int c) {
-  static_assert(N >= 1 && N <= 8 && (N & (N - 1)) == 0, "N must be a power of two <= 8");
-  int off = 4;
+// Sum the N per-lane values v (N a power of two, at most LPR) over the LPR lanes of a lane group (xor offsets LPR / 2
+// .. 1; LPR 8 or 16); the result is the complete sum of value index c / (LPR / N), c = lane % LPR.
+template <int N, int LPR>
+__device__ __forceinline__ float group_transpose_sum(float (&v)[N], int c) {
+  static_assert(N >= 1 && N <= LPR && (N & (N - 1)) == 0 && (LPR == 8 || LPR == 16), "N a power of two <= LPR");
+  int off = LPR / 2;
 #pragma unroll
   for (int n = N; n > 1; n >>= 1, off >>= 1) {
     const bool up = (c & off) != 0;
@@ -1703,17 +1704,22 @@ __device__ __forceinline__ float dot8_h(const uint4 w, const float2 (&q)[4]) {
   return (a0.x + a0.y) + (a1.x + a1.y);
 }
 
-constexpr int kRingStreamWarps = 4;
+// Warps per (stream, head): head_dim 64 rows take 8 lanes (four rows per warp load), 128 take 16 (two rows), so 4 / 8
+// warps keep 5 rows per lane group either way.
+__host__ __device__ constexpr int ring_stream_warps(int hd) { return hd == 64 ? 4 : 8; }
 constexpr int kRingStreamRows = 5;                           // rows per lane group and warp: P + R = 4 + 1
-constexpr int kRingStreamMaxKeys = 4 * kRingStreamWarps * kRingStreamRows;   // ring rows + the frame's own key: 80
+constexpr int kRingStreamMaxKeys = 80;                       // ring rows + the frame's own key: (32 / LPR) W * 5
 
-__global__ void __launch_bounds__(32 * kRingStreamWarps) ring_attn_frame_stream_kernel(const RingArgs a) {
-  constexpr int HD = 64, W = kRingStreamWarps, P = 4, R = 1, RPL = P + R;
-  static_assert(RPL == kRingStreamRows, "row batches");
-  constexpr int SP = 8 / P, SR = 8 / R;                      // lanes holding one completed score of a batch
+template <int HD>
+__global__ void __launch_bounds__(32 * ring_stream_warps(HD)) ring_attn_frame_stream_kernel(const RingArgs a) {
+  constexpr int W = ring_stream_warps(HD), P = 4, R = 1, RPL = P + R;
+  constexpr int LPR = HD / 8, RG = 32 / LPR, DPL = 8 / RG;   // lanes per row, row groups per warp, output dims per lane
+  static_assert(RPL == kRingStreamRows && RG * W * RPL == kRingStreamMaxKeys, "row batches");
+  constexpr int SP = LPR / P, SR = LPR / R;                  // lanes holding one completed score of a batch
+  using SelfW = typename std::conditional<DPL == 2, uint32_t, uint2>::type;   // DPL halves of the frame's k / v
   __shared__ float2 s_ml[W];                                 // (max, sum of exp(s - max)) per warp
-  __shared__ float3 s_acc[W - 1][32];                        // warps 1 .. W-1: two output dims and p_self per lane
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, c = lane & 7;
+  __shared__ float s_acc[W - 1][DPL + 1][32];                // warps 1 .. W-1: DPL output dims and p_self per lane
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane / LPR, c = lane % LPR;
   const int b = static_cast<int>(blockIdx.x / a.H), head = static_cast<int>(blockIdx.x % a.H);   // grid = B * H
   const int RING = a.ring;
   const int NV = a.past < RING ? a.past : RING;              // ring rows any frame can see (launch-wide)
@@ -1728,17 +1734,22 @@ __global__ void __launch_bounds__(32 * kRingStreamWarps) ring_attn_frame_stream_
   //      value enters through p_self)
   const long long fo = b * a.qkv_batch_stride + head * HD;   // the frame's q / k / v row of this head
   const long long ro = row * a.ring_stream_stride + head * HD + c * 8;
-  const int d0 = 8 * c + 2 * g;                              // the two output dims of this lane
+  const int d0 = 8 * c + DPL * g;                            // the DPL output dims of this lane
   const uint4 qw = ld_stream_v4(a.q + fo + c * 8);
-  uint32_t vself_w = 0u, kself_w = 0u;
+  SelfW vself_w{}, kself_w{};
   if (w == 0) {
-    vself_w = ld_nc_u1(a.v_new + fo + d0);
-    if (a.write_new) kself_w = ld_nc_u1(a.k_new + fo + d0);
+    if constexpr (DPL == 2) {
+      vself_w = ld_nc_u1(a.v_new + fo + d0);
+      if (a.write_new) kself_w = ld_nc_u1(a.k_new + fo + d0);
+    } else {
+      vself_w = ld_nc_u2(a.v_new + fo + d0);
+      if (a.write_new) kself_w = ld_nc_u2(a.k_new + fo + d0);
+    }
   }
   uint4 kw[RPL], vw[RPL];
 #pragma unroll
   for (int i = 0; i < RPL; ++i) {
-    const int r = 4 * (W * i + w) + g;
+    const int r = RG * (W * i + w) + g;
     kw[i] = make_uint4(0u, 0u, 0u, 0u);
     if (r < nvis) {
       int j = pm1_mod - r;
@@ -1750,7 +1761,7 @@ __global__ void __launch_bounds__(32 * kRingStreamWarps) ring_attn_frame_stream_
   }
 #pragma unroll
   for (int i = 0; i < RPL; ++i) {
-    const int r = 4 * (W * i + w) + g;
+    const int r = RG * (W * i + w) + g;
     vw[i] = make_uint4(0u, 0u, 0u, 0u);
     if (r < nvis) {
       int j = pm1_mod - r;
@@ -1771,13 +1782,13 @@ __global__ void __launch_bounds__(32 * kRingStreamWarps) ring_attn_frame_stream_
     float part[P];
 #pragma unroll
     for (int i = 0; i < P; ++i) part[i] = dot8_h(kw[i], q2);
-    s[0] = group8_transpose_sum<P>(part, c);
+    s[0] = group_transpose_sum<P, LPR>(part, c);
     float rest[R];
 #pragma unroll
     for (int i = 0; i < R; ++i) rest[i] = dot8_h(kw[P + i], q2);
-    s[1] = group8_transpose_sum<R>(rest, c);
+    s[1] = group_transpose_sum<R, LPR>(rest, c);
   }
-  const int rr[2] = {4 * (W * (c / SP) + w) + g, 4 * (W * (P + c / SR) + w) + g};
+  const int rr[2] = {RG * (W * (c / SP) + w) + g, RG * (W * (P + c / SR) + w) + g};
   const bool first[2] = {(c % SP) == 0, (c % SR) == 0};      // the lane that counts a duplicated score once
   float mw = -INFINITY;
 #pragma unroll
@@ -1804,11 +1815,11 @@ __global__ void __launch_bounds__(32 * kRingStreamWarps) ring_attn_frame_stream_
   float p[2];
 #pragma unroll
   for (int u = 0; u < 2; ++u) p[u] = rr[u] < nk ? round_fp16(expf(s[u] - m) * inv) : 0.f;
-  // p_self, on the warp holding row nvis = 4 (W i_s + w_s) + g_s
-  const int qd = nvis >> 2, w_s = qd % W, i_s = qd / W, g_s = nvis & 3;
+  // p_self, on the warp holding row nvis = RG (W i_s + w_s) + g_s
+  const int qd = nvis / RG, w_s = qd % W, i_s = qd / W, g_s = nvis % RG;
   float pself = 0.f;
   if (w == w_s)
-    pself = __shfl_sync(0xffffffffu, i_s < P ? p[0] : p[1], 8 * g_s + (i_s < P ? i_s * SP : (i_s - P) * SR));
+    pself = __shfl_sync(0xffffffffu, i_s < P ? p[0] : p[1], LPR * g_s + (i_s < P ? i_s * SP : (i_s - P) * SR));
 
   // ---- P_ring.V_ring over this lane's rows (V of rows >= nvis is zero), then over the row groups and the warps
   float acc[8];
@@ -1816,8 +1827,8 @@ __global__ void __launch_bounds__(32 * kRingStreamWarps) ring_attn_frame_stream_
   for (int j = 0; j < 8; ++j) acc[j] = 0.f;
 #pragma unroll
   for (int i = 0; i < RPL; ++i) {
-    const float pi = i < P ? __shfl_sync(0xffffffffu, p[0], 8 * g + i * SP)
-                           : __shfl_sync(0xffffffffu, p[1], 8 * g + (i - P) * SR);
+    const float pi = i < P ? __shfl_sync(0xffffffffu, p[0], LPR * g + i * SP)
+                           : __shfl_sync(0xffffffffu, p[1], LPR * g + (i - P) * SR);
     const float2 pp = make_float2(pi, pi);
     const __half2* vh = reinterpret_cast<const __half2*>(&vw[i]);
 #pragma unroll
@@ -1828,8 +1839,9 @@ __global__ void __launch_bounds__(32 * kRingStreamWarps) ring_attn_frame_stream_
       acc[2 * j + 1] = t.y;
     }
   }
+  // transposing butterfly over the row groups (xor 16 .. LPR): lane (g, c) ends with dims 8c + DPL g .. + DPL - 1
 #pragma unroll
-  for (int n = 8, off = 16; n > 2; n >>= 1, off >>= 1) {
+  for (int n = 8, off = 16; off >= LPR; n >>= 1, off >>= 1) {
     const bool up = (lane & off) != 0;
 #pragma unroll
     for (int i = 0; i < n / 2; ++i) {
@@ -1838,26 +1850,36 @@ __global__ void __launch_bounds__(32 * kRingStreamWarps) ring_attn_frame_stream_
       acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
     }
   }
-  if (w > 0) s_acc[w > 0 ? w - 1 : 0][lane] = make_float3(acc[0], acc[1], pself);
+  if (w > 0) {
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) s_acc[w - 1][j][lane] = acc[j];
+    s_acc[w - 1][DPL][lane] = pself;
+  }
   __syncthreads();
   if (w > 0) return;
 #pragma unroll
-  for (int j = 0; j < W - 1; ++j) {
-    const float3 t = s_acc[j][lane];
-    acc[0] += t.x;
-    acc[1] += t.y;
-    pself += t.z;
+  for (int k = 0; k < W - 1; ++k) {
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) acc[j] += s_acc[k][j][lane];
+    pself += s_acc[k][DPL][lane];
   }
-  const float2 vs = __half22float2(*reinterpret_cast<const __half2*>(&vself_w));
-  __half* op = a.out + b * a.out_batch_stride + head * HD + d0;
-  *reinterpret_cast<__half2*>(op) = __floats2half2_rn(round_fp16(acc[0]) + round_fp16(pself * vs.x),
-                                                      round_fp16(acc[1]) + round_fp16(pself * vs.y));
+  const __half2* vsh = reinterpret_cast<const __half2*>(&vself_w);
+  __half2 ov[DPL / 2];
+#pragma unroll
+  for (int j = 0; j < DPL / 2; ++j) {
+    const float2 vs = __half22float2(vsh[j]);
+    ov[j] = __floats2half2_rn(round_fp16(acc[2 * j]) + round_fp16(pself * vs.x),
+                              round_fp16(acc[2 * j + 1]) + round_fp16(pself * vs.y));
+  }
+  __half2* op = reinterpret_cast<__half2*>(a.out + b * a.out_batch_stride + head * HD + d0);   // 4-byte aligned
+#pragma unroll
+  for (int j = 0; j < DPL / 2; ++j) op[j] = ov[j];
   // ---- the frame's columns into the ring (a slot outside every window of this launch, never loaded)
   if (a.write_new) {
     const int pos_mod = pm1_mod + 1 == RING ? 0 : pm1_mod + 1;
     const long long off = row * a.ring_stream_stride + pos_mod * a.ring_slot_stride + head * HD + d0;
-    *reinterpret_cast<uint32_t*>(a.k_ring + off) = kself_w;
-    *reinterpret_cast<uint32_t*>(a.v_ring + off) = vself_w;
+    *reinterpret_cast<SelfW*>(a.k_ring + off) = kself_w;
+    *reinterpret_cast<SelfW*>(a.v_ring + off) = vself_w;
   }
 }
 
@@ -2051,11 +2073,14 @@ cudaError_t launch_ring_attn(const RingArgs& args, cudaStream_t stream) {
       return launch_chunk<128, 1>(cgrid, nv, a, stream);
     }
   }
-  if (a.n == 1 && g_ring_frame_kernel == 6 && a.hd == 64 && a.ring >= 2 && nv + 1 <= kRingStreamMaxKeys &&
+  if (a.n == 1 && g_ring_frame_kernel == 6 && a.ring >= 2 && nv + 1 <= kRingStreamMaxKeys &&
       static_cast<long long>(a.B) * a.H <= 2147483647ll) {
-    // one frame, nothing staged: a CTA of four warps per (stream, head)
-    ring_attn_frame_stream_kernel<<<static_cast<unsigned>(static_cast<long long>(a.B) * a.H), 32 * kRingStreamWarps, 0,
-                                    stream>>>(a);
+    // one frame, nothing staged: a CTA of 4 (head_dim 64) or 8 (128) warps per (stream, head)
+    const unsigned items = static_cast<unsigned>(static_cast<long long>(a.B) * a.H);
+    if (a.hd == 64)
+      ring_attn_frame_stream_kernel<64><<<items, 32 * ring_stream_warps(64), 0, stream>>>(a);
+    else
+      ring_attn_frame_stream_kernel<128><<<items, 32 * ring_stream_warps(128), 0, stream>>>(a);
     return cudaGetLastError();
   }
   if (a.n == 1 && (g_ring_frame_kernel == 2 || g_ring_frame_kernel == 6) && nv <= 95) {
