@@ -226,10 +226,10 @@ int q3_qk_norm_rope_rows(void* qkv, int64_t qkv_row_stride, const q3_qk_norm_rop
  * reference's fp16 rounding points (scores, P and each P.V half rounded to fp16). write_new != 0 also stores the
  * chunk's K/V into ring slots (pos + j) % ring (the caller's index_copy_, decoder_stream.py:330-333).
  * head_dim 64 or 128, ring <= 128, n <= min(17, ring - past). out: [B, n, heads * head_dim] fp16. */
-/* One-frame ring kernel used by q3_ring_window_attn for n == 1: 6 = nothing staged, four warps per (stream, head)
- * loading their rows straight into registers (head_dim 64, ring >= 2, past <= 79; the default, the fastest measured);
- * 2 = scalar math, one warp per head, G heads per CTA (4 for head_dim 64, 2 for 128; also every head_dim 128 call
- * under the default); 1 = scalar math, one CTA per (stream, head); 0 = tensor cores, one warp per head, G = 4 / 2,
+/* One-frame ring kernel used by q3_ring_window_attn for n == 1: 6 = nothing staged, 4 (head_dim 64) or 8 (128) warps
+ * per (stream, head) loading their rows straight into registers (ring >= 2, past <= 79; the default, the fastest
+ * measured); 2 = scalar math, one warp per head, G heads per CTA (4 for head_dim 64, 2 for 128; also the calls with
+ * wider windows under the default); 1 = scalar math, one CTA per (stream, head); 0 = tensor cores, one warp per head, G = 4 / 2,
  * 3 = G = 2 / 1, 4 = G = 1 (past < 96); 5 = a persistent TMA pipeline, quads of four warps per (stream, head) fed by
  * producer warps (head_dim 64, past <= 97). Calls a selection does not fit (G not dividing the head count, sizes) run
  * kernel 1. Other values leave the selection unchanged.

@@ -210,8 +210,8 @@ struct RingArgs {
 };
 size_t ring_smem_bytes(int ring, int past, int hd, int n);
 cudaError_t launch_ring_attn(const RingArgs& a, cudaStream_t stream);
-// Which one-frame ring kernel launch_ring_attn uses: 6 = nothing staged, four warps per (stream, head) loading straight
-// into registers (default; head_dim 128 and wider windows go to 2); 2 = scalar math, one warp per head, 4 x 64 / 2 x 128
+// Which one-frame ring kernel launch_ring_attn uses: 6 = nothing staged, 4 / 8 warps per (stream, head) of 64 / 128
+// dims loading straight into registers (default; windows past 79 rows go to 2); 2 = scalar math, one warp per head, 4 x 64 / 2 x 128
 // heads per CTA; 1 = scalar math, one CTA per (stream, head) (also every call another selection does not fit);
 // 0 / 3 / 4 = tensor cores, one warp per head, 4 / 2 / 1 heads of 64 per CTA; 5 = the persistent TMA pipeline.
 extern int g_ring_frame_kernel;

@@ -17,9 +17,9 @@
 // by the chunk's rows (the TMA pipeline in slot order). Ring rows no query sees are never used. The kernels
 // (launch_ring_attn picks one by chunk size and the q3_set_ring_frame_kernel / q3_set_ring_chunk_kernel selections;
 // the defaults are the fastest measured):
-//   * ring_attn_frame_stream_kernel (one frame, head_dim 64, default): four warps per (stream, head), every row
-//     loaded straight into registers, nothing staged;
-//   * ring_attn_frame_heads_kernel (one frame; head_dim 128 under the default): one warp per head, G heads per CTA,
+//   * ring_attn_frame_stream_kernel (one frame, default): 4 (head_dim 64) or 8 (128) warps per (stream, head), every
+//     row loaded straight into registers, nothing staged;
+//   * ring_attn_frame_heads_kernel (one frame; windows past 79 rows under the default): one warp per head, G heads per CTA,
 //     each staged row (the G heads of one slot) by one bulk copy into shared memory, scalar math;
 //   * ring_attn_frame_mma_kernel (one frame) and ring_attn_chunk_mma_kernel (2..16 frames): the same staging into rows
 //     padded by 16 bytes, both contractions on the tensor cores with P handed from the score fragments to the P.V
@@ -1641,23 +1641,24 @@ __global__ void __launch_bounds__(32 * G) ring_attn_chunk_mma_kernel(const RingA
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
-// One query frame with nothing staged (selection 6, head_dim 64): each (stream, head) is one CTA of W = 4 warps, and
-// every K and V row the frame sees goes straight from HBM into registers, all loads issued before the first is used.
-// Warp w holds key rows r = 4 (W i + w) + g, i < P + R (distance order; the frame's own key is row nvis), lane
-// l = 8 g + c the 16-byte piece c (dims 8c .. 8c+7) of them: one load instruction of a warp reads four whole 128-byte
-// rows, and a lane keeps (P + R) x 2 pieces in flight.
-//   scores   per-lane partial dot products over 8 dims (fp32), completed over the 8 lanes of a row group by a
+// One query frame with nothing staged (selection 6): each (stream, head) is one CTA of W warps (4 for head_dim 64, 8
+// for 128), and every K and V row the frame sees goes straight from HBM into registers, all loads issued before the
+// first is used. A row takes LPR = head_dim / 8 lanes (16 bytes each), so a warp load reads RG = 32 / LPR whole rows
+// (four of 128 bytes or two of 256). Warp w holds key rows r = RG (W i + w) + g, i < P + R (distance order; the
+// frame's own key is row nvis), lane l = LPR g + c the piece c (dims 8c .. 8c+7) of them; a lane keeps (P + R) x 2
+// pieces in flight.
+//   scores   per-lane partial dot products over 8 dims (fp32), completed over the LPR lanes of a row group by a
 //            transposing butterfly in a batch of P rows and one of R (afterwards lane c holds the score of batch index
-//            c / (8 / P), resp. P + c / (8 / R)); fp16-rounded, scaled in fp32 (decoder_stream.py:172);
+//            c / (LPR / P), resp. P + c / (LPR / R)); fp16-rounded, scaled in fp32 (decoder_stream.py:172);
 //   softmax  each warp's (max, sum of exp) pair meets the others' in shared memory, so every warp normalises with the
 //            whole row's max and sum before P is rounded to fp16 (:173);
-//   P.V      each lane takes its rows' probabilities by shuffles and accumulates its 8 dims; the four row groups meet by
-//            a second transposing butterfly (lane (g, c) ends with dims 8c + 2g, 8c + 2g + 1), warps 1 .. W-1 hand
-//            their partial sums (and p_self) to warp 0 through shared memory; o = fp16(fp16(ring) + fp16(p_self
+//   P.V      each lane takes its rows' probabilities by shuffles and accumulates its 8 dims; the RG row groups meet by
+//            a second transposing butterfly (lane (g, c) ends with the DPL = 8 / RG dims 8c + DPL g ..), warps 1 .. W-1
+//            hand their partial sums (and p_self) to warp 0 through shared memory; o = fp16(fp16(ring) + fp16(p_self
 //            v_self)) (:174).
-// Measured against one warp per (stream, head) (18 rows per lane group, 168 registers), 2, 6 and 8 warps per item, and
-// a resident grid walking the items: four warps per item, one item per CTA, at nine CTAs per SM gave the shortest
-// layer (the number of items in flight per SM is what counts).
+// Measured at head_dim 64 against one warp per (stream, head) (18 rows per lane group, 168 registers), 2, 6 and 8
+// warps per item, and a resident grid walking the items: four warps per item, one item per CTA, at nine CTAs per SM
+// gave the shortest layer (the number of items in flight per SM is what counts).
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
   uint4 r;
   asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"

@@ -622,8 +622,8 @@ def _(q, k, v, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, prefi
 
 
 def set_ring_frame_kernel(kernel: int) -> int:
-    """Select the one-frame ring attention kernel. 6 (default): nothing staged, four warps per (stream, head) loading
-    their rows straight into registers (head_dim 64, past <= 79; other calls run 2); 2: scalar math, one warp per head,
+    """Select the one-frame ring attention kernel. 6 (default): nothing staged, 4 (head_dim 64) or 8 (128) warps per
+    (stream, head) loading their rows straight into registers (past <= 79; other calls run 2); 2: scalar math, one warp per head,
     4 x 64 or 2 x 128 heads per CTA; 1: scalar math, one CTA per (stream, head); 0 / 3 / 4: tensor cores, one warp per
     head, 4 / 2 / 1 heads of 64 (2 / 1 / 1 of 128) per CTA; 5: persistent TMA pipeline, quads of four warps per
     (stream, head) fed by producer warps (head_dim 64). Calls a selection does not fit run 1. Returns the previous

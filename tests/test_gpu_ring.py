@@ -38,7 +38,7 @@ RING_KERNELS = [(6, 1), (2, 1), (1, 1), (0, 0), (3, 2), (4, 3), (5, 4)]
                 ids=["default", "heads", "cta_per_head", "mma_heads", "mma_narrow", "mma_one", "tma_pipe"])
 def ring_kernels(q3, request):
     """Every test runs on each kernel selection (one-frame kernel, multi-frame kernel). One frame: 6 = nothing staged,
-    four warps per (stream, head) loading straight into registers (default; head_dim 128 runs 2); 2 = scalar math, one
+    4 / 8 warps per (stream, head) of 64 / 128 dims loading straight into registers (default); 2 = scalar math, one
     warp per head, 4 x 64 / 2 x 128 heads per CTA; 1 = one CTA per (stream, head); 0 / 3 / 4 = tensor cores with
     4 / 2 / 1 heads of 64 per CTA; 5 = the persistent TMA pipeline (head_dim 64). Chunks of 2 .. 16 frames: 1 = one
     CTA per (stream, head) (default, also for 17 frames); 0 / 2 / 3 = tensor cores, one warp per head, with 2 / 4 / 1
