@@ -284,3 +284,25 @@ def test_noalloc_checks_every_argument_before_touching_cuda_or_its_scratch():
     assert call(kn=16) == _lib.Q3_ERR_INVALID                                   # k without v
     assert call(kn=16, vn=16, kvs=512) == _lib.Q3_ERR_ALIGNMENT                 # new rows shorter than 8 x 128
     assert call(B=0) == _lib.Q3_OK                                              # an empty batch does nothing at all
+
+
+@pytest.mark.parametrize("name,valid,default", [("q3_set_ring_frame_kernel", range(0, 7), 6),
+                                                ("q3_set_ring_chunk_kernel", range(0, 5), 1),
+                                                ("q3_set_decode_variant", range(0, 6), 5),
+                                                ("q3_set_prefill_kernel", range(0, 2), 0)])
+def test_kernel_selectors_take_known_values_and_return_the_previous_one(name, valid, default):
+    """The selectors are process-wide settings with no CUDA call: each returns the previous selection, takes every
+    value it knows and leaves the selection unchanged for any other."""
+    fn = getattr(_lib.load(), name)
+    start = fn(default)                     # whatever an earlier test left, back to the default
+    try:
+        assert fn(default) == default
+        for v in valid:
+            fn(v)
+            assert fn(v) == v
+        last = valid[-1]
+        for bad in (-1, valid[-1] + 1, 1000):
+            assert fn(bad) == last          # refused: the selection stays
+        assert fn(default) == last
+    finally:
+        fn(start)
